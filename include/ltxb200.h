@@ -1,0 +1,194 @@
+/*
+ * ltxb200.h - C ABI of libltxb200.so, the B200 (sm_100a) kernels behind the LTX-2.5 DiT
+ * denoising step.
+ *
+ * Conventions
+ *  - Every pointer argument is a device pointer owned by the caller; the library never
+ *    allocates device memory on these paths.
+ *  - `stream` is a cudaStream_t passed as void*; every call is asynchronous on it and
+ *    performs no device synchronisation.
+ *  - Every entry point returns LTX_OK (0) or an ltx_status error code; ltx_last_error()
+ *    returns a message for the calling thread's last failure. Nothing throws or exits.
+ *  - `dtype` selects the storage type of activations: LTX_F32 (the accuracy mode) or
+ *    LTX_BF16. Arithmetic is fp32 in both; bf16 results are rounded to nearest-even.
+ *  - Row-major matrices are described by (pointer, leading dimension in elements).
+ *  - "rows_per_batch" maps a flattened row index r to its sample b = r / rows_per_batch
+ *    (the reference's (B, T, D) activations flattened to (B*T, D)).
+ *
+ * Reference interface each entry replaces is cited as lipaul/ltx-nv file:line.
+ */
+#ifndef LTXB200_H
+#define LTXB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  LTX_OK = 0,
+  LTX_ERR_INVALID = 1,     /* bad argument: null pointer, size, alignment, stride */
+  LTX_ERR_CUDA = 2,        /* a CUDA runtime / driver call failed */
+  LTX_ERR_UNSUPPORTED = 3, /* valid request this build does not implement */
+  LTX_ERR_DEVICE = 4       /* a kernel reported an error through the device error word */
+} ltx_status;
+
+typedef enum { LTX_F32 = 0, LTX_BF16 = 1 } ltx_dtype;
+
+/* Message for the calling thread's last failed call ("" if none). */
+const char* ltx_last_error(void);
+/* ABI version of this library (bumped on any signature change). */
+int ltx_abi_version(void);
+/* Read (and clear when `clear` != 0) the device error word that bounded waits set when
+ * they give up (1 = mbarrier wait timed out). Synchronises `stream`. */
+int ltx_device_error_flags(int* flags, int clear, void* stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Initial noise: torch-compatible Philox4x32-10 normal fill.                          */
+/* Replaces cuda_c_standalone/common/philox.cu:19-45 (randn_kernel / randn_dispatch),  */
+/* the engine behind torch.randn(generator=cuda) in standalone/ltx_dit.py:502,513.     */
+/* ---------------------------------------------------------------------------------- */
+
+/* Grid that torch's launch policy picks for `n` elements on `device`
+ * (philox.cu:6-17: min(ceil(n/256), SMs * maxThreadsPerSM / 256)). */
+int ltx_philox_grid(int device, int64_t n, int* grid);
+/* Generator offset advance for one fill of `n` elements at `grid` blocks of 256
+ * threads (philox.cu:16): ((n-1)/(256*grid*4)+1)*4. */
+int64_t ltx_philox_offset_increment(int64_t n, int grid);
+/* out[i] = N(0,1) sample i of the stream (seed, offset) laid out exactly as torch's
+ * grid-stride kernel with `grid` blocks writes it (philox.cu:24-33). dtype F32/BF16. */
+int ltx_philox_randn(void* out, int64_t n, int dtype, uint64_t seed, uint64_t offset, int grid, void* stream);
+/* Raw Philox4x32-10 words: for thread t < threads and round r < rounds, writes the four
+ * 32-bit outputs of counter (offset/4 + r, subsequence t) under key `seed` to
+ * out[(r*threads + t)*4 + 0..3]. Test hook for the CPU restatement of the cipher. */
+int ltx_philox_raw(uint32_t* out, int64_t threads, int64_t rounds, uint64_t seed, uint64_t offset, void* stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Fused normalisation + adaLN modulation.                                             */
+/* Replaces rms_norm (standalone/ltx_nn.py:18) + get_ada_values (ltx_dit.py:192-198)   */
+/* + "norm(x) * (1 + scale) + shift" (ltx_dit.py:261,273,290,311,314) and the output   */
+/* head LayerNorm + modulation (ltx_dit.py:371-377).                                   */
+/* ---------------------------------------------------------------------------------- */
+/* LTX_NORM_NONE skips the normalisation: y = x * (1 + scale) + shift (the cross-adaLN
+ * text-context modulation, ltx_dit.py:246). */
+typedef enum { LTX_NORM_RMS = 0, LTX_NORM_LAYER = 1, LTX_NORM_NONE = 2 } ltx_norm_kind;
+
+/* Per-sample (or per-token) modulation vector v = table[toff + c] + mod[b*ld_b + t*ld_t
+ * + moff + c], rounded to the storage dtype the way the reference's bf16 add rounds. A
+ * NULL table or mod drops that term; off < 0 disables the vector. */
+typedef struct {
+  const void* table;   /* (n, D) adaLN scale-shift table, or NULL */
+  const void* mod;     /* (B, T?, n*D) timestep modulation, or NULL */
+  int64_t mod_ld_batch; /* elements between samples in `mod` */
+  int64_t mod_ld_tok;   /* elements between tokens in `mod` (0: per-sample) */
+  int64_t shift_table_off, shift_mod_off; /* element offsets of the shift vector */
+  int64_t scale_table_off, scale_mod_off; /* element offsets of the scale vector */
+  int has_shift, has_scale;
+} ltx_modulation;
+
+/* y[r, :] = norm(x[r, :]) * (1 + scale_b) + shift_b over `rows` rows of width D. */
+int ltx_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int64_t rows_per_batch,
+                      int D, int norm_kind, float eps, const ltx_modulation* mod, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* q/k RMSNorm (learned weight, over the whole inner dim) + split RoPE, in place.      */
+/* Replaces Attention.q_norm/k_norm (ltx_nn.py:186-187,214-215) and                    */
+/* apply_split_rotary_emb (ltx_nn.py:99-115).                                          */
+/* cos/sin: (rows_per_batch, heads*head_dim/2) tables, token stride ld_rope, sample    */
+/* stride rope_ld_batch (0 when all samples share positions). NULL cos: no RoPE;       */
+/* NULL weight: no normalisation (rotation only, apply_split_rotary_emb).              */
+/* ---------------------------------------------------------------------------------- */
+int ltx_qk_norm_rope(void* x, int64_t ldx, int64_t rows, int64_t rows_per_batch, int heads, int head_dim,
+                     const void* weight, float eps, const void* cos_tab, const void* sin_tab, int64_t ld_rope,
+                     int64_t rope_ld_batch, int dtype, void* stream);
+
+/* RoPE tables from token positions (precompute_freqs_cis, ltx_nn.py:63-96): `bounds`
+ * (n_axes, T, 2) fp32 [start, end) positions of one sample (the reference's
+ * positions[b]), `freqs` (F) fp32 frequency grid (computed in float64 by the caller,
+ * ltx_nn.py:34-46), max_pos per axis; writes cos/sin (T, dim/2) in `dtype` with the
+ * front padding of ltx_nn.py:88-92. */
+int ltx_rope_tables(const float* bounds, int n_axes, int64_t T, const float* freqs, int n_freq,
+                    const float* max_pos, int dim, void* cos_out, void* sin_out, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Element-wise kernels (FeedForward GELU ltx_nn.py:248, residual gate                */
+/* ltx_dit.py:265,311, timestep sinusoid standalone/common.py:138-148).                */
+/* ---------------------------------------------------------------------------------- */
+int ltx_gelu_tanh(const void* x, void* y, int64_t n, int dtype, void* stream);
+/* out[r, :] = x[r, :] + y[r, :] * gate_b, gate from `mod` (shift fields unused; the gate
+ * vector is described by scale_* fields). NULL mod: gate = 1. */
+int ltx_gate_residual(const void* x, int64_t ldx, const void* y, int64_t ldy, void* out, int64_t ldo,
+                      int64_t rows, int64_t rows_per_batch, int D, const ltx_modulation* gate, int dtype,
+                      void* stream);
+/* out[i, :] = [cos(t_i*scale*f_j), sin(t_i*scale*f_j)], f_j = exp(-ln(max_period) j/half). */
+int ltx_timestep_embedding(const float* t, int64_t n, float scale, int dim, float max_period, void* out, int dtype,
+                           void* stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Linear layers: C = epilogue(A * W^T + bias) with A (M, K) and W (N, K) K-major.     */
+/* Replaces every nn.Linear on the path (ltx_nn.py:126-158,188-192,244-245,            */
+/* ltx_dit.py:331-347) and cuda_c_standalone/common/gemm.cu:36-73 (linear()).          */
+/* bf16: TMA-fed tcgen05/TMEM kernel (M >= 32) or a weight-streaming kernel (M < 32);  */
+/* fp32: CUDA-core kernel.                                                             */
+/* ---------------------------------------------------------------------------------- */
+typedef enum {
+  LTX_EPI_NONE = 0,          /* C = acc (+ bias) */
+  LTX_EPI_GELU_TANH = 1,     /* C = gelu_tanh(acc + bias) */
+  LTX_EPI_SILU = 2,          /* C = silu(acc + bias) */
+  LTX_EPI_GATE_RESIDUAL = 3, /* C = residual + round(acc + bias) * gate_b */
+  LTX_EPI_ROW_MASK_ADD = 4   /* C = round(acc + bias) + (row_mask[r] > 0) * row_vec */
+} ltx_epilogue_kind;
+
+typedef struct {
+  int kind;
+  const void* bias;         /* (N,) or NULL */
+  const void* residual;     /* GATE_RESIDUAL: (M, N) with ld_residual; may alias C */
+  int64_t ld_residual;
+  ltx_modulation gate;      /* GATE_RESIDUAL: gate vector in the scale_* fields */
+  int64_t rows_per_batch;   /* row -> sample map for the gate */
+  const float* row_mask;    /* ROW_MASK_ADD: (M,) */
+  const void* row_vec;      /* ROW_MASK_ADD: (N,) */
+  int silu_input;           /* apply SiLU to A while loading it (weight-streaming path only) */
+} ltx_epilogue;
+
+int ltx_linear(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, int64_t ldc, int64_t M, int64_t N,
+               int64_t K, const ltx_epilogue* epi, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Attention: softmax(Q K^T * scale) V per (sample, head), non-causal, no mask, with   */
+/* the per-(token, head) output gate 2*sigmoid(logit) fused in.                        */
+/* Replaces sdpa (ltx_nn.py:22-26) + the gating of Attention.forward (ltx_nn.py:231-235)*/
+/* and cuda_c_standalone/common/gemm.cu:17-34 (the unfused QK^T / PV plan).            */
+/* Q rows of sample b start at q + b*Tq*ldq; head h occupies columns [h*d, (h+1)*d).    */
+/* gate_logits: (B*Tq, H) with ld_gate, or NULL for no gate.                           */
+/* bf16: tcgen05 FMHA (head_dim 64 or 128); fp32: CUDA-core kernel.                    */
+/* ---------------------------------------------------------------------------------- */
+int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
+                  int64_t ldo, int B, int64_t Tq, int64_t Tk, int heads, int head_dim, float scale,
+                  const void* gate_logits, int64_t ld_gate, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Denoise update: X0 conversion + CFG guidance + Euler step.                          */
+/* Replaces guided_denoise_step's X0 (ltx_dit.py:591-593), guide (ltx_dit.py:551-562,  */
+/* with rescale_scale = 0) and euler_step (ltx_dit.py:602-606).                        */
+/* ---------------------------------------------------------------------------------- */
+/* Element-wise form: vel (2, T, C) = model output for [cond, uncond] of one latent,
+ * latent/new_latent (T, C), timesteps (2, T) per-token sigma. Writes new_latent and
+ * (optionally) denoised (T, C). */
+int ltx_cfg_euler(const void* vel, const void* latent, const float* timesteps, int64_t T, int C, float cfg_scale,
+                  float sigma, float sigma_next, void* denoised, void* new_latent, int dtype, void* stream);
+
+/* Fused form: the output projection (proj_out, ltx_dit.py:378) of the head-modulated
+ * hidden state x (2*T, K) with weight W (C, K) and bias, followed in its epilogue by the
+ * same X0 + CFG + Euler update. vel_out (2, T, C) (optional) receives the projection. */
+int ltx_proj_out_cfg_euler(const void* x, int64_t ldx, const void* W, const void* bias, int64_t T, int C, int64_t K,
+                           const void* latent, const float* timesteps, float cfg_scale, float sigma,
+                           float sigma_next, void* vel_out, void* denoised, void* new_latent, int dtype,
+                           void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LTXB200_H */

@@ -1,0 +1,319 @@
+"""ctypes binding of libltxb200.so (the sm_100a kernels of the DiT step).
+
+PyTorch is used here only for device memory and streams: every wrapper takes torch
+tensors, passes their data pointers, sizes and the current CUDA stream through the C
+ABI declared in include/ltxb200.h, and raises LtxError when the library reports a
+failure. There is no CPU or PyTorch fallback: if the library is missing or a call is
+rejected, the error propagates.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libltxb200.so"
+
+LTX_F32, LTX_BF16 = 0, 1
+LTX_NORM_RMS, LTX_NORM_LAYER, LTX_NORM_NONE = 0, 1, 2
+EPI_NONE, EPI_GELU_TANH, EPI_SILU, EPI_GATE_RESIDUAL, EPI_ROW_MASK_ADD = 0, 1, 2, 3, 4
+
+c_i64 = ctypes.c_int64
+c_vp = ctypes.c_void_p
+
+
+class LtxError(RuntimeError):
+    """A libltxb200 call returned a non-zero status."""
+
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn} failed with status {code}: {msg}")
+        self.code = code
+
+
+class Modulation(ctypes.Structure):
+    """Mirror of ltx_modulation (include/ltxb200.h)."""
+
+    _fields_ = [
+        ("table", c_vp),
+        ("mod", c_vp),
+        ("mod_ld_batch", c_i64),
+        ("mod_ld_tok", c_i64),
+        ("shift_table_off", c_i64),
+        ("shift_mod_off", c_i64),
+        ("scale_table_off", c_i64),
+        ("scale_mod_off", c_i64),
+        ("has_shift", ctypes.c_int),
+        ("has_scale", ctypes.c_int),
+    ]
+
+
+class Epilogue(ctypes.Structure):
+    """Mirror of ltx_epilogue (include/ltxb200.h)."""
+
+    _fields_ = [
+        ("kind", ctypes.c_int),
+        ("bias", c_vp),
+        ("residual", c_vp),
+        ("ld_residual", c_i64),
+        ("gate", Modulation),
+        ("rows_per_batch", c_i64),
+        ("row_mask", c_vp),
+        ("row_vec", c_vp),
+        ("silu_input", ctypes.c_int),
+    ]
+
+
+# name -> (restype, argtypes); the exported symbols of include/ltxb200.h.
+_SIGNATURES = {
+    "ltx_last_error": (ctypes.c_char_p, []),
+    "ltx_abi_version": (ctypes.c_int, []),
+    "ltx_device_error_flags": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int, c_vp]),
+    "ltx_philox_grid": (ctypes.c_int, [ctypes.c_int, c_i64, ctypes.POINTER(ctypes.c_int)]),
+    "ltx_philox_offset_increment": (c_i64, [c_i64, ctypes.c_int]),
+    "ltx_philox_randn": (ctypes.c_int, [c_vp, c_i64, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, c_vp]),
+    "ltx_philox_raw": (ctypes.c_int, [c_vp, c_i64, c_i64, ctypes.c_uint64, ctypes.c_uint64, c_vp]),
+    "ltx_norm_modulate": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_float, ctypes.POINTER(Modulation), ctypes.c_int, c_vp]),
+    "ltx_qk_norm_rope": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i64, ctypes.c_int, ctypes.c_int, c_vp, ctypes.c_float,
+                                        c_vp, c_vp, c_i64, c_i64, ctypes.c_int, c_vp]),
+    "ltx_rope_tables": (ctypes.c_int, [c_vp, ctypes.c_int, c_i64, c_vp, ctypes.c_int, c_vp, ctypes.c_int, c_vp, c_vp,
+                                       ctypes.c_int, c_vp]),
+    "ltx_gelu_tanh": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_int, c_vp]),
+    "ltx_gate_residual": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, ctypes.c_int,
+                                         ctypes.POINTER(Modulation), ctypes.c_int, c_vp]),
+    "ltx_timestep_embedding": (ctypes.c_int, [c_vp, c_i64, ctypes.c_float, ctypes.c_int, ctypes.c_float, c_vp,
+                                              ctypes.c_int, c_vp]),
+    "ltx_linear": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                  ctypes.POINTER(Epilogue), ctypes.c_int, c_vp]),
+    "ltx_gemm_set_tile_n": (ctypes.c_int, [ctypes.c_int]),
+    "ltx_attention": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, ctypes.c_int, c_i64, c_i64,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, ctypes.c_int, c_vp]),
+    "ltx_cfg_euler": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                     ctypes.c_float, c_vp, c_vp, ctypes.c_int, c_vp]),
+    "ltx_proj_out_cfg_euler": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, ctypes.c_int, c_i64, c_vp, c_vp,
+                                              ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp,
+                                              ctypes.c_int, c_vp]),
+}
+
+_lib = None
+
+
+def load_library(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load libltxb200.so (once) and bind every exported entry point's signature."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise FileNotFoundError(
+            f"{p} not found: build it with `python -c 'import __graft_entry__ as g; g.build()'` "
+            "(there is no fallback implementation)")
+    lib = ctypes.CDLL(str(p))
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _check(name: str, status: int) -> None:
+    if status != 0:
+        msg = _lib.ltx_last_error().decode(errors="replace")
+        raise LtxError(name, status, msg)
+
+
+def _call(name: str, *args):
+    lib = load_library()
+    _check(name, getattr(lib, name)(*args))
+
+
+def _stream(t: torch.Tensor | None = None) -> int:
+    dev = t.device if t is not None else torch.device("cuda")
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return LTX_F32
+    if t.dtype == torch.bfloat16:
+        return LTX_BF16
+    raise TypeError(f"unsupported dtype {t.dtype}; the kernels take float32 or bfloat16")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("libltxb200 kernels take CUDA tensors only")
+    return t.data_ptr()
+
+
+def _ld(t: torch.Tensor) -> int:
+    """Leading dimension (elements between rows) of a row-major 2-D view."""
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"expected a 2-D row-major view, got shape {tuple(t.shape)} stride {t.stride()}")
+    return t.stride(0)
+
+
+# ---------------------------------------------------------------------------------------
+# Modulation descriptors
+# ---------------------------------------------------------------------------------------
+
+
+def modulation(table: torch.Tensor | None, mod: torch.Tensor | None, *, shift: tuple[int, int] | None,
+               scale: tuple[int, int] | None, mod_ld_batch: int = 0, mod_ld_tok: int = 0) -> Modulation:
+    """Describe shift/scale vectors table[t_off:] + mod[b, t, m_off:] (element offsets)."""
+    m = Modulation()
+    m.table = _ptr(table)
+    m.mod = _ptr(mod)
+    m.mod_ld_batch = mod_ld_batch
+    m.mod_ld_tok = mod_ld_tok
+    if shift is not None:
+        m.has_shift = 1
+        m.shift_table_off, m.shift_mod_off = shift
+    if scale is not None:
+        m.has_scale = 1
+        m.scale_table_off, m.scale_mod_off = scale
+    return m
+
+
+# ---------------------------------------------------------------------------------------
+# Wrappers
+# ---------------------------------------------------------------------------------------
+
+
+def abi_version() -> int:
+    return load_library().ltx_abi_version()
+
+
+def device_error_flags(clear: bool = True) -> int:
+    flags = ctypes.c_int(0)
+    _call("ltx_device_error_flags", ctypes.byref(flags), int(clear), _stream())
+    return flags.value
+
+
+def philox_grid(n: int, device: int | None = None) -> int:
+    g = ctypes.c_int(0)
+    dev = torch.cuda.current_device() if device is None else device
+    _call("ltx_philox_grid", dev, n, ctypes.byref(g))
+    return g.value
+
+
+def philox_offset_increment(n: int, grid: int) -> int:
+    return load_library().ltx_philox_offset_increment(n, grid)
+
+
+def philox_randn(out: torch.Tensor, seed: int, offset: int, grid: int) -> None:
+    if not out.is_contiguous():
+        raise ValueError("out must be contiguous")
+    _call("ltx_philox_randn", _ptr(out), out.numel(), _dt(out), seed, offset, grid, _stream(out))
+
+
+def philox_raw(out: torch.Tensor, threads: int, rounds: int, seed: int, offset: int) -> None:
+    if out.dtype != torch.int32 or out.numel() < threads * rounds * 4:
+        raise ValueError("out must be int32 with threads*rounds*4 elements")
+    _call("ltx_philox_raw", _ptr(out), threads, rounds, seed, offset, _stream(out))
+
+
+def norm_modulate(x: torch.Tensor, y: torch.Tensor, rows_per_batch: int, kind: int, eps: float,
+                  mod: Modulation | None) -> None:
+    rows, d = x.shape
+    _call("ltx_norm_modulate", _ptr(x), _ld(x), _ptr(y), _ld(y), rows, rows_per_batch, d, kind, eps,
+          ctypes.byref(mod) if mod is not None else None, _dt(x), _stream(x))
+
+
+def qk_norm_rope(x: torch.Tensor, rows_per_batch: int, heads: int, head_dim: int, weight: torch.Tensor, eps: float,
+                 cos: torch.Tensor | None, sin: torch.Tensor | None, rope_ld_batch: int = 0) -> None:
+    rows = x.shape[0]
+    ld_rope = _ld(cos) if cos is not None else 0
+    _call("ltx_qk_norm_rope", _ptr(x), _ld(x), rows, rows_per_batch, heads, head_dim, _ptr(weight), eps, _ptr(cos),
+          _ptr(sin), ld_rope, rope_ld_batch, _dt(x), _stream(x))
+
+
+def rope_tables(bounds: torch.Tensor, freqs: torch.Tensor, max_pos: torch.Tensor, dim: int, cos_out: torch.Tensor,
+                sin_out: torch.Tensor) -> None:
+    """bounds (n_axes, T, 2) fp32 contiguous positions of one sample -> cos/sin (T, dim/2)."""
+    n_axes, t, two = bounds.shape
+    if two != 2 or not bounds.is_contiguous() or bounds.dtype != torch.float32:
+        raise ValueError("bounds must be a contiguous float32 (n_axes, T, 2) tensor")
+    _call("ltx_rope_tables", _ptr(bounds), n_axes, t, _ptr(freqs), freqs.numel(), _ptr(max_pos), dim, _ptr(cos_out),
+          _ptr(sin_out), _dt(cos_out), _stream(bounds))
+
+
+def gelu_tanh(x: torch.Tensor, y: torch.Tensor) -> None:
+    _call("ltx_gelu_tanh", _ptr(x), _ptr(y), x.numel(), _dt(x), _stream(x))
+
+
+def gate_residual(x: torch.Tensor, y: torch.Tensor, out: torch.Tensor, rows_per_batch: int,
+                  gate: Modulation | None) -> None:
+    rows, d = x.shape
+    _call("ltx_gate_residual", _ptr(x), _ld(x), _ptr(y), _ld(y), _ptr(out), _ld(out), rows, rows_per_batch, d,
+          ctypes.byref(gate) if gate is not None else None, _dt(x), _stream(x))
+
+
+def timestep_embedding(t: torch.Tensor, scale: float, dim: int, max_period: float, out: torch.Tensor) -> None:
+    if t.dtype != torch.float32:
+        raise TypeError("timesteps must be float32")
+    _call("ltx_timestep_embedding", _ptr(t), t.numel(), scale, dim, max_period, _ptr(out), _dt(out), _stream(t))
+
+
+def epilogue(kind: int = EPI_NONE, bias: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+             gate: Modulation | None = None, rows_per_batch: int = 1, row_mask: torch.Tensor | None = None,
+             row_vec: torch.Tensor | None = None, silu_input: bool = False) -> Epilogue:
+    e = Epilogue()
+    e.kind = kind
+    e.bias = _ptr(bias)
+    if residual is not None:
+        e.residual = _ptr(residual)
+        e.ld_residual = _ld(residual)
+    if gate is not None:
+        e.gate = gate
+    e.rows_per_batch = rows_per_batch
+    e.row_mask = _ptr(row_mask)
+    e.row_vec = _ptr(row_vec)
+    e.silu_input = int(silu_input)
+    return e
+
+
+def linear(a: torch.Tensor, w: torch.Tensor, c: torch.Tensor, epi: Epilogue | None = None) -> None:
+    """c = epilogue(a @ w.T (+ bias)); a (M, K), w (N, K), c (M, N) row-major views."""
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k or c.shape[0] != m or c.shape[1] != n:
+        raise ValueError(f"shape mismatch a{tuple(a.shape)} w{tuple(w.shape)} c{tuple(c.shape)}")
+    _call("ltx_linear", _ptr(a), _ld(a), _ptr(w), _ld(w), _ptr(c), _ld(c), m, n, k,
+          ctypes.byref(epi) if epi is not None else None, _dt(a), _stream(a))
+
+
+def gemm_set_tile_n(bn: int) -> None:
+    _call("ltx_gemm_set_tile_n", bn)
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, batch: int, tq: int, tk: int,
+              heads: int, head_dim: int, scale: float, gate_logits: torch.Tensor | None = None) -> None:
+    """q (B*Tq, >=H*d), k/v (B*Tk, >=H*d), o (B*Tq, >=H*d) row-major views; gate (B*Tq, >=H)."""
+    _call("ltx_attention", _ptr(q), _ld(q), _ptr(k), _ld(k), _ptr(v), _ld(v), _ptr(o), _ld(o), batch, tq, tk, heads,
+          head_dim, scale, _ptr(gate_logits), _ld(gate_logits) if gate_logits is not None else 0, _dt(q), _stream(q))
+
+
+def cfg_euler(vel: torch.Tensor, latent: torch.Tensor, timesteps: torch.Tensor, cfg_scale: float, sigma: float,
+              sigma_next: float, new_latent: torch.Tensor, denoised: torch.Tensor | None = None) -> None:
+    t, c = latent.shape[-2], latent.shape[-1]
+    _call("ltx_cfg_euler", _ptr(vel), _ptr(latent), _ptr(timesteps), t, c, cfg_scale, sigma, sigma_next,
+          _ptr(denoised), _ptr(new_latent), _dt(latent), _stream(latent))
+
+
+def proj_out_cfg_euler(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, latent: torch.Tensor,
+                       timesteps: torch.Tensor, cfg_scale: float, sigma: float, sigma_next: float,
+                       new_latent: torch.Tensor, denoised: torch.Tensor | None = None,
+                       vel_out: torch.Tensor | None = None) -> None:
+    t, c = latent.shape[-2], latent.shape[-1]
+    _call("ltx_proj_out_cfg_euler", _ptr(x), _ld(x), _ptr(w), _ptr(bias), t, c, x.shape[1], _ptr(latent),
+          _ptr(timesteps), cfg_scale, sigma, sigma_next, _ptr(vel_out), _ptr(denoised), _ptr(new_latent), _dt(x),
+          _stream(x))

@@ -1,0 +1,87 @@
+// Library-wide C-ABI plumbing: error reporting, the device error word and TMA
+// descriptor encoding (through the driver entry point, so the library links only the
+// CUDA runtime).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <string>
+
+#include "ltx_common.cuh"
+#include "ltx_internal.h"
+
+namespace ltx {
+
+static thread_local std::string t_last_error;
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+void clear_error() { t_last_error.clear(); }
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+                              uint32_t box_outer) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+    throw ApiError{LTX_ERR_INVALID, "TMA operand must be 16-byte aligned"};
+  if ((ld * 2) % 16 != 0) throw ApiError{LTX_ERR_INVALID, "TMA row stride must be a multiple of 16 bytes"};
+  if (box_inner * 2 > 128 || box_outer > 256 || box_inner == 0 || box_outer == 0)
+    throw ApiError{LTX_ERR_INVALID, "TMA box out of range"};
+  auto fn = encode_fn();
+  if (fn == nullptr) throw ApiError{LTX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable"};
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw ApiError{LTX_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r))};
+  return m;
+}
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace ltx
+
+extern "C" const char* ltx_last_error(void) { return ltx::t_last_error.c_str(); }
+
+extern "C" int ltx_abi_version(void) { return 1; }
+
+extern "C" int ltx_device_error_flags(int* flags, int clear, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(flags != nullptr, "flags is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int value = 0;
+  LTX_CUDA(cudaMemcpyFromSymbolAsync(&value, g_ltx_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
+  LTX_CUDA(cudaStreamSynchronize(s));
+  *flags = value;
+  if (clear) {
+    const int zero = 0;
+    LTX_CUDA(cudaMemcpyToSymbolAsync(g_ltx_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
+    LTX_CUDA(cudaStreamSynchronize(s));
+  }
+  LTX_API_END
+}

@@ -1,0 +1,481 @@
+// Single-pass element-wise kernels of the DiT block: fused norm + adaLN modulation,
+// q/k RMSNorm + split RoPE, GELU-tanh, gated residual, timestep sinusoid, RoPE tables
+// and the X0 + CFG + Euler update.
+//
+// Each kernel reads its inputs once and writes its output once with 16-byte vector
+// accesses (8 bf16 / 2x4 fp32 per access); row reductions stay in registers + one
+// shared-memory exchange. Arithmetic is fp32; the storage dtype's rounding is applied
+// at the points where the reference's op-by-op PyTorch code rounds (each torch op on a
+// bf16 tensor returns a rounded bf16 tensor).
+#include "ltx_kernels.cuh"
+
+namespace ltx {
+namespace detail {
+
+constexpr int kMaxVecPerThread = 4;
+
+// ---------------------------------------------------------------------------------
+// y = norm(x) * (1 + scale) + shift          (ltx_dit.py:261,273,290,311,314,376-377)
+// ---------------------------------------------------------------------------------
+template <typename T, int NV>
+__global__ void __launch_bounds__(1024) norm_modulate_kernel(const T* __restrict__ x, int64_t ldx, T* __restrict__ y,
+                                                             int64_t ldy, int64_t rows_per_batch, int D, int kind,
+                                                             float eps, ModVec<T> shift, ModVec<T> scale) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int64_t b = row / rows_per_batch, t = row - b * rows_per_batch;
+  const T* xr = x + row * ldx;
+  T* yr = y + row * ldy;
+  const int nvec = D >> 3;
+  float v[NV][8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nvec) {
+      ld8<T>(xr + c * 8, v[i]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s += (kind == LTX_NORM_LAYER) ? v[i][k] : v[i][k] * v[i][k];
+    }
+  }
+  float mean = 0.f, rstd;
+  if (kind == LTX_NORM_NONE) {
+    rstd = 1.f;
+  } else if (kind == LTX_NORM_LAYER) {
+    mean = block_sum(s, red) / float(D);
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nvec) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float d = v[i][k] - mean;
+          s2 += d * d;
+        }
+      }
+    }
+    rstd = rsqrtf(block_sum(s2, red) / float(D) + eps);
+  } else {
+    rstd = rsqrtf(block_sum(s, red) / float(D) + eps);
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nvec) {
+      float o[8], sc[8], sh[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = round_to<T>((v[i][k] - mean) * rstd);
+      if (scale.on) {
+        scale.at8(b, t, c * 8, sc);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = round_to<T>(o[k] * round_to<T>(1.f + sc[k]));
+      }
+      if (shift.on) {
+        shift.at8(b, t, c * 8, sh);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = o[k] + sh[k];
+      }
+      st8<T>(yr + c * 8, o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// q/k RMSNorm over the whole inner dim (with weight) + split RoPE, in place
+// (ltx_nn.py:186-187,214-218 and 99-115). Thread -> (head h, 8 pair indices j0..j0+7):
+// it owns x[h*d + j] and its rotation partner x[h*d + d/2 + j].
+// ---------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(1024) qk_norm_rope_kernel(T* __restrict__ x, int64_t ldx, int64_t rows_per_batch,
+                                                            int heads, int d, const T* __restrict__ w, float eps,
+                                                            const T* __restrict__ cos_t,
+                                                            const T* __restrict__ sin_t, int64_t ld_rope,
+                                                            int64_t rope_ld_batch) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int64_t b = row / rows_per_batch, t = row - b * rows_per_batch;
+  const int per_head = d >> 4;  // threads per head
+  const int nthr = heads * per_head;
+  const int D = heads * d;
+  const bool active = threadIdx.x < nthr;
+  const int h = threadIdx.x / per_head;
+  const int j0 = (threadIdx.x % per_head) * 8;
+  const int c1 = h * d + j0, c2 = c1 + (d >> 1);
+  T* xr = x + row * ldx;
+  float a[8], bb[8];
+  float s = 0.f;
+  if (active) {
+    ld8<T>(xr + c1, a);
+    ld8<T>(xr + c2, bb);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += a[k] * a[k] + bb[k] * bb[k];
+  }
+  const float ss = block_sum(s, red);
+  if (!active) return;
+  if (w != nullptr) {  // NULL weight: rotation only
+    const float rstd = rsqrtf(ss / float(D) + eps);
+    float w1[8], w2[8];
+    ld8<T>(w + c1, w1);
+    ld8<T>(w + c2, w2);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      a[k] = round_to<T>(a[k] * rstd * w1[k]);
+      bb[k] = round_to<T>(bb[k] * rstd * w2[k]);
+    }
+  }
+  if (cos_t != nullptr) {
+    const int64_t ro = b * rope_ld_batch + t * ld_rope + h * (d >> 1) + j0;
+    float cs[8], sn[8];
+    ld8<T>(cos_t + ro, cs);
+    ld8<T>(sin_t + ro, sn);
+    float o1[8], o2[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      // first*c - second*s ; second*c + first*s, each product rounded like the
+      // reference's separate torch ops (no fused multiply-add).
+      o1[k] = round_to<T>(__fsub_rn(round_to<T>(__fmul_rn(a[k], cs[k])), round_to<T>(__fmul_rn(bb[k], sn[k]))));
+      o2[k] = round_to<T>(__fadd_rn(round_to<T>(__fmul_rn(bb[k], cs[k])), round_to<T>(__fmul_rn(a[k], sn[k]))));
+    }
+    st8<T>(xr + c1, o1);
+    st8<T>(xr + c2, o2);
+  } else {
+    st8<T>(xr + c1, a);
+    st8<T>(xr + c2, bb);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// RoPE tables (ltx_nn.py:80-96): column c of (T, dim/2): c < pad -> (1, 0); else
+// k = c - pad, f = k / n_axes, axis = k % n_axes, mid = (start + end) / 2 of the
+// token's bounds on that axis, angle = freqs[f] * ((mid / max_pos[axis]) * 2 - 1).
+// ---------------------------------------------------------------------------------
+template <typename T>
+__global__ void rope_tables_kernel(const float* __restrict__ bounds, int n_axes, int64_t T_, const float* __restrict__ freqs,
+                                   int n_freq, const float* __restrict__ max_pos, int half, T* __restrict__ cos_o,
+                                   T* __restrict__ sin_o) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= T_ * half) return;
+  const int64_t t = i / half;
+  const int c = int(i - t * half);
+  const int pad = half - n_freq * n_axes;
+  float cv = 1.f, sv = 0.f;
+  if (c >= pad) {
+    const int k = c - pad;
+    const int f = k / n_axes, axis = k - (k / n_axes) * n_axes;
+    const float* bt = bounds + (int64_t(axis) * T_ + t) * 2;
+    const float mid = __fdiv_rn(__fadd_rn(bt[0], bt[1]), 2.f);
+    const float frac = __fdiv_rn(mid, max_pos[axis]);
+    const float ang = __fmul_rn(freqs[f], __fsub_rn(__fmul_rn(frac, 2.f), 1.f));
+    cv = cosf(ang);
+    sv = sinf(ang);
+  }
+  st_elem<T>(cos_o + i, cv);
+  st_elem<T>(sin_o + i, sv);
+}
+
+// ---------------------------------------------------------------------------------
+// GELU-tanh (ltx_nn.py:248)
+// ---------------------------------------------------------------------------------
+template <typename T>
+__global__ void gelu_tanh_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n) {
+  const int64_t nv = n >> 3;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += stride) {
+    float v[8];
+    ld8<T>(x + i * 8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = gelu_tanh_f(v[k]);
+    st8<T>(y + i * 8, v);
+  }
+  // tail (n % 8)
+  const int64_t tail0 = nv * 8;
+  const int64_t i = tail0 + int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n && i < tail0 + 8) st_elem<T>(y + i, gelu_tanh_f(ld_elem<T>(x + i)));
+}
+
+// ---------------------------------------------------------------------------------
+// out = x + round(y * gate)              (ltx_dit.py:265,277,311,314)
+// ---------------------------------------------------------------------------------
+template <typename T>
+__global__ void gate_residual_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ y, int64_t ldy,
+                                     T* __restrict__ out, int64_t ldo, int64_t rows, int64_t rows_per_batch, int D,
+                                     ModVec<T> gate) {
+  const int nvr = D >> 3;
+  const int64_t total = rows * nvr;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t row = i / nvr;
+    const int c = int(i - row * nvr) * 8;
+    const int64_t b = row / rows_per_batch, t = row - b * rows_per_batch;
+    float xv[8], yv[8], g[8];
+    ld8<T>(x + row * ldx + c, xv);
+    ld8<T>(y + row * ldy + c, yv);
+    if (gate.on) {
+      gate.at8(b, t, c, g);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) g[k] = 1.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) xv[k] = xv[k] + round_to<T>(yv[k] * g[k]);
+    st8<T>(out + row * ldo + c, xv);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Timestep sinusoid [cos, sin] (standalone/common.py:138-148), argument t*scale.
+// ---------------------------------------------------------------------------------
+template <typename T>
+__global__ void timestep_embedding_kernel(const float* __restrict__ tv, int64_t n, float scale, int dim,
+                                          float log_max_period, T* __restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n * dim) return;
+  const int64_t r = i / dim;
+  const int c = int(i - r * dim);
+  const int half = dim >> 1;
+  float v = 0.f;  // odd-dim pad column
+  if (c < 2 * half) {
+    const int j = c < half ? c : c - half;
+    const float f = expf(__fdiv_rn(__fmul_rn(-log_max_period, float(j)), float(half)));
+    const float arg = __fmul_rn(__fmul_rn(tv[r], scale), f);
+    v = c < half ? cosf(arg) : sinf(arg);
+  }
+  st_elem<T>(out + i, v);
+}
+
+// ---------------------------------------------------------------------------------
+// X0 + CFG guide + Euler (ltx_dit.py:591-593, 551-562 with rescale 0, 602-606).
+// vel rows [0, T) are the cond pass, [T, 2T) the uncond pass of the same latent.
+// ---------------------------------------------------------------------------------
+template <typename T>
+LTX_DEVICE void cfg_euler_point(float vc, float vu, float lat, float tsc, float tsu, float cfg_m1, float sigma,
+                                float dt, float& den, float& nxt) {
+  // x0 = (latent - v * timesteps).to(dtype)
+  const float x0c = round_to<T>(__fsub_rn(lat, __fmul_rn(vc, tsc)));
+  const float x0u = round_to<T>(__fsub_rn(lat, __fmul_rn(vu, tsu)));
+  // pred = cond + (cfg - 1) * (cond - uncond), then .to(dtype)
+  den = round_to<T>(__fadd_rn(x0c, __fmul_rn(cfg_m1, __fsub_rn(x0c, x0u))));
+  // velocity = ((sample - denoised) / sigma).to(dtype); sample + velocity * dt
+  const float vel = round_to<T>(__fdiv_rn(__fsub_rn(lat, den), sigma));
+  nxt = round_to<T>(__fadd_rn(lat, __fmul_rn(vel, dt)));
+}
+
+template <typename T>
+__global__ void cfg_euler_kernel(const T* __restrict__ vel, const T* __restrict__ latent, const float* __restrict__ ts,
+                                 int64_t T_, int C, float cfg_m1, float sigma, float dt, T* __restrict__ denoised,
+                                 T* __restrict__ new_latent) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t n = T_ * C;
+  if (i >= n) return;
+  const int64_t t = i / C;
+  float den, nxt;
+  cfg_euler_point<T>(ld_elem<T>(vel + i), ld_elem<T>(vel + n + i), ld_elem<T>(latent + i), ts[t], ts[T_ + t], cfg_m1,
+                     sigma, dt, den, nxt);
+  if (denoised) st_elem<T>(denoised + i, den);
+  st_elem<T>(new_latent + i, nxt);
+}
+
+inline unsigned grid_for(int64_t work, int threads) {
+  int64_t g = (work + threads - 1) / threads;
+  const int64_t cap = int64_t(num_sms()) * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return unsigned(g);
+}
+
+template <typename T>
+void launch_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows, int64_t rpb, int D, int kind,
+                          float eps, const ltx_modulation* m, cudaStream_t s) {
+  const int nvec = D / 8;
+  int threads = ((nvec + 31) / 32) * 32;
+  int nv = 1;
+  while (threads > 1024 && nv < kMaxVecPerThread) {
+    ++nv;
+    threads = (((nvec + nv - 1) / nv + 31) / 32) * 32;
+  }
+  LTX_UNSUPPORTED(threads <= 1024, "D too large for norm_modulate");
+  ModVec<T> sh = make_modvec<T>(m, 0), sc = make_modvec<T>(m, 1);
+  auto xp = static_cast<const T*>(x);
+  auto yp = static_cast<T*>(y);
+  switch (nv) {
+    case 1: norm_modulate_kernel<T, 1><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc); break;
+    case 2: norm_modulate_kernel<T, 2><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc); break;
+    case 3: norm_modulate_kernel<T, 3><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc); break;
+    default: norm_modulate_kernel<T, 4><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc); break;
+  }
+}
+
+}  // namespace detail
+}  // namespace ltx
+
+using namespace ltx;
+using namespace ltx::detail;
+
+#define LTX_CHECK_DTYPE(dt) LTX_REQUIRE((dt) == LTX_F32 || (dt) == LTX_BF16, "dtype must be F32 or BF16")
+
+extern "C" int ltx_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t rows,
+                                 int64_t rows_per_batch, int D, int norm_kind, float eps, const ltx_modulation* mod,
+                                 int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(x && y, "x and y must be non-NULL");
+  LTX_REQUIRE(rows > 0 && rows < (int64_t(1) << 31), "rows out of range");
+  LTX_REQUIRE(D > 0 && D % 8 == 0, "D must be a positive multiple of 8");
+  LTX_REQUIRE(ldx % 8 == 0 && ldy % 8 == 0 && ldx >= D && ldy >= D, "ldx/ldy must be multiples of 8 and >= D");
+  LTX_REQUIRE(rows_per_batch > 0, "rows_per_batch must be positive");
+  LTX_REQUIRE(norm_kind == LTX_NORM_RMS || norm_kind == LTX_NORM_LAYER || norm_kind == LTX_NORM_NONE, "bad norm_kind");
+  check_vec_ptr(x, "x");
+  check_vec_ptr(y, "y");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LTX_F32)
+    launch_norm_modulate<float>(x, ldx, y, ldy, rows, rows_per_batch, D, norm_kind, eps, mod, s);
+  else
+    launch_norm_modulate<__nv_bfloat16>(x, ldx, y, ldy, rows, rows_per_batch, D, norm_kind, eps, mod, s);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_qk_norm_rope(void* x, int64_t ldx, int64_t rows, int64_t rows_per_batch, int heads, int head_dim,
+                                const void* weight, float eps, const void* cos_tab, const void* sin_tab,
+                                int64_t ld_rope, int64_t rope_ld_batch, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(x != nullptr, "x must be non-NULL");
+  LTX_REQUIRE(weight != nullptr || cos_tab != nullptr, "nothing to do: no weight and no RoPE tables");
+  LTX_REQUIRE(rows > 0 && rows < (int64_t(1) << 31), "rows out of range");
+  LTX_REQUIRE(heads > 0 && head_dim > 0 && head_dim % 16 == 0, "head_dim must be a positive multiple of 16");
+  const int nthr = heads * (head_dim / 16);
+  LTX_UNSUPPORTED(nthr <= 1024, "heads*head_dim too large (max 16384)");
+  LTX_REQUIRE(ldx % 8 == 0 && ldx >= int64_t(heads) * head_dim, "ldx must be a multiple of 8 and >= heads*head_dim");
+  LTX_REQUIRE(rows_per_batch > 0, "rows_per_batch must be positive");
+  LTX_REQUIRE((cos_tab == nullptr) == (sin_tab == nullptr), "cos and sin must both be given or both be NULL");
+  if (cos_tab) LTX_REQUIRE(ld_rope % 8 == 0 && rope_ld_batch % 8 == 0, "rope strides must be multiples of 8");
+  check_vec_ptr(x, "x");
+  check_vec_ptr(weight, "weight");
+  check_vec_ptr(cos_tab, "cos");
+  check_vec_ptr(sin_tab, "sin");
+  const int threads = ((nthr + 31) / 32) * 32;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LTX_F32)
+    qk_norm_rope_kernel<float><<<unsigned(rows), threads, 0, s>>>(
+        static_cast<float*>(x), ldx, rows_per_batch, heads, head_dim, static_cast<const float*>(weight), eps,
+        static_cast<const float*>(cos_tab), static_cast<const float*>(sin_tab), ld_rope, rope_ld_batch);
+  else
+    qk_norm_rope_kernel<__nv_bfloat16><<<unsigned(rows), threads, 0, s>>>(
+        static_cast<__nv_bfloat16*>(x), ldx, rows_per_batch, heads, head_dim,
+        static_cast<const __nv_bfloat16*>(weight), eps, static_cast<const __nv_bfloat16*>(cos_tab),
+        static_cast<const __nv_bfloat16*>(sin_tab), ld_rope, rope_ld_batch);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_rope_tables(const float* bounds, int n_axes, int64_t T, const float* freqs, int n_freq,
+                               const float* max_pos, int dim, void* cos_out, void* sin_out, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(bounds && freqs && max_pos && cos_out && sin_out, "NULL argument");
+  LTX_REQUIRE(n_axes > 0 && T > 0 && n_freq > 0 && dim > 0 && dim % 2 == 0, "bad sizes");
+  const int half = dim / 2;
+  LTX_REQUIRE(n_freq * n_axes <= half, "n_freq * n_axes must be <= dim/2");
+  const int64_t n = T * half;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = unsigned((n + 255) / 256);
+  if (dtype == LTX_F32)
+    rope_tables_kernel<float><<<blocks, 256, 0, s>>>(bounds, n_axes, T, freqs, n_freq, max_pos, half,
+                                                     static_cast<float*>(cos_out), static_cast<float*>(sin_out));
+  else
+    rope_tables_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(bounds, n_axes, T, freqs, n_freq, max_pos, half,
+                                                             static_cast<__nv_bfloat16*>(cos_out),
+                                                             static_cast<__nv_bfloat16*>(sin_out));
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_gelu_tanh(const void* x, void* y, int64_t n, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(x && y, "NULL argument");
+  LTX_REQUIRE(n > 0, "n must be positive");
+  check_vec_ptr(x, "x");
+  check_vec_ptr(y, "y");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned g = grid_for(n / 8 + 8, 256);
+  if (dtype == LTX_F32)
+    gelu_tanh_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), static_cast<float*>(y), n);
+  else
+    gelu_tanh_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                       static_cast<__nv_bfloat16*>(y), n);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_gate_residual(const void* x, int64_t ldx, const void* y, int64_t ldy, void* out, int64_t ldo,
+                                 int64_t rows, int64_t rows_per_batch, int D, const ltx_modulation* gate, int dtype,
+                                 void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(x && y && out, "NULL argument");
+  LTX_REQUIRE(rows > 0 && D > 0 && D % 8 == 0, "rows must be positive and D a multiple of 8");
+  LTX_REQUIRE(ldx % 8 == 0 && ldy % 8 == 0 && ldo % 8 == 0, "leading dimensions must be multiples of 8");
+  LTX_REQUIRE(rows_per_batch > 0, "rows_per_batch must be positive");
+  check_vec_ptr(x, "x");
+  check_vec_ptr(y, "y");
+  check_vec_ptr(out, "out");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned g = grid_for(rows * (D / 8), 256);
+  if (dtype == LTX_F32)
+    gate_residual_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), ldx, static_cast<const float*>(y), ldy,
+                                                  static_cast<float*>(out), ldo, rows, rows_per_batch, D,
+                                                  make_modvec<float>(gate, 1));
+  else
+    gate_residual_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(y), ldy,
+        static_cast<__nv_bfloat16*>(out), ldo, rows, rows_per_batch, D, make_modvec<__nv_bfloat16>(gate, 1));
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_timestep_embedding(const float* t, int64_t n, float scale, int dim, float max_period, void* out,
+                                      int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(t && out, "NULL argument");
+  LTX_REQUIRE(n > 0 && dim > 1 && max_period > 0.f, "bad sizes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t total = n * dim;
+  const unsigned blocks = unsigned((total + 255) / 256);
+  const float lmp = logf(max_period);
+  if (dtype == LTX_F32)
+    timestep_embedding_kernel<float><<<blocks, 256, 0, s>>>(t, n, scale, dim, lmp, static_cast<float*>(out));
+  else
+    timestep_embedding_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(t, n, scale, dim, lmp,
+                                                                    static_cast<__nv_bfloat16*>(out));
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_cfg_euler(const void* vel, const void* latent, const float* timesteps, int64_t T, int C,
+                             float cfg_scale, float sigma, float sigma_next, void* denoised, void* new_latent,
+                             int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(vel && latent && timesteps && new_latent, "NULL argument");
+  LTX_REQUIRE(T > 0 && C > 0, "bad sizes");
+  LTX_REQUIRE(sigma != 0.f, "sigma must be non-zero (Euler divides by it)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n = T * C;
+  const unsigned blocks = unsigned((n + 255) / 256);
+  const float cfg_m1 = cfg_scale - 1.f;
+  const float dt = sigma_next - sigma;
+  if (dtype == LTX_F32)
+    cfg_euler_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(vel), static_cast<const float*>(latent),
+                                                   timesteps, T, C, cfg_m1, sigma, dt, static_cast<float*>(denoised),
+                                                   static_cast<float*>(new_latent));
+  else
+    cfg_euler_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(vel), static_cast<const __nv_bfloat16*>(latent), timesteps, T, C, cfg_m1,
+        sigma, dt, static_cast<__nv_bfloat16*>(denoised), static_cast<__nv_bfloat16*>(new_latent));
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}

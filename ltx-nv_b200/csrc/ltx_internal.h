@@ -1,0 +1,63 @@
+// Host-side plumbing shared by the C-ABI entry points: status codes, the thread-local
+// error message, argument checks and TMA descriptor encoding.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <string>
+
+#include "../../include/ltxb200.h"
+
+namespace ltx {
+
+void set_error(const std::string& msg);
+void clear_error();
+
+struct ApiError {
+  int code;
+  std::string msg;
+};
+
+// Encode a 2-D, 128-byte-swizzled bf16 tensor map over a row-major matrix.
+// inner = elements per row (contiguous), outer = rows, ld = elements between rows,
+// box = (box_inner x box_outer) elements; box_inner * 2 must be <= 128.
+// Throws ApiError on invalid input.
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+                              uint32_t box_outer);
+
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+}  // namespace ltx
+
+#define LTX_API_BEGIN \
+  try {               \
+    ltx::clear_error();
+#define LTX_API_END                                              \
+  return LTX_OK;                                                 \
+  }                                                              \
+  catch (const ltx::ApiError& e) {                               \
+    ltx::set_error(e.msg);                                       \
+    return e.code;                                               \
+  }                                                              \
+  catch (...) {                                                  \
+    ltx::set_error("unexpected C++ exception");                  \
+    return LTX_ERR_INVALID;                                      \
+  }
+
+#define LTX_REQUIRE(cond, msg)                                                   \
+  do {                                                                           \
+    if (!(cond)) throw ltx::ApiError{LTX_ERR_INVALID, std::string(__func__) + ": " + (msg)}; \
+  } while (0)
+
+#define LTX_UNSUPPORTED(cond, msg)                                                   \
+  do {                                                                               \
+    if (!(cond)) throw ltx::ApiError{LTX_ERR_UNSUPPORTED, std::string(__func__) + ": " + (msg)}; \
+  } while (0)
+
+#define LTX_CUDA(call)                                                                                  \
+  do {                                                                                                  \
+    cudaError_t err_ = (call);                                                                          \
+    if (err_ != cudaSuccess)                                                                            \
+      throw ltx::ApiError{LTX_ERR_CUDA, std::string(__func__) + ": " #call ": " + cudaGetErrorString(err_)}; \
+  } while (0)

@@ -1,0 +1,211 @@
+"""Generate the golden fixtures in tests/golden/ from the reference implementation.
+
+The reference (lipaul/ltx-nv, standalone/ltx_dit.py + ltx_nn.py) is pure PyTorch and is
+importable in the build container, so this script runs it on CPU for small
+configurations and records inputs and outputs. The fixtures pin the CPU oracle
+(oracle/ltx_oracle.py, oracle/philox_oracle.c); the GPU parity tests then compare the
+sm_100a kernels with that oracle. The reference is not needed at test time.
+
+    python tests/golden/make_golden.py [--reference /path/to/lipaul/ltx-nv]
+
+Fixtures written:
+  philox_m1.npz       the reference's own golden noise (cuda_c_standalone/artifacts/
+                      m1_philox: torch.randn seed 10, bf16, video [1,3456,128] then audio
+                      [1,68,128], RTX 6000 Ada launch grid): the audio tensor and the
+                      first 65536 video values as uint16 bits, and a SHA-256 of all
+                      video bits.
+  dit_<case>.pt       config, parameter (name, shape) list, weight seed, inputs and the
+                      reference's outputs for LTXModel.forward and for two CFG denoise
+                      steps (X0 + guide + Euler).
+  sched.pt            ltx2_scheduler_sigmas(30), video/audio positions.
+
+Weights are N(0, 0.02) from numpy's PCG64 (platform independent) in the reference's
+named_parameters() order, q/k RMSNorm gains offset by +1 (oracle.synthetic_state_dict).
+"""
+
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import hashlib
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parents[2]
+OUT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from oracle import ltx_oracle  # noqa: E402
+
+
+def _import_reference(ref_root: Path):
+    sys.path.insert(0, str(ref_root / "standalone"))
+    import ltx_dit  # noqa: F401
+
+    return sys.modules["ltx_dit"]
+
+
+def rng_normal(shape, seed, scale=1.0, dtype=torch.float32):
+    g = np.random.default_rng(seed)
+    return torch.from_numpy(g.standard_normal(shape, dtype=np.float32) * np.float32(scale)).to(dtype)
+
+
+CASES = {
+    # video-only benchmark geometry in miniature: context width != hidden, no cross-adaLN
+    "tiny_video": dict(num_layers=2, video_heads=4, video_head_dim=16, video_cross_dim=96, audio_heads=2,
+                       audio_head_dim=16, audio_cross_dim=32, cross_attention_adaln=False),
+    # the real LTX-2.5 AV structure (cross-adaLN, A<->V attention) in miniature
+    "tiny_av": dict(num_layers=2, video_heads=4, video_head_dim=16, video_cross_dim=64, audio_heads=2,
+                    audio_head_dim=16, audio_cross_dim=32, cross_attention_adaln=True),
+}
+FRAMES = (2, 3, 4)  # latent f, h, w -> 24 video tokens
+AUDIO_T = 5
+TEXT_S = 8
+WEIGHT_SEED = 1
+
+
+def build_reference_model(ld, cfg, dtype):
+    torch.manual_seed(0)
+    model = ld.LTXModel(cfg)
+    shapes = [(n, tuple(p.shape)) for n, p in model.named_parameters()]
+    sd = ltx_oracle.synthetic_state_dict(shapes, WEIGHT_SEED, dtype=torch.float32)
+    model.load_state_dict(sd)
+    return model.to(dtype).eval(), shapes
+
+
+def patch_context_view(ld):
+    """The survey's adapter for context width != hidden: undo the view at ltx_dit.py:157."""
+    orig = ld.ArgsPreprocessor.prepare
+
+    def prepare(self, modality, cross):
+        ctx = modality.context
+        b = ctx.shape[0]
+        hidden = self.m.cfg.audio_dim if self.stream == "audio" else self.m.cfg.video_dim
+        if ctx.numel() % (b * hidden) != 0:
+            raise ValueError("context size not viewable; pick another fixture size")
+        args = orig(self, modality, cross)
+        return dataclasses.replace(args, context=ctx)
+
+    ld.ArgsPreprocessor.prepare = prepare
+    return orig
+
+
+def video_inputs(ld, cfg, dtype, batch, sigma, seed):
+    f, h, w = FRAMES
+    t = f * h * w
+    latent = rng_normal((batch, t, cfg.video_in), seed).to(dtype)
+    positions = ld.video_positions(batch, f, h, w, 24.0, "cpu")
+    kf = torch.zeros(batch, t, 1)
+    kf[:, : h * w] = 1.0
+    ctx = rng_normal((batch, TEXT_S, cfg.video_cross_dim), seed + 1).to(dtype)
+    sig = torch.full((batch,), float(sigma), dtype=torch.float32)
+    ts = torch.ones(batch, t, 1) * sig.view(batch, 1, 1)
+    return ld.Modality(latent=latent, sigma=sig, timesteps=ts, positions=positions, context=ctx, keyframes_mask=kf)
+
+
+def audio_inputs(ld, cfg, dtype, batch, sigma, seed, enabled=True, t=AUDIO_T):
+    latent = rng_normal((batch, t, cfg.audio_in), seed + 2).to(dtype)
+    positions = ld.audio_positions(batch, t, "cpu")
+    ctx = rng_normal((batch, TEXT_S, cfg.audio_cross_dim), seed + 3).to(dtype)
+    sig = torch.full((batch,), float(sigma), dtype=torch.float32)
+    ts = torch.ones(batch, t, 1) * sig.view(batch, 1, 1)
+    return ld.Modality(latent=latent, sigma=sig, timesteps=ts, positions=positions, context=ctx, enabled=enabled)
+
+
+def modality_dict(m):
+    return {k: v for k, v in dataclasses.asdict(m).items()}
+
+
+@torch.inference_mode()
+def make_case(ld, name, overrides, dtype):
+    cfg = ld.DiTConfig(**overrides)
+    model, shapes = build_reference_model(ld, cfg, dtype)
+    video_only = name == "tiny_video"
+    batch = 2
+    video = video_inputs(ld, cfg, dtype, batch, 0.7, seed=100)
+    if video_only:
+        # Disabled 1-token audio stream + zero A2V row (ltx_dit.py:253-257, 286).
+        audio = audio_inputs(ld, cfg, dtype, batch, 0.7, seed=100, enabled=False, t=1)
+        pert = torch.ones(4, cfg.num_layers, batch, dtype=dtype)
+        pert[2] = 0
+    else:
+        audio = audio_inputs(ld, cfg, dtype, batch, 0.7, seed=100)
+        pert = None
+    vx, ax = model(video, audio, pert)
+    rec = {
+        "case": name,
+        "dtype": str(dtype).replace("torch.", ""),
+        "config": dataclasses.asdict(cfg),
+        "param_shapes": shapes,
+        "weight_seed": WEIGHT_SEED,
+        "video": modality_dict(video),
+        "audio": None if video_only else modality_dict(audio),
+        "vx": vx.clone(),
+        "ax": None if video_only else ax.clone(),
+    }
+    # Two CFG denoise steps of the video stream (B=2 forward, X0, guide, Euler) on a
+    # (1, T, C) latent with sigmas linspace(1, 0, 9) (BASELINE config 1's schedule).
+    if video_only:
+        sigmas = torch.linspace(1.0, 0.0, 9)
+        latent = video.latent[:1].clone()
+        ctx_pos, ctx_neg = video.context[:1].clone(), video.context[1:].clone()
+        params = ld.GuiderParams(cfg_scale=3.0, stg_scale=0.0, rescale_scale=0.0, modality_scale=1.0, stg_blocks=())
+        steps = []
+        for idx in range(2):
+            sig = sigmas[idx]
+            sig2 = sig.expand(2)
+            lat2 = latent.repeat(2, 1, 1)
+            ts = torch.ones(2, latent.shape[1], 1) * sig2.view(2, 1, 1)
+            vm = ld.Modality(latent=lat2, sigma=sig2, timesteps=ts, positions=video.positions,
+                             context=torch.cat([ctx_pos, ctx_neg]), keyframes_mask=video.keyframes_mask)
+            am = audio_inputs(ld, cfg, dtype, 2, float(sig), seed=100, enabled=False, t=1)
+            vel, _ = model(vm, am, pert)
+            x0 = (lat2.float() - vel.float() * ts.float()).to(vel.dtype)
+            den = ld.guide(x0[0:1], x0[1:2], x0[0:1], x0[0:1], params)
+            nxt = ld.euler_step(latent, den, sigmas, idx)
+            steps.append({"latent_in": latent.clone(), "velocity": vel.clone(), "denoised": den.clone(),
+                          "latent_out": nxt.clone()})
+            latent = nxt
+        rec["steps"] = {"sigmas": sigmas, "cfg_scale": 3.0, "context_pos": ctx_pos, "context_neg": ctx_neg,
+                        "positions": video.positions[:1].clone(), "keyframes_mask": video.keyframes_mask[:1].clone(),
+                        "records": steps}
+    return rec
+
+
+def make_philox(ref_root: Path):
+    art = ref_root / "cuda_c_standalone" / "artifacts" / "m1_philox"
+    v = np.fromfile(art / "video_noise.bin", dtype=np.uint16)
+    a = np.fromfile(art / "audio_noise.bin", dtype=np.uint16)
+    assert v.size == 3456 * 128 and a.size == 68 * 128
+    np.savez(OUT / "philox_m1.npz", video_prefix=v[:65536], audio=a, video_numel=np.int64(v.size),
+             video_sha256=np.frombuffer(hashlib.sha256(v.tobytes()).digest(), dtype=np.uint8), seed=np.int64(10),
+             ada_grid_video=np.int64(852), ada_grid_audio=np.int64(34))
+
+
+def make_sched(ld):
+    torch.save({"sigmas30": ld.ltx2_scheduler_sigmas(30), "sigmas8_tokens480": ld.ltx2_scheduler_sigmas(8, 480),
+                "video_positions": ld.video_positions(1, 3, 4, 5, 24.0, "cpu"),
+                "audio_positions": ld.audio_positions(1, 7, "cpu")}, OUT / "sched.pt")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    ref_root = Path(args.reference)
+    ld = _import_reference(ref_root)
+    patch_context_view(ld)
+    make_philox(ref_root)
+    make_sched(ld)
+    for name, ov in CASES.items():
+        for dtype in (torch.float32, torch.bfloat16):
+            rec = make_case(ld, name, ov, dtype)
+            torch.save(rec, OUT / f"dit_{name}_{rec['dtype']}.pt")
+            print("wrote", name, rec["dtype"], tuple(rec["vx"].shape))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,351 @@
+"""Kernel-level parity on the B200: every libltxb200 entry point against the CPU oracle
+(Philox) or a float32 PyTorch restatement of the same op (floating-point kernels)."""
+
+import hashlib
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import _native as nat
+import golden_cases as gc
+from oracle import ltx_oracle, philox_oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_l2(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+def bits16(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+# ------------------------------------------------------------------------------ Philox
+
+
+def test_philox_matches_reference_golden_noise_bit_exact():
+    g = np.load(gc.GOLDEN / "philox_m1.npz")
+    n_v = int(g["video_numel"])
+    grid_v, grid_a = int(g["ada_grid_video"]), int(g["ada_grid_audio"])
+    v = torch.empty(n_v, dtype=torch.bfloat16, device=DEV)
+    nat.philox_randn(v, int(g["seed"]), 0, grid_v)
+    off = nat.philox_offset_increment(n_v, grid_v)
+    a = torch.empty(g["audio"].size, dtype=torch.bfloat16, device=DEV)
+    nat.philox_randn(a, int(g["seed"]), off, grid_a)
+    vb = bits16(v)
+    assert hashlib.sha256(vb.tobytes()).digest() == g["video_sha256"].tobytes()
+    assert (vb[: g["video_prefix"].size] == g["video_prefix"]).all()
+    assert (bits16(a) == g["audio"]).all()
+
+
+@pytest.mark.parametrize("shape,seed,dtype", [((2, 128, 16, 16, 24), 42, torch.float32),
+                                               ((1, 480, 128), 0, torch.float32),
+                                               ((1, 3456, 128), 10, torch.bfloat16),
+                                               ((3, 1001), 7, torch.float32),
+                                               ((5,), 3, torch.bfloat16)])
+def test_philox_bit_exact_vs_torch_randn_on_this_device(shape, seed, dtype):
+    gen = torch.Generator(device=DEV).manual_seed(seed)
+    ref1 = torch.randn(shape, dtype=dtype, device=DEV, generator=gen)
+    ref2 = torch.randn(shape, dtype=dtype, device=DEV, generator=gen)
+    n = ref1.numel()
+    grid = nat.philox_grid(n)
+    out = torch.empty(shape, dtype=dtype, device=DEV)
+    nat.philox_randn(out, seed, 0, grid)
+    assert torch.equal(out, ref1)
+    nat.philox_randn(out, seed, nat.philox_offset_increment(n, grid), grid)
+    assert torch.equal(out, ref2)
+
+
+def test_philox_raw_words_match_c_restatement():
+    threads, rounds, seed, offset = 700, 3, 0x1234_5678_9ABC, 8
+    out = torch.empty(threads * rounds * 4, dtype=torch.int32, device=DEV)
+    nat.philox_raw(out, threads, rounds, seed, offset)
+    got = out.cpu().numpy().view(np.uint32)
+    ref = philox_oracle.philox_raw(threads, rounds, seed, offset)
+    assert (got == ref).all()
+
+
+def test_philox_fp32_within_ulp_of_oracle_at_b200_grid():
+    n = 2 * 128 * 16 * 16 * 24
+    grid = nat.philox_grid(n)
+    out = torch.empty(n, dtype=torch.float32, device=DEV)
+    nat.philox_randn(out, 42, 0, grid)
+    ref = philox_oracle.randn(n, 42, 0, grid)
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.abs(got - ref).max() < 1e-4
+
+
+# ------------------------------------------------------------------------- element-wise
+
+
+def _mod_ref(table, mod, b, idx, d):
+    return (table[idx].float() + mod.view(mod.shape[0], -1)[b, idx * d:(idx + 1) * d].float())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("d", [64, 2048, 4096])
+@pytest.mark.parametrize("kind", [nat.LTX_NORM_RMS, nat.LTX_NORM_LAYER])
+def test_norm_modulate(dtype, d, kind):
+    torch.manual_seed(0)
+    b, t = 2, 37
+    x = torch.randn(b * t, d, device=DEV).to(dtype)
+    table = (torch.randn(6, d, device=DEV) * 0.1).to(dtype)
+    mod = (torch.randn(b, 6 * d, device=DEV) * 0.1).to(dtype)
+    y = torch.empty_like(x)
+    m = nat.modulation(table, mod, shift=(0, 0), scale=(d, d), mod_ld_batch=6 * d)
+    nat.norm_modulate(x, y, t, kind, 1e-6, m)
+    xf = x.float().view(b, t, d)
+    n = F.rms_norm(xf, (d,), eps=1e-6) if kind == nat.LTX_NORM_RMS else F.layer_norm(xf, (d,), eps=1e-6)
+    sh = torch.stack([_mod_ref(table, mod, i, 0, d) for i in range(b)])[:, None]
+    sc = torch.stack([_mod_ref(table, mod, i, 1, d) for i in range(b)])[:, None]
+    ref = (n * (1 + sc) + sh).view(b * t, d)
+    assert rel_l2(y, ref) < (1e-6 if dtype == torch.float32 else 8e-3)
+
+
+def test_norm_modulate_per_token_and_plain():
+    torch.manual_seed(1)
+    b, t, d = 2, 16, 256
+    x = torch.randn(b * t, d, device=DEV, dtype=torch.bfloat16)
+    mod = (torch.randn(b, t, 2 * d, device=DEV) * 0.1).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    m = nat.modulation(None, mod, shift=(0, 0), scale=(0, d), mod_ld_batch=t * 2 * d, mod_ld_tok=2 * d)
+    nat.norm_modulate(x, y, t, nat.LTX_NORM_RMS, 1e-6, m)
+    n = F.rms_norm(x.float().view(b, t, d), (d,), eps=1e-6)
+    ref = n * (1 + mod[..., d:].float()) + mod[..., :d].float()
+    assert rel_l2(y.view(b, t, d), ref) < 8e-3
+    nat.norm_modulate(x, y, t, nat.LTX_NORM_RMS, 1e-6, None)
+    assert rel_l2(y.view(b, t, d), n) < 5e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("heads,hd", [(32, 64), (32, 128), (4, 16), (2, 32)])
+def test_qk_norm_rope_vs_oracle(dtype, heads, hd):
+    torch.manual_seed(2)
+    b, f, h, w = 2, 2, 3, 5
+    t = f * h * w
+    d = heads * hd
+    pos = ltx_oracle.video_positions(b, f, h, w, 24.0)
+    cos_r, sin_r = ltx_oracle.rope_tables(pos, d, dtype, 10000.0, [20, 2048, 2048], heads)
+    x = torch.randn(b, t, d).to(dtype)
+    wgt = (1 + 0.02 * torch.randn(d)).to(dtype)
+    ref = ltx_oracle.apply_rope(ltx_oracle.rms_norm(x, 1e-6, wgt), (cos_r, sin_r))
+    # tables on the GPU from the same positions
+    freqs = ltx_oracle.freq_grid(10000.0, 3, d).to(DEV)
+    cos = torch.empty(t, d // 2, device=DEV, dtype=dtype)
+    sin = torch.empty_like(cos)
+    nat.rope_tables(pos[0].contiguous().to(DEV), freqs, torch.tensor([20.0, 2048.0, 2048.0], device=DEV), d, cos,
+                    sin)
+    ref_cos = cos_r[0].transpose(0, 1).reshape(t, d // 2)
+    assert rel_l2(cos.cpu(), ref_cos) < (1e-6 if dtype == torch.float32 else 4e-3)
+    xd = x.view(b * t, d).to(DEV).clone()
+    nat.qk_norm_rope(xd, t, heads, hd, wgt.to(DEV), 1e-6, cos, sin, rope_ld_batch=0)
+    assert rel_l2(xd.cpu().view(b, t, d), ref) < (2e-6 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gelu_gate_residual_timestep(dtype):
+    torch.manual_seed(3)
+    x = torch.randn(1000, 64, device=DEV).to(dtype)
+    y = torch.empty_like(x)
+    nat.gelu_tanh(x, y)
+    assert rel_l2(y, F.gelu(x.float(), approximate="tanh")) < (1e-6 if dtype == torch.float32 else 5e-3)
+    odd = torch.randn(1003, device=DEV).to(dtype)
+    oy = torch.empty_like(odd)
+    nat.gelu_tanh(odd, oy)
+    assert rel_l2(oy, F.gelu(odd.float(), approximate="tanh")) < (1e-6 if dtype == torch.float32 else 5e-3)
+    b, t, d = 2, 50, 64
+    r = torch.randn(b * t, d, device=DEV).to(dtype)
+    u = torch.randn(b * t, d, device=DEV).to(dtype)
+    g = (torch.randn(b, 6 * d, device=DEV) * 0.5).to(dtype)
+    table = torch.randn(6, d, device=DEV).to(dtype) * 0.1
+    out = torch.empty_like(r)
+    gm = nat.modulation(table, g, shift=None, scale=(2 * d, 2 * d), mod_ld_batch=6 * d)
+    nat.gate_residual(r, u, out, t, gm)
+    gate = torch.stack([_mod_ref(table, g, i, 2, d) for i in range(b)])[:, None]
+    ref = (r.float().view(b, t, d) + u.float().view(b, t, d) * gate).view(b * t, d)
+    assert rel_l2(out, ref) < (1e-6 if dtype == torch.float32 else 5e-3)
+    ts = torch.tensor([0.5, 1.0, 0.03], device=DEV)
+    emb = torch.empty(3, 256, device=DEV, dtype=dtype)
+    nat.timestep_embedding(ts, 1000.0, 256, 10000.0, emb)
+    ref = ltx_oracle.timestep_sinusoid(ts.cpu() * 1000, 256)
+    assert (emb.float().cpu() - ref).abs().max() < (2e-3 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_cfg_euler_vs_oracle(dtype):
+    torch.manual_seed(4)
+    t, c = 300, 128
+    lat = torch.randn(1, t, c).to(dtype)
+    vel = torch.randn(2, t, c).to(dtype)
+    sigmas = torch.linspace(1.0, 0.0, 9)
+    idx = 2
+    ts = torch.full((2, t), float(sigmas[idx]))
+    x0 = (lat.repeat(2, 1, 1).float() - vel.float() * ts[..., None]).to(dtype)
+    den_ref = ltx_oracle.guide_cfg(x0[0:1], x0[1:2], 3.0)
+    nxt_ref = ltx_oracle.euler_step(lat, den_ref, sigmas, idx)
+    den = torch.empty(1, t, c, device=DEV, dtype=dtype)
+    nxt = torch.empty_like(den)
+    nat.cfg_euler(vel.to(DEV), lat.to(DEV), ts.to(DEV), 3.0, float(sigmas[idx]), float(sigmas[idx + 1]), nxt, den)
+    assert torch.equal(den.cpu(), den_ref)
+    assert torch.equal(nxt.cpu(), nxt_ref)
+
+
+# ------------------------------------------------------------------------------- GEMM
+
+
+def _lin_ref(a, w, bias):
+    return a.float() @ w.float().t() + (bias.float() if bias is not None else 0)
+
+
+@pytest.mark.parametrize("m,n,k,bn", [(128, 256, 64, 0), (256, 256, 128, 0), (300, 384, 192, 128),
+                                      (1000, 6176, 256, 0), (777, 2048, 2048, 128), (4096, 2048, 2048, 256),
+                                      (40, 136, 72, 0), (12288, 512, 128, 0)])
+def test_linear_bf16_tcgen05(m, n, k, bn):
+    torch.manual_seed(5)
+    a = torch.randn(m, k, device=DEV, dtype=torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * k ** -0.5).to(torch.bfloat16)
+    bias = torch.randn(n, device=DEV, dtype=torch.bfloat16)
+    c = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    nat.gemm_set_tile_n(bn)
+    try:
+        nat.linear(a, w, c, nat.epilogue(bias=bias))
+    finally:
+        nat.gemm_set_tile_n(0)
+    torch.cuda.synchronize()
+    assert nat.device_error_flags() == 0
+    assert rel_l2(c, _lin_ref(a, w, bias)) < 4e-3
+
+
+def test_linear_bf16_strided_operands_and_epilogues():
+    torch.manual_seed(6)
+    b, t, d, k = 2, 200, 256, 512
+    m = b * t
+    big = torch.randn(m, 3 * k, device=DEV, dtype=torch.bfloat16)
+    a = big[:, k:2 * k]  # strided view (ld = 3k)
+    w = (torch.randn(d, k, device=DEV) * k ** -0.5).to(torch.bfloat16)
+    bias = torch.randn(d, device=DEV, dtype=torch.bfloat16)
+    base = _lin_ref(a, w, bias)
+    # GELU
+    c = torch.empty(m, d, device=DEV, dtype=torch.bfloat16)
+    nat.linear(a, w, c, nat.epilogue(nat.EPI_GELU_TANH, bias=bias))
+    assert rel_l2(c, F.gelu(base.to(torch.bfloat16).float(), approximate="tanh")) < 6e-3
+    # gate * residual, in place
+    res = torch.randn(m, d, device=DEV, dtype=torch.bfloat16)
+    res0 = res.clone()
+    table = torch.randn(6, d, device=DEV, dtype=torch.bfloat16) * 0.1
+    mod = torch.randn(b, 6 * d, device=DEV, dtype=torch.bfloat16) * 0.1
+    gm = nat.modulation(table, mod, shift=None, scale=(5 * d, 5 * d), mod_ld_batch=6 * d)
+    nat.linear(a, w, res, nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=bias, residual=res, gate=gm, rows_per_batch=t))
+    gate = torch.stack([_mod_ref(table, mod, i, 5, d) for i in range(b)])[:, None]
+    ref = (res0.float().view(b, t, d) + base.view(b, t, d) * gate).view(m, d)
+    assert rel_l2(res, ref) < 5e-3
+    # keyframe row add
+    mask = (torch.arange(m, device=DEV) % 7 == 0).float()
+    vec = torch.randn(d, device=DEV, dtype=torch.bfloat16)
+    nat.linear(a, w, c, nat.epilogue(nat.EPI_ROW_MASK_ADD, bias=bias, row_mask=mask, row_vec=vec))
+    assert rel_l2(c, base + mask[:, None] * vec.float()) < 4e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("m,n,k", [(2, 12288, 2048), (3, 64, 256), (31, 300, 8192), (2, 2048, 256)])
+def test_linear_skinny(dtype, m, n, k):
+    torch.manual_seed(7)
+    a = torch.randn(m, k, device=DEV).to(dtype)
+    w = (torch.randn(n, k, device=DEV) * k ** -0.5).to(dtype)
+    bias = torch.randn(n, device=DEV).to(dtype)
+    c = torch.empty(m, n, device=DEV, dtype=dtype)
+    nat.linear(a, w, c, nat.epilogue(bias=bias))
+    assert rel_l2(c, _lin_ref(a, w, bias)) < (1e-5 if dtype == torch.float32 else 4e-3)
+    nat.linear(a, w, c, nat.epilogue(nat.EPI_SILU, bias=bias, silu_input=True))
+    ref = F.silu(_lin_ref(F.silu(a.float()).to(dtype), w, bias).to(dtype).float())
+    assert rel_l2(c, ref) < (1e-5 if dtype == torch.float32 else 6e-3)
+
+
+@pytest.mark.parametrize("m,n,k", [(480, 2048, 2048), (960, 8192, 512), (100, 100, 200)])
+def test_linear_fp32_cuda_cores(m, n, k):
+    torch.manual_seed(8)
+    a = torch.randn(m, k, device=DEV)
+    w = torch.randn(n, k, device=DEV) * k ** -0.5
+    bias = torch.randn(n, device=DEV)
+    c = torch.empty(m, n, device=DEV)
+    nat.linear(a, w, c, nat.epilogue(bias=bias))
+    ref = (a.double() @ w.double().t() + bias.double()).float()
+    assert rel_l2(c, ref) < 1e-6
+
+
+# -------------------------------------------------------------------------- attention
+
+
+def _attn_ref(q, k, v, b, tq, tk, h, d, gate=None):
+    qh = q.float().view(b, tq, h, d).transpose(1, 2)
+    kh = k.float().view(b, tk, h, d).transpose(1, 2)
+    vh = v.float().view(b, tk, h, d).transpose(1, 2)
+    o = F.scaled_dot_product_attention(qh, kh, vh).transpose(1, 2)
+    if gate is not None:
+        o = o * (2 * torch.sigmoid(gate.float().view(b, tq, h, 1)))
+    return o.reshape(b * tq, h * d)
+
+
+@pytest.mark.parametrize("b,tq,tk,h,d", [(1, 128, 128, 2, 64), (2, 200, 300, 4, 64), (2, 6144, 128, 2, 64),
+                                         (2, 126, 1000, 3, 64), (1, 256, 640, 2, 128), (2, 100, 126, 2, 128),
+                                         (2, 1536, 1536, 32, 64)])
+def test_attention_bf16_tcgen05(b, tq, tk, h, d):
+    torch.manual_seed(9)
+    # a fused QKV-like buffer: q, k, v and gate logits side by side (strided operands);
+    # the gate block is padded so the row stride stays a multiple of 8 elements
+    qkv = torch.randn(b * max(tq, tk), 3 * h * d + ((h + 7) // 8) * 8, device=DEV, dtype=torch.bfloat16)
+    q = qkv[: b * tq, : h * d]
+    k = qkv[: b * tk, h * d:2 * h * d]
+    v = qkv[: b * tk, 2 * h * d:3 * h * d]
+    gate = qkv[: b * tq, 3 * h * d:]
+    o = torch.empty(b * tq, h * d, device=DEV, dtype=torch.bfloat16)
+    nat.attention(q, k, v, o, b, tq, tk, h, d, d ** -0.5, gate)
+    torch.cuda.synchronize()
+    assert nat.device_error_flags() == 0
+    assert rel_l2(o, _attn_ref(q, k, v, b, tq, tk, h, d, gate)) < 1e-2
+    nat.attention(q, k, v, o, b, tq, tk, h, d, d ** -0.5, None)
+    assert rel_l2(o, _attn_ref(q, k, v, b, tq, tk, h, d)) < 1e-2
+
+
+@pytest.mark.parametrize("b,tq,tk,h,d", [(2, 480, 480, 32, 64), (2, 100, 8, 4, 16 * 2), (1, 70, 90, 2, 128)])
+def test_attention_fp32(b, tq, tk, h, d):
+    torch.manual_seed(10)
+    q = torch.randn(b * tq, h * d, device=DEV)
+    k = torch.randn(b * tk, h * d, device=DEV)
+    v = torch.randn(b * tk, h * d, device=DEV)
+    gate = torch.randn(b * tq, h, device=DEV)
+    o = torch.empty(b * tq, h * d, device=DEV)
+    nat.attention(q, k, v, o, b, tq, tk, h, d, d ** -0.5, gate)
+    ref = _attn_ref(q.double(), k.double(), v.double(), b, tq, tk, h, d, gate.double())
+    assert rel_l2(o, ref) < 1e-5
+
+
+# ------------------------------------------------------------------- fused head + Euler
+
+
+@pytest.mark.parametrize("t,k", [(300, 256), (6144, 2048)])
+def test_proj_out_cfg_euler_bf16(t, k):
+    torch.manual_seed(11)
+    x = torch.randn(2 * t, k, device=DEV, dtype=torch.bfloat16)
+    w = (torch.randn(128, k, device=DEV) * k ** -0.5).to(torch.bfloat16)
+    bias = torch.randn(128, device=DEV, dtype=torch.bfloat16) * 0.1
+    lat = torch.randn(t, 128, device=DEV, dtype=torch.bfloat16)
+    ts = torch.full((2, t), 0.75, device=DEV)
+    vel = torch.empty(2 * t, 128, device=DEV, dtype=torch.bfloat16)
+    den = torch.empty(t, 128, device=DEV, dtype=torch.bfloat16)
+    nxt = torch.empty_like(den)
+    nat.proj_out_cfg_euler(x, w, bias, lat, ts, 3.0, 0.75, 0.625, nxt, den, vel)
+    torch.cuda.synchronize()
+    assert rel_l2(vel, _lin_ref(x, w, bias)) < 4e-3
+    # the epilogue's update applied to the kernel's own velocity must equal the
+    # element-wise kernel exactly
+    den2 = torch.empty_like(den)
+    nxt2 = torch.empty_like(den)
+    nat.cfg_euler(vel, lat, ts, 3.0, 0.75, 0.625, nxt2, den2)
+    assert torch.equal(den, den2) and torch.equal(nxt, nxt2)
