@@ -41,6 +41,10 @@ typedef enum { LTX_F32 = 0, LTX_BF16 = 1 } ltx_dtype;
 const char* ltx_last_error(void);
 /* ABI version of this library (bumped on any signature change). */
 int ltx_abi_version(void);
+/* Number of kernels this library has launched in this process (all devices, all
+ * streams; CUDA-graph replays are not counted). Instrumentation, no reference
+ * counterpart. */
+uint64_t ltx_launch_count(void);
 /* Read (and clear when `clear` != 0) the device error word that bounded waits set when
  * they give up (1 = mbarrier wait timed out). Synchronises `stream`. */
 int ltx_device_error_flags(int* flags, int clear, void* stream);
@@ -155,6 +159,9 @@ typedef struct {
 
 int ltx_linear(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, int64_t ldc, int64_t M, int64_t N,
                int64_t K, const ltx_epilogue* epi, int dtype, void* stream);
+/* Tuning knob (process-wide): force the tcgen05 tile width to 128 or 256 columns, or 0
+ * for the automatic choice. No counterpart in the reference (cuBLASLt picks its own). */
+int ltx_gemm_set_tile_n(int bn);
 
 /* ---------------------------------------------------------------------------------- */
 /* Attention: softmax(Q K^T * scale) V per (sample, head), non-causal, no mask, with   */
@@ -179,6 +186,15 @@ int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const 
  * (optionally) denoised (T, C). */
 int ltx_cfg_euler(const void* vel, const void* latent, const float* timesteps, int64_t T, int C, float cfg_scale,
                   float sigma, float sigma_next, void* denoised, void* new_latent, int dtype, void* stream);
+
+/* Guidance blend of four x0 predictions (ltx_dit.py:551-557, rescale_scale = 0):
+ * out = cond + (cfg-1)(cond-uncond) + stg(cond-ptb) + (modality-1)(cond-mod). */
+int ltx_guide(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n, float cfg_scale,
+              float stg_scale, float modality_scale, void* out, int dtype, void* stream);
+/* Euler step (ltx_dit.py:602-606): v = round((sample-denoised)/sigma);
+ * out = sample + v*(sigma_next - sigma). */
+int ltx_euler(const void* sample, const void* denoised, int64_t n, float sigma, float sigma_next, void* out,
+              int dtype, void* stream);
 
 /* Fused form: the output projection (proj_out, ltx_dit.py:378) of the head-modulated
  * hidden state x (2*T, K) with weight W (C, K) and bias, followed in its epilogue by the

@@ -71,6 +71,7 @@ class Epilogue(ctypes.Structure):
 _SIGNATURES = {
     "ltx_last_error": (ctypes.c_char_p, []),
     "ltx_abi_version": (ctypes.c_int, []),
+    "ltx_launch_count": (ctypes.c_uint64, []),
     "ltx_device_error_flags": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int, c_vp]),
     "ltx_philox_grid": (ctypes.c_int, [ctypes.c_int, c_i64, ctypes.POINTER(ctypes.c_int)]),
     "ltx_philox_offset_increment": (c_i64, [c_i64, ctypes.c_int]),
@@ -94,6 +95,9 @@ _SIGNATURES = {
                                      ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, ctypes.c_int, c_vp]),
     "ltx_cfg_euler": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_float,
                                      ctypes.c_float, c_vp, c_vp, ctypes.c_int, c_vp]),
+    "ltx_guide": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp,
+                                 ctypes.c_int, c_vp]),
+    "ltx_euler": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
     "ltx_proj_out_cfg_euler": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, ctypes.c_int, c_i64, c_vp, c_vp,
                                               ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp,
                                               ctypes.c_int, c_vp]),
@@ -128,9 +132,45 @@ def _check(name: str, status: int) -> None:
         raise LtxError(name, status, msg)
 
 
-def _call(name: str, *args):
+_profile: dict | None = None
+
+
+class profile:
+    """Context manager that brackets every library call with CUDA events on the
+    launching (current) stream: {label: [(start, end), ...]}, label = entry point name
+    plus the call's shape. Used by bench.py for per-kernel durations."""
+
+    def __enter__(self):
+        global _profile
+        _profile = {}
+        self.records = _profile
+        return self
+
+    def __exit__(self, *exc):
+        global _profile
+        _profile = None
+
+    def summary(self) -> dict:
+        torch.cuda.synchronize()
+        out = {}
+        for label, evs in self.records.items():
+            ms = [s.elapsed_time(e) for s, e in evs]
+            out[label] = {"launches": len(ms), "total_ms": sum(ms), "avg_ms": sum(ms) / len(ms)}
+        return out
+
+
+def _call(name: str, *args, label: str | None = None):
     lib = load_library()
-    _check(name, getattr(lib, name)(*args))
+    if _profile is None:
+        _check(name, getattr(lib, name)(*args))
+        return
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    st = getattr(lib, name)(*args)
+    e.record()
+    _check(name, st)
+    _profile.setdefault(label or name, []).append((s, e))
 
 
 def _stream(t: torch.Tensor | None = None) -> int:
@@ -190,6 +230,11 @@ def modulation(table: torch.Tensor | None, mod: torch.Tensor | None, *, shift: t
 
 def abi_version() -> int:
     return load_library().ltx_abi_version()
+
+
+def launch_count() -> int:
+    """Kernels launched by libltxb200 in this process so far."""
+    return int(load_library().ltx_launch_count())
 
 
 def device_error_flags(clear: bool = True) -> int:
@@ -307,6 +352,17 @@ def cfg_euler(vel: torch.Tensor, latent: torch.Tensor, timesteps: torch.Tensor, 
     t, c = latent.shape[-2], latent.shape[-1]
     _call("ltx_cfg_euler", _ptr(vel), _ptr(latent), _ptr(timesteps), t, c, cfg_scale, sigma, sigma_next,
           _ptr(denoised), _ptr(new_latent), _dt(latent), _stream(latent))
+
+
+def guide(cond: torch.Tensor, uncond: torch.Tensor, ptb: torch.Tensor, mod: torch.Tensor, cfg_scale: float,
+          stg_scale: float, modality_scale: float, out: torch.Tensor) -> None:
+    _call("ltx_guide", _ptr(cond), _ptr(uncond), _ptr(ptb), _ptr(mod), cond.numel(), cfg_scale, stg_scale,
+          modality_scale, _ptr(out), _dt(cond), _stream(cond))
+
+
+def euler(sample: torch.Tensor, denoised: torch.Tensor, sigma: float, sigma_next: float, out: torch.Tensor) -> None:
+    _call("ltx_euler", _ptr(sample), _ptr(denoised), sample.numel(), sigma, sigma_next, _ptr(out), _dt(sample),
+          _stream(sample))
 
 
 def proj_out_cfg_euler(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, latent: torch.Tensor,

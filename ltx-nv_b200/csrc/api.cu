@@ -3,6 +3,7 @@
 // CUDA runtime).
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -51,6 +52,9 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, u
   return m;
 }
 
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 int num_sms() {
   static int cache[64] = {0};
   int dev = 0;
@@ -69,6 +73,8 @@ int num_sms() {
 extern "C" const char* ltx_last_error(void) { return ltx::t_last_error.c_str(); }
 
 extern "C" int ltx_abi_version(void) { return 1; }
+
+extern "C" uint64_t ltx_launch_count(void) { return ltx::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int ltx_device_error_flags(int* flags, int clear, void* stream) {
   LTX_API_BEGIN

@@ -364,7 +364,7 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   dim3 grid(unsigned((Tq + 127) / 128), unsigned(H), unsigned(B));
   const float scale_log2 = scale * 1.4426950408889634f;
   kern<<<grid, 192, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), scale_log2,
-                                    static_cast<const __nv_bfloat16*>(gate), ld_gate);
+                                    static_cast<const __nv_bfloat16*>(gate), ld_gate), ltx::note_launch();
 }
 
 }  // namespace detail
@@ -404,9 +404,9 @@ extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t 
     auto Op = static_cast<float*>(o);
     auto Gp = static_cast<const float*>(gate_logits);
     switch (head_dim) {
-      case 32: attn_simt_kernel<32><<<grid, 128, 0, s>>>(Qp, ldq, Kp, ldk, Vp, ldv, Op, ldo, int(Tq), int(Tk), scale, Gp, ld_gate); break;
-      case 64: attn_simt_kernel<64><<<grid, 128, 0, s>>>(Qp, ldq, Kp, ldk, Vp, ldv, Op, ldo, int(Tq), int(Tk), scale, Gp, ld_gate); break;
-      case 128: attn_simt_kernel<128><<<grid, 128, 0, s>>>(Qp, ldq, Kp, ldk, Vp, ldv, Op, ldo, int(Tq), int(Tk), scale, Gp, ld_gate); break;
+      case 32: attn_simt_kernel<32><<<grid, 128, 0, s>>>(Qp, ldq, Kp, ldk, Vp, ldv, Op, ldo, int(Tq), int(Tk), scale, Gp, ld_gate), ltx::note_launch(); break;
+      case 64: attn_simt_kernel<64><<<grid, 128, 0, s>>>(Qp, ldq, Kp, ldk, Vp, ldv, Op, ldo, int(Tq), int(Tk), scale, Gp, ld_gate), ltx::note_launch(); break;
+      case 128: attn_simt_kernel<128><<<grid, 128, 0, s>>>(Qp, ldq, Kp, ldk, Vp, ldv, Op, ldo, int(Tq), int(Tk), scale, Gp, ld_gate), ltx::note_launch(); break;
       default: LTX_UNSUPPORTED(false, "fp32 attention supports head_dim 32, 64 and 128");
     }
   }

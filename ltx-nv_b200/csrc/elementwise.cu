@@ -276,6 +276,32 @@ __global__ void cfg_euler_kernel(const T* __restrict__ vel, const T* __restrict_
   st_elem<T>(new_latent + i, nxt);
 }
 
+// pred = c + (cfg-1)(c-u) + stg(c-p) + (mod-1)(c-m), evaluated left to right in fp32 and
+// rounded once, like the reference's fp32 tensor expression (ltx_dit.py:552-557).
+template <typename T>
+__global__ void guide_kernel(const T* __restrict__ c, const T* __restrict__ u, const T* __restrict__ p,
+                             const T* __restrict__ m, int64_t n, float cfg_m1, float stg, float mod_m1,
+                             T* __restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float cv = ld_elem<T>(c + i);
+  float r = __fadd_rn(cv, __fmul_rn(cfg_m1, __fsub_rn(cv, ld_elem<T>(u + i))));
+  r = __fadd_rn(r, __fmul_rn(stg, __fsub_rn(cv, ld_elem<T>(p + i))));
+  r = __fadd_rn(r, __fmul_rn(mod_m1, __fsub_rn(cv, ld_elem<T>(m + i))));
+  st_elem<T>(out + i, r);
+}
+
+// velocity = round((sample - denoised) / sigma); out = round(sample + velocity * dt).
+template <typename T>
+__global__ void euler_kernel(const T* __restrict__ s, const T* __restrict__ d, int64_t n, float sigma, float dt,
+                             T* __restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float sv = ld_elem<T>(s + i);
+  const float vel = round_to<T>(__fdiv_rn(__fsub_rn(sv, ld_elem<T>(d + i)), sigma));
+  st_elem<T>(out + i, __fadd_rn(sv, __fmul_rn(vel, dt)));
+}
+
 inline unsigned grid_for(int64_t work, int threads) {
   int64_t g = (work + threads - 1) / threads;
   const int64_t cap = int64_t(num_sms()) * 16;
@@ -299,10 +325,10 @@ void launch_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ldy, int6
   auto xp = static_cast<const T*>(x);
   auto yp = static_cast<T*>(y);
   switch (nv) {
-    case 1: norm_modulate_kernel<T, 1><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc); break;
-    case 2: norm_modulate_kernel<T, 2><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc); break;
-    case 3: norm_modulate_kernel<T, 3><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc); break;
-    default: norm_modulate_kernel<T, 4><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc); break;
+    case 1: norm_modulate_kernel<T, 1><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc), ltx::note_launch(); break;
+    case 2: norm_modulate_kernel<T, 2><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc), ltx::note_launch(); break;
+    case 3: norm_modulate_kernel<T, 3><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc), ltx::note_launch(); break;
+    default: norm_modulate_kernel<T, 4><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc), ltx::note_launch(); break;
   }
 }
 
@@ -360,12 +386,12 @@ extern "C" int ltx_qk_norm_rope(void* x, int64_t ldx, int64_t rows, int64_t rows
   if (dtype == LTX_F32)
     qk_norm_rope_kernel<float><<<unsigned(rows), threads, 0, s>>>(
         static_cast<float*>(x), ldx, rows_per_batch, heads, head_dim, static_cast<const float*>(weight), eps,
-        static_cast<const float*>(cos_tab), static_cast<const float*>(sin_tab), ld_rope, rope_ld_batch);
+        static_cast<const float*>(cos_tab), static_cast<const float*>(sin_tab), ld_rope, rope_ld_batch), ltx::note_launch();
   else
     qk_norm_rope_kernel<__nv_bfloat16><<<unsigned(rows), threads, 0, s>>>(
         static_cast<__nv_bfloat16*>(x), ldx, rows_per_batch, heads, head_dim,
         static_cast<const __nv_bfloat16*>(weight), eps, static_cast<const __nv_bfloat16*>(cos_tab),
-        static_cast<const __nv_bfloat16*>(sin_tab), ld_rope, rope_ld_batch);
+        static_cast<const __nv_bfloat16*>(sin_tab), ld_rope, rope_ld_batch), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
@@ -383,11 +409,11 @@ extern "C" int ltx_rope_tables(const float* bounds, int n_axes, int64_t T, const
   const unsigned blocks = unsigned((n + 255) / 256);
   if (dtype == LTX_F32)
     rope_tables_kernel<float><<<blocks, 256, 0, s>>>(bounds, n_axes, T, freqs, n_freq, max_pos, half,
-                                                     static_cast<float*>(cos_out), static_cast<float*>(sin_out));
+                                                     static_cast<float*>(cos_out), static_cast<float*>(sin_out)), ltx::note_launch();
   else
     rope_tables_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(bounds, n_axes, T, freqs, n_freq, max_pos, half,
                                                              static_cast<__nv_bfloat16*>(cos_out),
-                                                             static_cast<__nv_bfloat16*>(sin_out));
+                                                             static_cast<__nv_bfloat16*>(sin_out)), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
@@ -402,10 +428,10 @@ extern "C" int ltx_gelu_tanh(const void* x, void* y, int64_t n, int dtype, void*
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned g = grid_for(n / 8 + 8, 256);
   if (dtype == LTX_F32)
-    gelu_tanh_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), static_cast<float*>(y), n);
+    gelu_tanh_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), static_cast<float*>(y), n), ltx::note_launch();
   else
     gelu_tanh_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
-                                                       static_cast<__nv_bfloat16*>(y), n);
+                                                       static_cast<__nv_bfloat16*>(y), n), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
@@ -427,11 +453,11 @@ extern "C" int ltx_gate_residual(const void* x, int64_t ldx, const void* y, int6
   if (dtype == LTX_F32)
     gate_residual_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), ldx, static_cast<const float*>(y), ldy,
                                                   static_cast<float*>(out), ldo, rows, rows_per_batch, D,
-                                                  make_modvec<float>(gate, 1));
+                                                  make_modvec<float>(gate, 1)), ltx::note_launch();
   else
     gate_residual_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(y), ldy,
-        static_cast<__nv_bfloat16*>(out), ldo, rows, rows_per_batch, D, make_modvec<__nv_bfloat16>(gate, 1));
+        static_cast<__nv_bfloat16*>(out), ldo, rows, rows_per_batch, D, make_modvec<__nv_bfloat16>(gate, 1)), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
@@ -447,10 +473,10 @@ extern "C" int ltx_timestep_embedding(const float* t, int64_t n, float scale, in
   const unsigned blocks = unsigned((total + 255) / 256);
   const float lmp = logf(max_period);
   if (dtype == LTX_F32)
-    timestep_embedding_kernel<float><<<blocks, 256, 0, s>>>(t, n, scale, dim, lmp, static_cast<float*>(out));
+    timestep_embedding_kernel<float><<<blocks, 256, 0, s>>>(t, n, scale, dim, lmp, static_cast<float*>(out)), ltx::note_launch();
   else
     timestep_embedding_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(t, n, scale, dim, lmp,
-                                                                    static_cast<__nv_bfloat16*>(out));
+                                                                    static_cast<__nv_bfloat16*>(out)), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
@@ -471,11 +497,53 @@ extern "C" int ltx_cfg_euler(const void* vel, const void* latent, const float* t
   if (dtype == LTX_F32)
     cfg_euler_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(vel), static_cast<const float*>(latent),
                                                    timesteps, T, C, cfg_m1, sigma, dt, static_cast<float*>(denoised),
-                                                   static_cast<float*>(new_latent));
+                                                   static_cast<float*>(new_latent)), ltx::note_launch();
   else
     cfg_euler_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(vel), static_cast<const __nv_bfloat16*>(latent), timesteps, T, C, cfg_m1,
-        sigma, dt, static_cast<__nv_bfloat16*>(denoised), static_cast<__nv_bfloat16*>(new_latent));
+        sigma, dt, static_cast<__nv_bfloat16*>(denoised), static_cast<__nv_bfloat16*>(new_latent)), ltx::note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_guide(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
+                         float cfg_scale, float stg_scale, float modality_scale, void* out, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(cond && uncond && ptb && mod && out, "NULL argument");
+  LTX_REQUIRE(n > 0, "n must be positive");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = unsigned((n + 255) / 256);
+  if (dtype == LTX_F32)
+    guide_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(cond), static_cast<const float*>(uncond),
+                                               static_cast<const float*>(ptb), static_cast<const float*>(mod), n,
+                                               cfg_scale - 1.f, stg_scale, modality_scale - 1.f,
+                                               static_cast<float*>(out)), ltx::note_launch();
+  else
+    guide_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(cond), static_cast<const __nv_bfloat16*>(uncond),
+        static_cast<const __nv_bfloat16*>(ptb), static_cast<const __nv_bfloat16*>(mod), n, cfg_scale - 1.f,
+        stg_scale, modality_scale - 1.f, static_cast<__nv_bfloat16*>(out)), ltx::note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_euler(const void* sample, const void* denoised, int64_t n, float sigma, float sigma_next,
+                         void* out, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(sample && denoised && out, "NULL argument");
+  LTX_REQUIRE(n > 0, "n must be positive");
+  LTX_REQUIRE(sigma != 0.f, "sigma must be non-zero (Euler divides by it)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = unsigned((n + 255) / 256);
+  if (dtype == LTX_F32)
+    euler_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(sample), static_cast<const float*>(denoised),
+                                               n, sigma, sigma_next - sigma, static_cast<float*>(out)), ltx::note_launch();
+  else
+    euler_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(sample),
+                                                       static_cast<const __nv_bfloat16*>(denoised), n, sigma,
+                                                       sigma_next - sigma, static_cast<__nv_bfloat16*>(out)), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

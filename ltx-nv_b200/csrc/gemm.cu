@@ -303,7 +303,7 @@ void launch_skinny(const T* A, int64_t lda, const T* W, int64_t ldw, T* C, int64
       auto kern = gemm_skinny_kernel<T, MRC>;
       if (smem > 48 * 1024) LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
       kern<<<unsigned(blocks), 256, smem, s>>>(A + r0 * lda, lda, W, ldw, C + r0 * ldc, ldc, mm, int(N), int(K), e,
-                                               silu_in, r0);
+                                               silu_in, r0), ltx::note_launch();
     };
     switch (mr) {
       case 8: run(std::integral_constant<int, 8>{}); break;
@@ -331,7 +331,7 @@ void launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, 
     LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     attr_dev = dev;
   }
-  kern<<<unsigned(grid), 192, Cfg::SMEM, s>>>(ta, tb, static_cast<__nv_bfloat16*>(C), ldc, int(M), int(N), int(K), epi);
+  kern<<<unsigned(grid), 192, Cfg::SMEM, s>>>(ta, tb, static_cast<__nv_bfloat16*>(C), ldc, int(M), int(N), int(K), epi), ltx::note_launch();
 }
 
 
@@ -512,7 +512,7 @@ extern "C" int ltx_linear(const void* A, int64_t lda, const void* W, int64_t ldw
     } else {
       dim3 grid(unsigned((N + 63) / 64), unsigned((M + 63) / 64));
       gemm_simt_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(A), lda, static_cast<const float*>(W),
-                                                   ldw, static_cast<float*>(C), ldc, int(M), int(N), int(K), e);
+                                                   ldw, static_cast<float*>(C), ldc, int(M), int(N), int(K), e), ltx::note_launch();
     }
   } else {
     Epi<__nv_bfloat16> e = make_epi<__nv_bfloat16>(epi);
@@ -552,12 +552,12 @@ extern "C" int ltx_proj_out_cfg_euler(const void* x, int64_t ldx, const void* W,
     Epi<float> ef = make_epi<float>(&e);
     dim3 grid(unsigned((C + 63) / 64), unsigned((2 * T + 63) / 64));
     gemm_simt_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), ldx, static_cast<const float*>(W), K,
-                                                 static_cast<float*>(vel_out), C, int(2 * T), C, int(K), ef);
+                                                 static_cast<float*>(vel_out), C, int(2 * T), C, int(K), ef), ltx::note_launch();
     LTX_CUDA(cudaGetLastError());
     const int64_t n = T * C;
     cfg_euler_kernel<float><<<unsigned((n + 255) / 256), 256, 0, s>>>(
         static_cast<const float*>(vel_out), static_cast<const float*>(latent), timesteps, T, C, cfg_scale - 1.f,
-        sigma, sigma_next - sigma, static_cast<float*>(denoised), static_cast<float*>(new_latent));
+        sigma, sigma_next - sigma, static_cast<float*>(denoised), static_cast<float*>(new_latent)), ltx::note_launch();
   } else {
     LTX_UNSUPPORTED(C == 128, "the fused bf16 head supports 128 output channels");
     check_vec_ptr(x, "x");
@@ -580,7 +580,7 @@ extern "C" int ltx_proj_out_cfg_euler(const void* x, int64_t ldx, const void* W,
     head_cfg_euler_kernel<<<unsigned((T + kBM - 1) / kBM), 192, HeadCfg::SMEM, s>>>(
         ta, tb, int(T), int(K), static_cast<const __nv_bfloat16*>(bias), static_cast<const __nv_bfloat16*>(latent),
         timesteps, cfg_scale - 1.f, sigma, sigma_next - sigma, static_cast<__nv_bfloat16*>(vel_out),
-        static_cast<__nv_bfloat16*>(denoised), static_cast<__nv_bfloat16*>(new_latent));
+        static_cast<__nv_bfloat16*>(denoised), static_cast<__nv_bfloat16*>(new_latent)), ltx::note_launch();
   }
   LTX_CUDA(cudaGetLastError());
   LTX_API_END

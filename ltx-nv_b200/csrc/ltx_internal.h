@@ -28,6 +28,9 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, u
 // Number of SMs of the current device (cached per device).
 int num_sms();
 
+// Process-wide count of kernels this library has launched (ltx_launch_count).
+void note_launch();
+
 }  // namespace ltx
 
 #define LTX_API_BEGIN \

@@ -110,9 +110,9 @@ extern "C" int ltx_philox_randn(void* out, int64_t n, int dtype, uint64_t seed, 
   LTX_REQUIRE(offset % 4 == 0, "offset must be a multiple of 4 (torch advances it in 4s)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == LTX_F32)
-    philox_randn_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(out), n, seed, offset);
+    philox_randn_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(out), n, seed, offset), ltx::note_launch();
   else
-    philox_randn_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out), n, seed, offset);
+    philox_randn_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out), n, seed, offset), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
@@ -125,7 +125,7 @@ extern "C" int ltx_philox_raw(uint32_t* out, int64_t threads, int64_t rounds, ui
   LTX_REQUIRE(threads <= (int64_t(1) << 30), "threads out of range");
   const int64_t blocks = (threads + 255) / 256;
   philox_raw_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(out, threads, rounds, seed,
-                                                                                     offset);
+                                                                                     offset), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

@@ -1,0 +1,753 @@
+"""B200-native LTX-2.5 DiT denoising step (drop-in for lipaul/ltx-nv standalone/ltx_dit.py).
+
+Same public names and signatures as the reference module: DiTConfig, Modality,
+LTXModel(cfg).forward(video, audio, perturbations) -> (vx, ax), load_transformer,
+video_positions / audio_positions, (un)patchify_*, LatentState, create_noised_states,
+ltx2_scheduler_sigmas, GuiderParams, guide, euler_step, guided_denoise_step, run_dit,
+build_perturbation_config. The parameters of LTXModel have the reference's names,
+shapes and registration order, so its state dicts and checkpoints load unchanged.
+
+What runs underneath: every op of the forward is a libltxb200 sm_100a kernel called
+through _native (no cuBLAS, no cuDNN, no torch element-wise math on the path):
+  patchify  tcgen05 GEMM (+ keyframe add in the epilogue)
+  adaLN     weight-streaming GEMMs on one row per sample (timesteps are uniform over
+            tokens in every denoise step; a per-token path exists for general masks)
+  block     norm+modulate -> packed QKV(+gate) GEMM -> q/k RMSNorm+RoPE -> tcgen05
+            attention (gate fused) -> out GEMM with gate*out+residual epilogue;
+            the same for text cross-attention and A<->V attention; norm+modulate ->
+            FFN-in GEMM with GELU epilogue -> FFN-out GEMM with gated residual epilogue
+  head      LayerNorm+modulate -> proj_out GEMM; in cfg_denoise_step the proj_out
+            epilogue also applies X0 + CFG + Euler and writes the next latent.
+Activations are (B*T, D) row-major buffers in HBM; the residual stream is updated in
+place by the GEMM epilogues.
+
+Supported guidance in this build: CFG (cond/uncond). STG and modality-isolation passes
+(partial perturbation masks) and guidance rescale raise NotImplementedError.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+import time
+from dataclasses import dataclass, replace
+
+import torch
+
+import _native as nat
+from ltx_nn import AdaLayerNormSingle, Attention, FeedForward, RopeTables, rope_tables
+
+DEVICE = torch.device("cuda")
+
+# ---------------------------------------------------------------------------------------
+# Config (ltx_dit.py:28-82)
+# ---------------------------------------------------------------------------------------
+
+
+@dataclass(frozen=True)
+class DiTConfig:
+    num_layers: int = 48
+    video_heads: int = 32
+    video_head_dim: int = 128
+    video_in: int = 128
+    video_out: int = 128
+    video_cross_dim: int = 4096
+    audio_heads: int = 32
+    audio_head_dim: int = 64
+    audio_in: int = 128
+    audio_out: int = 128
+    audio_cross_dim: int = 2048
+    norm_eps: float = 1e-6
+    theta: float = 10000.0
+    video_max_pos: tuple = (20, 2048, 2048)
+    audio_max_pos: tuple = (20,)
+    timestep_scale_multiplier: int = 1000
+    av_ca_timestep_scale_multiplier: float = 1000.0
+    double_rope: bool = True
+    gated_attention: bool = True
+    cross_attention_adaln: bool = True
+    ff_bias: bool = False
+    audio_ff_bias: bool = True
+    use_keyframes: bool = True
+
+    @staticmethod
+    def from_checkpoint(transformer_path: str) -> "DiTConfig":
+        """Read the transformer config from a safetensors file's metadata (ltx_dit.py:54-73)."""
+        from safetensors import safe_open
+
+        with safe_open(transformer_path, framework="pt") as f:
+            meta = f.metadata() or {}
+        c = json.loads(meta["config"])["transformer"]
+        return DiTConfig(
+            num_layers=c["num_layers"], video_heads=c["num_attention_heads"],
+            video_head_dim=c["attention_head_dim"], video_in=c["in_channels"], video_out=c["out_channels"],
+            video_cross_dim=c["cross_attention_dim"], audio_heads=c["audio_num_attention_heads"],
+            audio_head_dim=c["audio_attention_head_dim"], audio_in=c.get("audio_in_channels", 128),
+            audio_out=c["audio_out_channels"], audio_cross_dim=c["audio_cross_attention_dim"],
+            norm_eps=c["norm_eps"], theta=c["positional_embedding_theta"],
+            video_max_pos=tuple(c["positional_embedding_max_pos"]),
+            audio_max_pos=tuple(c["audio_positional_embedding_max_pos"]),
+            timestep_scale_multiplier=c["timestep_scale_multiplier"],
+            av_ca_timestep_scale_multiplier=c["av_ca_timestep_scale_multiplier"],
+            double_rope=c.get("frequencies_precision", False) == "float64",
+            gated_attention=c.get("apply_gated_attention", False),
+            cross_attention_adaln=c.get("cross_attention_adaln", False),
+            ff_bias=c.get("ff_bias", True), audio_ff_bias=c.get("audio_ff_bias", True),
+            use_keyframes=c.get("use_keyframes_abs_pos_embedding", False),
+        )
+
+    @staticmethod
+    def video_only(num_layers: int, heads: int, head_dim: int, cross_dim: int) -> "DiTConfig":
+        """Video-only DiT (3, 5): text cross-attention without
+        cross-adaLN, and a minimal audio stream that is never run (its parameters exist
+        only so the state dict matches the reference's AV model)."""
+        return DiTConfig(num_layers=num_layers, video_heads=heads, video_head_dim=head_dim, video_cross_dim=cross_dim,
+                         audio_heads=2, audio_head_dim=32, audio_cross_dim=max(2 * heads, 64),
+                         cross_attention_adaln=False)
+
+    @property
+    def video_dim(self) -> int:
+        return self.video_heads * self.video_head_dim
+
+    @property
+    def audio_dim(self) -> int:
+        return self.audio_heads * self.audio_head_dim
+
+
+# ---------------------------------------------------------------------------------------
+# Per-modality inputs (ltx_dit.py:89-117)
+# ---------------------------------------------------------------------------------------
+
+
+@dataclass
+class Modality:
+    latent: torch.Tensor  # (B, T, 128) patchified
+    sigma: torch.Tensor  # (B,)
+    timesteps: torch.Tensor  # (B, T, 1) = denoise_mask * sigma
+    positions: torch.Tensor  # video (B,3,T,2) pixel-space bounds; audio (B,1,T,2) seconds
+    context: torch.Tensor  # (B, S, cross_dim) text encoding
+    keyframes_mask: torch.Tensor | None = None  # (B, T, 1)
+    enabled: bool = True
+
+
+@dataclass
+class _Stream:
+    """Prepared state of one stream for the block loop (the reference's TransformerArgs)."""
+
+    name: str
+    B: int
+    T: int
+    D: int
+    heads: int
+    head_dim: int
+    x: torch.Tensor  # (B*T, D) residual stream
+    tmod: torch.Tensor  # (N, n*D) timestep modulation, N = B (per sample) or B*T
+    tmod_ld_tok: int
+    emb: torch.Tensor  # (N, D) embedded timestep
+    prompt_mod: torch.Tensor | None  # (B, 2D)
+    context: torch.Tensor  # (B*S, C)
+    S: int
+    pe: RopeTables
+    cross_pe: RopeTables | None
+    cross_ss: torch.Tensor | None  # (N, 4D)
+    cross_gate: torch.Tensor | None  # (B, D)
+    enabled: bool
+
+    def mod(self, table: torch.Tensor, tmod: torch.Tensor, shift: int | None, scale: int | None,
+            n_total: int | None = None, ld_tok: int | None = None) -> nat.Modulation:
+        """Modulation from rows `shift` / `scale` of an adaLN table (n, D) and the
+        matching slices of a (N, n*D) timestep modulation."""
+        d = table.shape[-1]
+        ld_row = tmod.shape[-1]
+        per_tok = self.tmod_ld_tok if ld_tok is None else ld_tok
+        return nat.modulation(table, tmod,
+                              shift=(shift * d, shift * d) if shift is not None else None,
+                              scale=(scale * d, scale * d) if scale is not None else None,
+                              mod_ld_batch=ld_row * (self.T if per_tok else 1), mod_ld_tok=ld_row if per_tok else 0)
+
+
+# ---------------------------------------------------------------------------------------
+# Model (ltx_dit.py:209-378)
+# ---------------------------------------------------------------------------------------
+
+
+class Block(torch.nn.Module):
+    """BasicAVTransformerBlock parameters (ltx_dit.py:209-235)."""
+
+    def __init__(self, cfg: DiTConfig):
+        super().__init__()
+        v, a = cfg.video_dim, cfg.audio_dim
+        n_ca = 9 if cfg.cross_attention_adaln else 6
+        self.attn1 = Attention(v, None, cfg.video_heads, cfg.video_head_dim, cfg.norm_eps, cfg.gated_attention)
+        self.attn2 = Attention(v, cfg.video_cross_dim, cfg.video_heads, cfg.video_head_dim, cfg.norm_eps,
+                               cfg.gated_attention)
+        self.ff = FeedForward(v, v, bias=cfg.ff_bias)
+        self.scale_shift_table = torch.nn.Parameter(torch.empty(n_ca, v))
+        self.audio_attn1 = Attention(a, None, cfg.audio_heads, cfg.audio_head_dim, cfg.norm_eps, cfg.gated_attention)
+        self.audio_attn2 = Attention(a, cfg.audio_cross_dim, cfg.audio_heads, cfg.audio_head_dim, cfg.norm_eps,
+                                     cfg.gated_attention)
+        self.audio_ff = FeedForward(a, a, bias=cfg.audio_ff_bias)
+        self.audio_scale_shift_table = torch.nn.Parameter(torch.empty(n_ca, a))
+        self.audio_to_video_attn = Attention(v, a, cfg.audio_heads, cfg.audio_head_dim, cfg.norm_eps,
+                                             cfg.gated_attention)
+        self.video_to_audio_attn = Attention(a, v, cfg.audio_heads, cfg.audio_head_dim, cfg.norm_eps,
+                                             cfg.gated_attention)
+        self.scale_shift_table_a2v_ca_audio = torch.nn.Parameter(torch.empty(5, a))
+        self.scale_shift_table_a2v_ca_video = torch.nn.Parameter(torch.empty(5, v))
+        if cfg.cross_attention_adaln:
+            self.prompt_scale_shift_table = torch.nn.Parameter(torch.empty(2, v))
+            self.audio_prompt_scale_shift_table = torch.nn.Parameter(torch.empty(2, a))
+
+
+class LTXModel(torch.nn.Module):
+    """LTX-2.5 AV transformer (ltx_dit.py:325-378) executed by libltxb200 kernels."""
+
+    def __init__(self, cfg: DiTConfig):
+        super().__init__()
+        self.cfg = cfg
+        v, a = cfg.video_dim, cfg.audio_dim
+        n_adaln = 9 if cfg.cross_attention_adaln else 6
+        self.patchify_proj = torch.nn.Linear(cfg.video_in, v, bias=True)
+        self.keyframes_abs_pos_embedding = torch.nn.Parameter(torch.zeros(1, v)) if cfg.use_keyframes else None
+        self.adaln_single = AdaLayerNormSingle(v, n_adaln)
+        self.prompt_adaln_single = AdaLayerNormSingle(v, 2) if cfg.cross_attention_adaln else None
+        self.scale_shift_table = torch.nn.Parameter(torch.empty(2, v))
+        self.norm_out = torch.nn.LayerNorm(v, elementwise_affine=False, eps=cfg.norm_eps)
+        self.proj_out = torch.nn.Linear(v, cfg.video_out)
+        self.audio_patchify_proj = torch.nn.Linear(cfg.audio_in, a, bias=True)
+        self.audio_adaln_single = AdaLayerNormSingle(a, n_adaln)
+        self.audio_prompt_adaln_single = AdaLayerNormSingle(a, 2) if cfg.cross_attention_adaln else None
+        self.audio_scale_shift_table = torch.nn.Parameter(torch.empty(2, a))
+        self.audio_norm_out = torch.nn.LayerNorm(a, elementwise_affine=False, eps=cfg.norm_eps)
+        self.audio_proj_out = torch.nn.Linear(a, cfg.audio_out)
+        self.av_ca_video_scale_shift_adaln_single = AdaLayerNormSingle(v, 4)
+        self.av_ca_audio_scale_shift_adaln_single = AdaLayerNormSingle(a, 4)
+        self.av_ca_a2v_gate_adaln_single = AdaLayerNormSingle(v, 1)
+        self.av_ca_v2a_gate_adaln_single = AdaLayerNormSingle(a, 1)
+        self.blocks = torch.nn.ModuleList([Block(cfg) for _ in range(cfg.num_layers)])
+        self._rope_cache: dict = {}
+
+    # ------------------------------------------------------------------ preparation
+    def _rope(self, positions: torch.Tensor, dim: int, dtype: torch.dtype, max_pos: list, heads: int) -> RopeTables:
+        key = (positions.data_ptr(), positions._version, tuple(positions.shape), dim, dtype, tuple(max_pos), heads)
+        tabs = self._rope_cache.get(key)
+        if tabs is None:
+            if len(self._rope_cache) > 16:
+                self._rope_cache.clear()
+            tabs = rope_tables(positions, dim, dtype, self.cfg.theta, max_pos, heads, self.cfg.double_rope)
+            self._rope_cache[key] = tabs
+        return tabs
+
+    @staticmethod
+    def _per_sample_timesteps(ts: torch.Tensor) -> torch.Tensor | None:
+        """(B,) timesteps when every token of a sample shares its timestep, else None."""
+        first = ts[:, :1]
+        if bool((ts == first).all()):
+            return first.reshape(ts.shape[0]).to(torch.float32).contiguous()
+        return None
+
+    def _prepare(self, stream: str, m: Modality, cross: Modality | None, uniform_timesteps: bool = False) -> _Stream:
+        """ArgsPreprocessor.prepare (ltx_dit.py:131-184). `uniform_timesteps` asserts that
+        every token of a sample has the same timestep (a full denoise mask), which skips
+        the device-to-host check."""
+        cfg = self.cfg
+        a = stream == "audio"
+        patch = self.audio_patchify_proj if a else self.patchify_proj
+        adaln = self.audio_adaln_single if a else self.adaln_single
+        prompt_adaln = self.audio_prompt_adaln_single if a else self.prompt_adaln_single
+        dim = cfg.audio_dim if a else cfg.video_dim
+        heads = cfg.audio_heads if a else cfg.video_heads
+        hd = cfg.audio_head_dim if a else cfg.video_head_dim
+        dtype = patch.weight.dtype
+        b, t, cin = m.latent.shape
+        lat = m.latent.to(dtype).reshape(b * t, cin).contiguous()
+        x = torch.empty(b * t, dim, device=lat.device, dtype=dtype)
+        kf = self.keyframes_abs_pos_embedding
+        if not a and m.keyframes_mask is not None and kf is not None:
+            mask = m.keyframes_mask.reshape(b * t).to(torch.float32).contiguous()
+            nat.linear(lat, patch.weight, x, nat.epilogue(nat.EPI_ROW_MASK_ADD, bias=patch.bias, row_mask=mask,
+                                                          row_vec=kf.reshape(-1)))
+        else:
+            nat.linear(lat, patch.weight, x, nat.epilogue(bias=patch.bias))
+        scale = float(cfg.timestep_scale_multiplier)
+        ts = m.timesteps.reshape(b, t).to(torch.float32)
+        if uniform_timesteps:
+            t_sample = ts[:, 0].contiguous()
+        else:
+            t_sample = self._per_sample_timesteps(ts)
+        t_in = t_sample if t_sample is not None else ts.reshape(-1).contiguous()
+        tmod, emb = adaln(t_in, dtype, scale)
+        prompt = None
+        if prompt_adaln is not None:
+            prompt, _ = prompt_adaln(m.sigma.to(torch.float32).reshape(-1).contiguous(), dtype, scale)
+        s_len = m.context.shape[1]
+        context = m.context.to(dtype).reshape(b * s_len, -1).contiguous()
+        max_pos = list(cfg.audio_max_pos if a else cfg.video_max_pos)
+        pe = self._rope(m.positions, dim, dtype, max_pos, heads)
+        cross_pe = cross_ss = cross_gate = None
+        if cross is not None:
+            cross_pe = self._rope(m.positions[:, 0:1], cfg.audio_cross_dim, dtype,
+                                  [max(cfg.video_max_pos[0], cfg.audio_max_pos[0])], heads)
+            ss_mod = self.av_ca_audio_scale_shift_adaln_single if a else self.av_ca_video_scale_shift_adaln_single
+            g_mod = self.av_ca_v2a_gate_adaln_single if a else self.av_ca_a2v_gate_adaln_single
+            cross_ss, _ = ss_mod(t_in, dtype, scale)
+            factor = cfg.av_ca_timestep_scale_multiplier / cfg.timestep_scale_multiplier
+            cross_gate, _ = g_mod(cross.sigma.to(torch.float32).reshape(-1).contiguous(), dtype, scale * factor)
+        return _Stream(stream, b, t, dim, heads, hd, x, tmod, 0 if t_sample is not None else 1, emb, prompt,
+                       context, s_len, pe, cross_pe, cross_ss, cross_gate, m.enabled)
+
+    # ------------------------------------------------------------------ block pieces
+    def _self_and_text(self, blk: Block, st: _Stream, h: torch.Tensor):
+        """Self-attention + text cross-attention of one stream (ltx_dit.py:259-282)."""
+        cfg = self.cfg
+        a = st.name == "audio"
+        attn1 = blk.audio_attn1 if a else blk.attn1
+        attn2 = blk.audio_attn2 if a else blk.attn2
+        table = blk.audio_scale_shift_table if a else blk.scale_shift_table
+        d, eps, rows = st.D, cfg.norm_eps, st.B * st.T
+        inner = attn1.heads * attn1.dim_head
+        gated = cfg.gated_attention
+        # self-attention
+        nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_RMS, eps, st.mod(table, st.tmod, 0, 1))
+        qkv = attn1.project_qkv(h, st.T, st.pe)
+        o = attn1.attend(qkv[:, :inner], qkv[:, inner:2 * inner], qkv[:, 2 * inner:3 * inner],
+                         qkv[:, 3 * inner:] if gated else None, st.B, st.T, st.T)
+        nat.linear(o, attn1.to_out.weight, st.x,
+                   nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn1.to_out.bias, residual=st.x,
+                                gate=st.mod(table, st.tmod, None, 2), rows_per_batch=st.T))
+        # text cross-attention
+        if cfg.cross_attention_adaln:
+            nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_RMS, eps, st.mod(table, st.tmod, 6, 7))
+        else:
+            nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_RMS, eps, None)
+        wq, bq = attn2.packed_q()
+        qg = torch.empty(rows, wq.shape[0], device=h.device, dtype=h.dtype)
+        nat.linear(h, wq, qg, nat.epilogue(bias=bq))
+        attn2._norm_rope(qg[:, :inner], st.T, attn2.q_norm.weight, None)
+        ctx = st.context
+        if cfg.cross_attention_adaln:
+            psst = blk.audio_prompt_scale_shift_table if a else blk.prompt_scale_shift_table
+            if ctx.shape[1] != d:
+                raise ValueError("cross-adaLN needs the text context width to equal the hidden size")
+            enc = torch.empty_like(ctx)
+            nat.norm_modulate(ctx, enc, st.S, nat.LTX_NORM_NONE, eps,
+                              nat.modulation(psst, st.prompt_mod, shift=(0, 0), scale=(d, d),
+                                             mod_ld_batch=st.prompt_mod.shape[-1]))
+            ctx = enc
+        wkv, bkv = attn2.packed_kv()
+        kv = torch.empty(ctx.shape[0], wkv.shape[0], device=h.device, dtype=h.dtype)
+        nat.linear(ctx, wkv, kv, nat.epilogue(bias=bkv))
+        attn2._norm_rope(kv[:, :inner], st.S, attn2.k_norm.weight, None)
+        o = attn2.attend(qg[:, :inner], kv[:, :inner], kv[:, inner:2 * inner], qg[:, inner:] if gated else None,
+                         st.B, st.T, st.S)
+        gate = st.mod(table, st.tmod, None, 8) if cfg.cross_attention_adaln else None
+        nat.linear(o, attn2.to_out.weight, st.x,
+                   nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn2.to_out.bias, residual=st.x, gate=gate,
+                                rows_per_batch=st.T))
+
+    def _ffn(self, blk: Block, st: _Stream, h: torch.Tensor):
+        """Feed-forward with adaLN (ltx_dit.py:309-314)."""
+        a = st.name == "audio"
+        ff = blk.audio_ff if a else blk.ff
+        table = blk.audio_scale_shift_table if a else blk.scale_shift_table
+        nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_RMS, self.cfg.norm_eps, st.mod(table, st.tmod, 3, 4))
+        f = torch.empty(st.B * st.T, ff.proj_in.out_features, device=h.device, dtype=h.dtype)
+        nat.linear(h, ff.proj_in.weight, f, nat.epilogue(nat.EPI_GELU_TANH, bias=ff.proj_in.bias))
+        nat.linear(f, ff.proj_out.weight, st.x,
+                   nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=ff.proj_out.bias, residual=st.x,
+                                gate=st.mod(table, st.tmod, None, 5), rows_per_batch=st.T))
+
+    def _av_cross(self, blk: Block, vs: _Stream, as_: _Stream, run_a2v: bool, run_v2a: bool):
+        """Audio<->video cross-attention (ltx_dit.py:284-307); both read the pre-AV states."""
+        cfg = self.cfg
+        eps = cfg.norm_eps
+        tv, ta = blk.scale_shift_table_a2v_ca_video, blk.scale_shift_table_a2v_ca_audio
+
+        def normed(st, table, rows_sl):
+            out = torch.empty_like(st.x)
+            # get_av_ca_ada_values returns (scale, shift) = table rows (r0, r0 + 1)
+            r0 = rows_sl
+            nat.norm_modulate(st.x, out, st.T, nat.LTX_NORM_RMS, eps, st.mod(table, st.cross_ss, r0 + 1, r0))
+            return out
+
+        def gate_of(st, table):
+            d = table.shape[-1]
+            return nat.modulation(table, st.cross_gate, shift=None, scale=(4 * d, 0), mod_ld_batch=d)
+
+        a2v_v = normed(vs, tv, 0) if run_a2v else None
+        a2v_a = normed(as_, ta, 0) if run_a2v else None
+        v2a_a = normed(as_, ta, 2) if run_v2a else None
+        v2a_v = normed(vs, tv, 2) if run_v2a else None
+        if run_a2v:
+            self._cross_attend(blk.audio_to_video_attn, a2v_v, vs, a2v_a, as_, vs.cross_pe, as_.cross_pe,
+                               gate_of(vs, tv), vs)
+        if run_v2a:
+            self._cross_attend(blk.video_to_audio_attn, v2a_a, as_, v2a_v, vs, as_.cross_pe, vs.cross_pe,
+                               gate_of(as_, ta), as_)
+
+    def _cross_attend(self, attn: Attention, q_in, q_st: _Stream, kv_in, kv_st: _Stream, q_pe, k_pe, gate,
+                      out_st: _Stream):
+        inner = attn.heads * attn.dim_head
+        gated = self.cfg.gated_attention
+        wq, bq = attn.packed_q()
+        qg = torch.empty(q_in.shape[0], wq.shape[0], device=q_in.device, dtype=q_in.dtype)
+        nat.linear(q_in, wq, qg, nat.epilogue(bias=bq))
+        attn._norm_rope(qg[:, :inner], q_st.T, attn.q_norm.weight, q_pe)
+        wkv, bkv = attn.packed_kv()
+        kv = torch.empty(kv_in.shape[0], wkv.shape[0], device=q_in.device, dtype=q_in.dtype)
+        nat.linear(kv_in, wkv, kv, nat.epilogue(bias=bkv))
+        attn._norm_rope(kv[:, :inner], kv_st.T, attn.k_norm.weight, k_pe)
+        o = attn.attend(qg[:, :inner], kv[:, :inner], kv[:, inner:2 * inner], qg[:, inner:] if gated else None,
+                        q_st.B, q_st.T, kv_st.T)
+        nat.linear(o, attn.to_out.weight, out_st.x,
+                   nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn.to_out.bias, residual=out_st.x, gate=gate,
+                                rows_per_batch=out_st.T))
+
+    # ------------------------------------------------------------------ forward
+    def _keep_masks(self, perturbations, batch: int):
+        """Host copy of the (4, L, B) keep-mask (ltx_dit.py:381-411); None = all ones."""
+        if perturbations is None:
+            return None
+        keep = perturbations.detach().to("cpu", torch.float32)
+        if bool((keep[0:2] != 1).any()):
+            raise NotImplementedError("self-attention perturbation (STG) is not supported yet")
+        rows = keep[2:4]
+        mixed = (rows != 0).any(dim=-1) & (rows != 1).any(dim=-1)
+        if bool(mixed.any()):
+            raise NotImplementedError("partial A2V/V2A perturbation masks (modality guidance) are not supported yet")
+        return keep
+
+    def run_blocks(self, va: _Stream | None, aa: _Stream | None, perturbations=None):
+        keep = self._keep_masks(perturbations, (va or aa).B)
+        hv = torch.empty_like(va.x) if va is not None else None
+        ha = torch.empty_like(aa.x) if aa is not None else None
+        for i, blk in enumerate(self.blocks):
+            run_v = va is not None and va.enabled and va.x.numel() > 0
+            run_a = aa is not None and aa.enabled and aa.x.numel() > 0
+            run_a2v = run_v and aa is not None and aa.x.numel() > 0
+            run_v2a = run_a and va is not None and va.x.numel() > 0
+            if keep is not None:
+                run_a2v = run_a2v and bool((keep[2, i] != 0).any())
+                run_v2a = run_v2a and bool((keep[3, i] != 0).any())
+            if run_v:
+                self._self_and_text(blk, va, hv)
+            if run_a:
+                self._self_and_text(blk, aa, ha)
+            if run_a2v or run_v2a:
+                self._av_cross(blk, va, aa, run_a2v, run_v2a)
+            if run_v:
+                self._ffn(blk, va, hv)
+            if run_a:
+                self._ffn(blk, aa, ha)
+
+    def head_hidden(self, st: _Stream) -> torch.Tensor:
+        """LayerNorm + (1 + scale) / shift of the output head (ltx_dit.py:371-377)."""
+        a = st.name == "audio"
+        sst = self.audio_scale_shift_table if a else self.scale_shift_table
+        h = torch.empty_like(st.x)
+        d = st.D
+        per_tok = st.tmod_ld_tok
+        m = nat.modulation(sst, st.emb, shift=(0, 0), scale=(d, 0), mod_ld_batch=d * (st.T if per_tok else 1),
+                           mod_ld_tok=d if per_tok else 0)
+        nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_LAYER, self.cfg.norm_eps, m)
+        return h
+
+    def _output(self, st: _Stream) -> torch.Tensor:
+        proj = self.audio_proj_out if st.name == "audio" else self.proj_out
+        h = self.head_hidden(st)
+        out = torch.empty(st.B * st.T, proj.out_features, device=h.device, dtype=h.dtype)
+        nat.linear(h, proj.weight, out, nat.epilogue(bias=proj.bias))
+        return out.view(st.B, st.T, -1)
+
+    def prepare(self, video: Modality | None, audio: Modality | None, uniform_timesteps: bool = False):
+        va = self._prepare("video", video, audio, uniform_timesteps) if video is not None else None
+        aa = self._prepare("audio", audio, video, uniform_timesteps) if audio is not None else None
+        return va, aa
+
+    @torch.inference_mode()
+    def forward(self, video: Modality | None, audio: Modality | None, perturbations=None) -> tuple:
+        """(vx, ax) velocities (ltx_dit.py:354-369)."""
+        va, aa = self.prepare(video, audio)
+        self.run_blocks(va, aa, perturbations)
+        vx = self._output(va) if va is not None else None
+        ax = self._output(aa) if aa is not None else None
+        return vx, ax
+
+
+# ---------------------------------------------------------------------------------------
+# Perturbations / loading (ltx_dit.py:381-432)
+# ---------------------------------------------------------------------------------------
+
+
+def build_perturbation_config(num_blocks: int, passes: list[str], v_stg_blocks: list[int], a_stg_blocks: list[int],
+                              device: torch.device, dtype: torch.dtype) -> torch.Tensor:
+    """(4, num_blocks, B) keep-mask: 0 skip-video-self, 1 skip-audio-self, 2 skip-A2V, 3 skip-V2A."""
+    keep = torch.ones(4, num_blocks, len(passes), dtype=dtype)
+    for i, name in enumerate(passes):
+        if name == "ptb":
+            for blk in v_stg_blocks:
+                keep[0, blk, i] = 0
+            for blk in a_stg_blocks:
+                keep[1, blk, i] = 0
+        elif name == "mod":
+            keep[2, :, i] = 0
+            keep[3, :, i] = 0
+    return keep.to(device)
+
+
+def _rename(key: str) -> str | None:
+    if not key.startswith("model.diffusion_model."):
+        return None
+    k = key.removeprefix("model.diffusion_model.")
+    k = k.replace("transformer_blocks.", "blocks.")
+    k = k.replace("to_out.0.", "to_out.").replace("ff.net.0.proj.", "ff.proj_in.").replace("ff.net.2.", "ff.proj_out.")
+    k = k.replace("audio_ff.net.0.proj.", "audio_ff.proj_in.").replace("audio_ff.net.2.", "audio_ff.proj_out.")
+    return k
+
+
+def load_transformer(path: str, cfg: DiTConfig, device: torch.device = DEVICE,
+                     dtype: torch.dtype = torch.bfloat16) -> LTXModel:
+    """Build the model and load a dev-transformer safetensors checkpoint (ltx_dit.py:414-432)."""
+    from safetensors import safe_open
+
+    with torch.device("meta"):
+        model = LTXModel(cfg)
+    sd = {}
+    with safe_open(path, framework="pt", device=str(device)) as f:
+        for name in f.keys():  # noqa: SIM118
+            new = _rename(name)
+            if new is None:
+                continue
+            t = f.get_tensor(name)
+            sd[new] = t.to(dtype) if t.is_floating_point() else t
+    res = model.load_state_dict(sd, strict=False, assign=True)
+    missing = [k for k in res.missing_keys if k != "keyframes_abs_pos_embedding"]
+    if missing:
+        raise RuntimeError(f"transformer missing keys: {missing[:10]} ({len(missing)} total)")
+    if model.keyframes_abs_pos_embedding is not None and model.keyframes_abs_pos_embedding.is_meta:
+        model.keyframes_abs_pos_embedding = torch.nn.Parameter(torch.zeros(1, cfg.video_dim, device=device,
+                                                                           dtype=dtype))
+    return model.to(device).eval()
+
+
+# ---------------------------------------------------------------------------------------
+# Latent state (ltx_dit.py:439-520)
+# ---------------------------------------------------------------------------------------
+
+SCALE_T, SCALE_H, SCALE_W = 8, 32, 32
+
+
+def video_positions(batch: int, f: int, h: int, w: int, fps: float, device) -> torch.Tensor:
+    """(B, 3, T, 2) pixel-space [start, end) per token; time / fps with the causal fix."""
+    coords = torch.meshgrid(torch.arange(f, device=device), torch.arange(h, device=device),
+                            torch.arange(w, device=device), indexing="ij")
+    starts = torch.stack(coords, dim=0)
+    bounds = torch.stack([starts, starts + 1], dim=-1).reshape(3, -1, 2)
+    bounds = bounds.unsqueeze(0).expand(batch, -1, -1, -1).clone().float()
+    bounds = bounds * torch.tensor([SCALE_T, SCALE_H, SCALE_W], device=device).view(1, 3, 1, 1)
+    bounds[:, 0] = (bounds[:, 0] + 1 - SCALE_T).clamp(min=0)
+    bounds[:, 0] = bounds[:, 0] / fps
+    return bounds
+
+
+def audio_positions(batch: int, frames: int, device) -> torch.Tensor:
+    """(B, 1, T, 2) latent-frame [start, end) bounds in seconds."""
+    idx = torch.arange(frames, dtype=torch.float32, device=device)
+    start = ((idx * 4 + 1 - 4).clamp(min=0)) * 160 / 16000
+    end = (((idx + 1) * 4 + 1 - 4).clamp(min=0)) * 160 / 16000
+    return torch.stack([start, end], dim=-1)[None, None].expand(batch, 1, -1, -1).contiguous()
+
+
+def patchify_video(latent: torch.Tensor) -> torch.Tensor:
+    return latent.permute(0, 2, 3, 4, 1).reshape(latent.shape[0], -1, latent.shape[1])
+
+
+def unpatchify_video(tokens: torch.Tensor, f: int, h: int, w: int) -> torch.Tensor:
+    b, _, c = tokens.shape
+    return tokens.view(b, f, h, w, c).permute(0, 4, 1, 2, 3)
+
+
+def patchify_audio(latent: torch.Tensor) -> torch.Tensor:
+    return latent.permute(0, 2, 1, 3).reshape(latent.shape[0], latent.shape[2], -1)
+
+
+def unpatchify_audio(tokens: torch.Tensor, channels: int, mel_bins: int) -> torch.Tensor:
+    b, t, _ = tokens.shape
+    return tokens.view(b, t, channels, mel_bins).permute(0, 2, 1, 3)
+
+
+@dataclass
+class LatentState:
+    latent: torch.Tensor
+    denoise_mask: torch.Tensor
+    positions: torch.Tensor
+    clean_latent: torch.Tensor
+    keyframes_mask: torch.Tensor | None = None
+
+
+class PhiloxGenerator:
+    """torch.Generator(device='cuda').manual_seed(seed) equivalent for randn: the same
+    Philox stream, launch policy and offset bookkeeping, filled by libltxb200."""
+
+    def __init__(self, seed: int, device: torch.device | str = DEVICE):
+        self.seed = int(seed)
+        self.offset = 0
+        self.device = torch.device(device)
+
+    def randn(self, *shape: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        out = torch.empty(*shape, device=self.device, dtype=dtype)
+        n = out.numel()
+        if n == 0:
+            return out
+        grid = nat.philox_grid(n, self.device.index if self.device.index is not None else torch.cuda.current_device())
+        nat.philox_randn(out, self.seed, self.offset, grid)
+        self.offset += nat.philox_offset_increment(n, grid)
+        return out
+
+
+def create_noised_states(batch: int, num_video_frames: int, height: int, width: int, fps: float, seed: int,
+                         device: torch.device, dtype: torch.dtype) -> tuple[LatentState, LatentState]:
+    """Unconditioned t2v initial state (ltx_dit.py:495-520), noise from the Philox kernel."""
+    gen = PhiloxGenerator(seed, device)
+    f = (num_video_frames - 1) // SCALE_T + 1
+    h, w = height // SCALE_H, width // SCALE_W
+    v_tokens = f * h * w
+    video_noise = gen.randn(batch, v_tokens, 128, dtype=dtype)
+    keyframes_mask = torch.zeros(batch, v_tokens, 1, device=device, dtype=torch.float32)
+    keyframes_mask[:, : h * w] = 1.0
+    video_state = LatentState(latent=video_noise,
+                              denoise_mask=torch.ones(batch, v_tokens, 1, device=device, dtype=torch.float32),
+                              positions=video_positions(batch, f, h, w, fps, device),
+                              clean_latent=torch.zeros_like(video_noise), keyframes_mask=keyframes_mask)
+    audio_frames = round(num_video_frames / fps * 25.0)
+    audio_noise = gen.randn(batch, audio_frames, 128, dtype=dtype)
+    audio_state = LatentState(latent=audio_noise,
+                              denoise_mask=torch.ones(batch, audio_frames, 1, device=device, dtype=torch.float32),
+                              positions=audio_positions(batch, audio_frames, device),
+                              clean_latent=torch.zeros_like(audio_noise))
+    return video_state, audio_state
+
+
+# ---------------------------------------------------------------------------------------
+# Scheduler + guidance + sampling (ltx_dit.py:528-621)
+# ---------------------------------------------------------------------------------------
+
+
+def ltx2_scheduler_sigmas(steps: int, tokens: int = 4096, max_shift: float = 2.05, base_shift: float = 0.95,
+                          terminal: float = 0.1) -> torch.Tensor:
+    """Shifted flow-matching sigmas (host-side, 31 values)."""
+    sigmas = torch.linspace(1.0, 0.0, steps + 1)
+    mm = (max_shift - base_shift) / (4096 - 1024)
+    shift = tokens * mm + (base_shift - mm * 1024)
+    e = math.exp(shift)
+    sigmas = torch.where(sigmas != 0, e / (e + (1 / sigmas - 1)), sigmas)
+    nz = sigmas != 0
+    one_minus = 1.0 - sigmas[nz]
+    scale = one_minus[-1] / (1.0 - terminal)
+    sigmas[nz] = 1.0 - one_minus / scale
+    return sigmas.to(torch.float32)
+
+
+@dataclass(frozen=True)
+class GuiderParams:
+    cfg_scale: float
+    stg_scale: float
+    rescale_scale: float
+    modality_scale: float
+    stg_blocks: tuple[int, ...]
+
+    @property
+    def cfg_only(self) -> bool:
+        return self.stg_scale == 0 and self.modality_scale == 1 and self.rescale_scale == 0
+
+
+def _sigma_pair(sigmas: torch.Tensor, idx: int) -> tuple[float, float]:
+    s = sigmas.detach().to("cpu", torch.float32)
+    return float(s[idx]), float(s[idx + 1])
+
+
+@torch.inference_mode()
+def cfg_denoise_step(model: LTXModel, latent: torch.Tensor, positions: torch.Tensor, context_pos: torch.Tensor,
+                     context_neg: torch.Tensor, sigmas: torch.Tensor, idx: int, cfg_scale: float,
+                     keyframes_mask: torch.Tensor | None = None, fused_head: bool = True):
+    """One CFG denoise step of the video stream (B = 2 [cond, uncond] forward, X0,
+    guide, Euler; ltx_dit.py:565-606 with CFG-only guidance).
+
+    latent (1, T, C), positions (1, 3, T, 2), contexts (1, S, Cctx). Returns
+    (velocity (2, T, C), denoised (1, T, C), next latent (1, T, C)). The X0 + CFG + Euler
+    update runs in the proj_out GEMM epilogue (bf16) or right after it (fp32)."""
+    dtype = model.proj_out.weight.dtype
+    dev = latent.device
+    _, t, c = latent.shape
+    sigma, sigma_next = _sigma_pair(sigmas, idx)
+    sig = torch.full((2,), sigma, device=dev, dtype=torch.float32)
+    ts = torch.full((2, t, 1), sigma, device=dev, dtype=torch.float32)
+    lat = latent.to(dtype)
+    video = Modality(latent=lat.expand(2, -1, -1), sigma=sig, timesteps=ts, positions=positions.expand(2, -1, -1, -1),
+                     context=torch.cat([context_pos, context_neg], dim=0).to(dtype),
+                     keyframes_mask=keyframes_mask.expand(2, -1, -1) if keyframes_mask is not None else None)
+    va, _ = model.prepare(video, None, uniform_timesteps=True)
+    model.run_blocks(va, None)
+    h = model.head_hidden(va)
+    lat2 = lat.reshape(t, c).contiguous()
+    vel = torch.empty(2 * t, c, device=dev, dtype=dtype)
+    den = torch.empty(t, c, device=dev, dtype=dtype)
+    nxt = torch.empty(t, c, device=dev, dtype=dtype)
+    ts2 = ts.reshape(2, t)
+    if fused_head:
+        nat.proj_out_cfg_euler(h, model.proj_out.weight, model.proj_out.bias, lat2, ts2, cfg_scale, sigma, sigma_next,
+                               nxt, den, vel)
+    else:
+        nat.linear(h, model.proj_out.weight, vel, nat.epilogue(bias=model.proj_out.bias))
+        nat.cfg_euler(vel, lat2, ts2, cfg_scale, sigma, sigma_next, nxt, den)
+    return vel.view(2, t, c), den.view(1, t, c), nxt.view(1, t, c)
+
+
+def guide(cond, uncond, ptb, mod, p: GuiderParams) -> torch.Tensor:
+    """Guidance blend cond + (cfg-1)(cond-uncond) + stg(cond-ptb) + (mod-1)(cond-mod)
+    (ltx_dit.py:551-562) as one device kernel. Rescale (a global std) is not supported yet."""
+    if p.rescale_scale != 0:
+        raise NotImplementedError("guidance rescale is not supported yet")
+    out = torch.empty_like(cond)
+    nat.guide(cond.contiguous(), uncond.contiguous(), ptb.contiguous(), mod.contiguous(), p.cfg_scale, p.stg_scale,
+              p.modality_scale, out)
+    return out
+
+
+def euler_step(sample: torch.Tensor, denoised: torch.Tensor, sigmas: torch.Tensor, idx: int) -> torch.Tensor:
+    """Flow-matching Euler update (ltx_dit.py:602-606) as one device kernel."""
+    sigma, sigma_next = _sigma_pair(sigmas, idx)
+    out = torch.empty_like(sample)
+    nat.euler(sample.contiguous(), denoised.contiguous(), sigma, sigma_next, out)
+    return out
+
+
+def guided_denoise_step(model: LTXModel, video_state: LatentState, audio_state: LatentState | None, contexts: dict,
+                        sigma: torch.Tensor, step_idx: int, v_params: GuiderParams, a_params: GuiderParams | None,
+                        cfg: DiTConfig):
+    raise NotImplementedError("the 4-pass (cond/uncond/STG/modality) guidance batch is not supported yet; "
+                              "run_dit with CFG-only GuiderParams uses cfg_denoise_step")
+
+
+@torch.inference_mode()
+def run_dit(model: LTXModel, cfg: DiTConfig, contexts: dict, video_state: LatentState,
+            audio_state: LatentState | None, sigmas: torch.Tensor, v_params: GuiderParams,
+            a_params: GuiderParams | None, on_step=None) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Denoising loop (ltx_dit.py:609-621). Video-only CFG guidance in this build."""
+    if audio_state is not None or not v_params.cfg_only:
+        raise NotImplementedError("this build runs video-only CFG guidance (audio / STG / modality / rescale: next)")
+    latent = video_state.latent
+    if latent.shape[0] != 1:
+        raise ValueError("run_dit denoises one latent (batch 1); CFG makes the model batch 2")
+    for idx in range(len(sigmas) - 1):
+        t0 = time.perf_counter()
+        vel, den, nxt = cfg_denoise_step(model, latent, video_state.positions[:1], contexts["v_pos"],
+                                         contexts["v_neg"], sigmas, idx, v_params.cfg_scale,
+                                         keyframes_mask=video_state.keyframes_mask[:1]
+                                         if video_state.keyframes_mask is not None else None)
+        latent = nxt
+        video_state = replace(video_state, latent=latent)
+        if on_step:
+            on_step(idx, time.perf_counter() - t0, den, None, {"cond": (vel[0:1], None), "uncond": (vel[1:2], None)},
+                    video_state, audio_state)
+    return video_state.latent, None

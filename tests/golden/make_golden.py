@@ -55,11 +55,12 @@ def rng_normal(shape, seed, scale=1.0, dtype=torch.float32):
 
 CASES = {
     # video-only benchmark geometry in miniature: context width != hidden, no cross-adaLN
-    "tiny_video": dict(num_layers=2, video_heads=4, video_head_dim=16, video_cross_dim=96, audio_heads=2,
-                       audio_head_dim=16, audio_cross_dim=32, cross_attention_adaln=False),
+    # (the audio dims are those of DiTConfig.video_only: a stream that never runs)
+    "tiny_video": dict(num_layers=2, video_heads=4, video_head_dim=64, video_cross_dim=384, audio_heads=2,
+                       audio_head_dim=32, audio_cross_dim=64, cross_attention_adaln=False),
     # the real LTX-2.5 AV structure (cross-adaLN, A<->V attention) in miniature
-    "tiny_av": dict(num_layers=2, video_heads=4, video_head_dim=16, video_cross_dim=64, audio_heads=2,
-                    audio_head_dim=16, audio_cross_dim=32, cross_attention_adaln=True),
+    "tiny_av": dict(num_layers=2, video_heads=4, video_head_dim=64, video_cross_dim=256, audio_heads=2,
+                    audio_head_dim=64, audio_cross_dim=128, cross_attention_adaln=True),
 }
 FRAMES = (2, 3, 4)  # latent f, h, w -> 24 video tokens
 AUDIO_T = 5

@@ -1,0 +1,86 @@
+"""Host-side checks that need no GPU: the C ABI exports what include/ltxb200.h declares,
+the drop-in module's parameter layout equals the reference's, and the host helpers
+(schedule, positions, perturbation masks, Philox bookkeeping) agree with the oracle."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import _native as nat
+import golden_cases as gc
+import ltx_dit
+from oracle import ltx_oracle, philox_oracle
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def header_functions() -> list[str]:
+    text = (ROOT / "include" / "ltxb200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ltx_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(nat.LIB_PATH))
+    names = header_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the Python binding covers the whole header
+    assert set(names) <= set(nat._SIGNATURES), set(names) - set(nat._SIGNATURES)
+
+
+def test_library_status_codes_without_a_gpu():
+    lib = nat.load_library()
+    assert lib.ltx_abi_version() == 1
+    # argument validation happens before any CUDA call
+    st = lib.ltx_philox_randn(None, 16, 0, 1, 0, 1, None)
+    assert st == 1 and b"out is NULL" in lib.ltx_last_error()
+    st = lib.ltx_linear(None, 8, None, 8, None, 8, 8, 8, 8, None, 1, None)
+    assert st == 1
+    assert lib.ltx_philox_offset_increment(442368, 852) == 4
+    assert lib.ltx_philox_offset_increment(1572864, 1184) == 8
+    assert lib.ltx_philox_offset_increment(1572864, 1184) == philox_oracle.offset_increment(1572864, 1184)
+
+
+def test_native_wrappers_refuse_cpu_tensors():
+    with pytest.raises(ValueError):
+        nat.gelu_tanh(torch.zeros(8), torch.zeros(8))
+
+
+@pytest.mark.parametrize("case", ["tiny_video_float32", "tiny_av_float32"])
+def test_parameter_layout_matches_reference(case):
+    rec = gc.load(case)
+    cfg = ltx_dit.DiTConfig(**{k: (tuple(v) if isinstance(v, list) else v) for k, v in rec["config"].items()})
+    with torch.device("meta"):
+        model = ltx_dit.LTXModel(cfg)
+    mine = [(n, tuple(p.shape)) for n, p in model.named_parameters()]
+    ref = [(n, tuple(s)) for n, s in rec["param_shapes"]]
+    assert mine == ref
+
+
+def test_video_only_config_matches_golden_geometry():
+    rec = gc.load("tiny_video_float32")
+    cfg = ltx_dit.DiTConfig.video_only(num_layers=2, heads=4, head_dim=64, cross_dim=384)
+    for k, v in rec["config"].items():
+        mine = getattr(cfg, k)
+        assert (tuple(mine) if isinstance(mine, tuple) else mine) == (tuple(v) if isinstance(v, list) else v), k
+
+
+def test_schedule_positions_and_perturbations_match_oracle():
+    assert torch.equal(ltx_dit.ltx2_scheduler_sigmas(30), ltx_oracle.scheduler_sigmas(30))
+    assert torch.equal(ltx_dit.video_positions(2, 3, 4, 5, 24.0, "cpu"), ltx_oracle.video_positions(2, 3, 4, 5, 24.0))
+    assert torch.equal(ltx_dit.audio_positions(2, 9, "cpu"), ltx_oracle.audio_positions(2, 9))
+    keep = ltx_dit.build_perturbation_config(4, ["cond", "uncond", "ptb", "mod"], [2], [1], "cpu", torch.float32)
+    assert keep.shape == (4, 4, 4)
+    assert keep[0, 2, 2] == 0 and keep[1, 1, 2] == 0 and keep[2:, :, 3].eq(0).all() and keep[:, :, :2].eq(1).all()
+
+
+def test_unsupported_guidance_is_rejected_loudly():
+    p = ltx_dit.GuiderParams(cfg_scale=3.0, stg_scale=1.0, rescale_scale=0.7, modality_scale=3.0, stg_blocks=(28,))
+    assert not p.cfg_only
+    with pytest.raises(NotImplementedError):
+        ltx_dit.run_dit(None, None, {}, None, object(), torch.zeros(2), p, p)

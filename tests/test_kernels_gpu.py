@@ -303,7 +303,7 @@ def test_attention_bf16_tcgen05(b, tq, tk, h, d):
     q = qkv[: b * tq, : h * d]
     k = qkv[: b * tk, h * d:2 * h * d]
     v = qkv[: b * tk, 2 * h * d:3 * h * d]
-    gate = qkv[: b * tq, 3 * h * d:]
+    gate = qkv[: b * tq, 3 * h * d:3 * h * d + h]
     o = torch.empty(b * tq, h * d, device=DEV, dtype=torch.bfloat16)
     nat.attention(q, k, v, o, b, tq, tk, h, d, d ** -0.5, gate)
     torch.cuda.synchronize()
