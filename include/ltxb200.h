@@ -204,6 +204,19 @@ int ltx_proj_out_cfg_euler(const void* x, int64_t ldx, const void* W, const void
                            float sigma_next, void* vel_out, void* denoised, void* new_latent, int dtype,
                            void* stream);
 
+/* ---------------------------------------------------------------------------------- */
+/* Sequence-parallel (Ulysses) exchange layouts around NCCL all-to-all. No counterpart */
+/* in the reference, which runs the whole sequence on one GPU (full-sequence sdpa,     */
+/* ltx_nn.py:227).                                                                     */
+/* ---------------------------------------------------------------------------------- */
+/* dst[j][r][:] = concat over segments s of src[r][off_s + j*w_s, off_s + (j+1)*w_s),
+ * for j < parts, r < rows (1..4 segments, 16-byte aligned widths and offsets). */
+int ltx_sp_pack(const void* src, int64_t ld_src, int64_t rows, int parts, int n_seg, const int* seg_off,
+                const int* seg_w, void* dst, int dtype, void* stream);
+/* dst[r][j*w, (j+1)*w) = src[j][r][:] for j < parts, r < rows. */
+int ltx_sp_unpack(const void* src, int64_t rows, int parts, int w, void* dst, int64_t ld_dst, int dtype,
+                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

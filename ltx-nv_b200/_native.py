@@ -95,6 +95,9 @@ _SIGNATURES = {
                                      ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, ctypes.c_int, c_vp]),
     "ltx_cfg_euler": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_float,
                                      ctypes.c_float, c_vp, c_vp, ctypes.c_int, c_vp]),
+    "ltx_sp_pack": (ctypes.c_int, [c_vp, c_i64, c_i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                   ctypes.POINTER(ctypes.c_int), c_vp, ctypes.c_int, c_vp]),
+    "ltx_sp_unpack": (ctypes.c_int, [c_vp, c_i64, ctypes.c_int, ctypes.c_int, c_vp, c_i64, ctypes.c_int, c_vp]),
     "ltx_guide": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp,
                                  ctypes.c_int, c_vp]),
     "ltx_euler": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
@@ -333,7 +336,8 @@ def linear(a: torch.Tensor, w: torch.Tensor, c: torch.Tensor, epi: Epilogue | No
     if w.shape[1] != k or c.shape[0] != m or c.shape[1] != n:
         raise ValueError(f"shape mismatch a{tuple(a.shape)} w{tuple(w.shape)} c{tuple(c.shape)}")
     _call("ltx_linear", _ptr(a), _ld(a), _ptr(w), _ld(w), _ptr(c), _ld(c), m, n, k,
-          ctypes.byref(epi) if epi is not None else None, _dt(a), _stream(a))
+          ctypes.byref(epi) if epi is not None else None, _dt(a), _stream(a),
+          label=f"linear M={m} N={n} K={k}" if _profile is not None else None)
 
 
 def gemm_set_tile_n(bn: int) -> None:
@@ -344,7 +348,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor
               heads: int, head_dim: int, scale: float, gate_logits: torch.Tensor | None = None) -> None:
     """q (B*Tq, >=H*d), k/v (B*Tk, >=H*d), o (B*Tq, >=H*d) row-major views; gate (B*Tq, >=H)."""
     _call("ltx_attention", _ptr(q), _ld(q), _ptr(k), _ld(k), _ptr(v), _ld(v), _ptr(o), _ld(o), batch, tq, tk, heads,
-          head_dim, scale, _ptr(gate_logits), _ld(gate_logits) if gate_logits is not None else 0, _dt(q), _stream(q))
+          head_dim, scale, _ptr(gate_logits), _ld(gate_logits) if gate_logits is not None else 0, _dt(q), _stream(q),
+          label=f"attention B={batch} H={heads} Tq={tq} Tk={tk} d={head_dim}" if _profile is not None else None)
 
 
 def cfg_euler(vel: torch.Tensor, latent: torch.Tensor, timesteps: torch.Tensor, cfg_scale: float, sigma: float,
@@ -352,6 +357,20 @@ def cfg_euler(vel: torch.Tensor, latent: torch.Tensor, timesteps: torch.Tensor, 
     t, c = latent.shape[-2], latent.shape[-1]
     _call("ltx_cfg_euler", _ptr(vel), _ptr(latent), _ptr(timesteps), t, c, cfg_scale, sigma, sigma_next,
           _ptr(denoised), _ptr(new_latent), _dt(latent), _stream(latent))
+
+
+def sp_pack(src: torch.Tensor, parts: int, segments: list[tuple[int, int]], dst: torch.Tensor) -> None:
+    """dst (parts, rows, W) <- per-destination column segments (offset, width) of src (rows, ld)."""
+    n = len(segments)
+    off = (ctypes.c_int * n)(*[s[0] for s in segments])
+    wid = (ctypes.c_int * n)(*[s[1] for s in segments])
+    _call("ltx_sp_pack", _ptr(src), _ld(src), src.shape[0], parts, n, off, wid, _ptr(dst), _dt(src), _stream(src))
+
+
+def sp_unpack(src: torch.Tensor, parts: int, dst: torch.Tensor) -> None:
+    """dst (rows, parts*w) <- src (parts, rows, w)."""
+    p, rows, w = src.shape
+    _call("ltx_sp_unpack", _ptr(src), rows, parts, w, _ptr(dst), _ld(dst), _dt(src), _stream(src))
 
 
 def guide(cond: torch.Tensor, uncond: torch.Tensor, ptb: torch.Tensor, mod: torch.Tensor, cfg_scale: float,

@@ -1,17 +1,23 @@
 // Attention core softmax(Q K^T * scale) V with the per-(token, head) output gate
 // 2*sigmoid(logit) fused in (ltx_nn.py:22-26 sdpa, 227-235 gating).
 //
-// bf16 path, one CTA per (128 queries, head, sample), 6 warps:
-//   warps 0-3  softmax / correction / epilogue, one query row per thread (TMEM lane)
-//   warp 4     TMA producer: Q once, then K and V tiles of 128 keys into a ring
-//   warp 5     tcgen05.mma issuer (and TMEM owner)
-// TMEM (512 columns): S/P buffers 0,1 at [0,128) and [128,256): S = Q K^T lands there
-// as fp32, the softmax overwrites it in place with P as packed bf16 (P chunk c goes to
-// columns [16c, 16c+16), all of which it has already read). O_part buffers 0,1 at
-// [256, 256+D) and [256+D, 256+2D) receive P V (A operand read from TMEM, V as an
-// MN-major 128B-swizzled smem operand). The softmax threads keep the running output
-// in registers: O = (O + O_part[j-1]) * exp2(m[j-1] - m[j]) while P V of tile j runs.
-// Keys at or beyond Tk are masked to -inf, query rows at or beyond Tq are not stored.
+// bf16 path: one CTA per (256 queries, head, sample) = two 128-row Q tiles, 10 warps:
+//   warps 0-3   softmax of Q tile 0 (one query row per thread = TMEM lane)
+//   warps 4-7   softmax of Q tile 1
+//   warp 8      TMA producer: both Q tiles once, then K and V tiles of 128 keys into a
+//               STAGES-deep ring
+//   warp 9      tcgen05.mma issuer and TMEM owner
+// TMEM (512 columns): S_i at [128 i, 128 i + 128) receives S = Q_i K^T in fp32; the softmax
+// of tile i reads it once and writes P as packed bf16 over its first 64 columns; O_i at
+// [256 + D i, 256 + D (i+1)) accumulates P V across all key tiles (A operand read from
+// TMEM, V as an MN-major 128B-swizzled smem operand).
+// MMA issue order per key tile j: P_0 V_j, S_0 <- Q_0 K_{j+1}^T, P_1 V_j, S_1 <- Q_1 K_{j+1}^T,
+// so the softmax of one tile overlaps the MMAs of the other.
+// Lazy rescaling: each row keeps a reference max m_ref and only moves it (rescaling its
+// O row and l) when the tile max exceeds it by more than 8 (log2 units); P = 2^(s - m_ref)
+// then stays <= 256, and O / l is unchanged by the choice of reference.
+// Keys at or beyond Tk are masked to -inf (last tile only); rows at or beyond Tq are not
+// stored.
 //
 // fp32 path: CUDA-core online-softmax kernel, one query per thread (accuracy mode).
 #include "ltx_kernels.cuh"
@@ -21,14 +27,15 @@ namespace detail {
 
 template <int D>
 struct FaCfg {
-  static constexpr int BM = 128;
-  static constexpr int BN = 128;
+  static constexpr int BM = 128;                    // rows per Q tile
+  static constexpr int BN = 128;                    // keys per K/V tile
   static constexpr int SUB = D / 64;                // 64-column (128-byte) sub-tiles per row
-  static constexpr int TILE_BYTES = 128 * D * 2;    // Q, K or V tile
+  static constexpr int TILE_BYTES = 128 * D * 2;    // one Q, K or V tile
   static constexpr int STAGES = D == 64 ? 3 : 2;
-  static constexpr int SMEM = TILE_BYTES * (1 + 2 * STAGES) + 512 + 1024;
+  static constexpr int SMEM = TILE_BYTES * (2 + 2 * STAGES) + 512 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t O_COL = 256;
+  static constexpr float RESCALE_THRESHOLD = 8.f;
 };
 
 LTX_DEVICE uint8_t* fa_align1024(uint8_t* p) {
@@ -36,30 +43,30 @@ LTX_DEVICE uint8_t* fa_align1024(uint8_t* p) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+// 10 warps: three share one SM sub-partition's 16K registers, so <= 168 per thread.
+__global__ void __launch_bounds__(320, 1)
     fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
                    int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate) {
   using Cfg = FaCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = fa_align1024(smem_raw);
-  uint8_t* sQ = smem;
-  uint8_t* sKV = smem + Cfg::TILE_BYTES;  // stage s: K at sKV + 2s*TILE, V at +TILE
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::TILE_BYTES * (1 + 2 * Cfg::STAGES));
+  uint8_t* sQ = smem;                          // Q tile i at sQ + i * TILE
+  uint8_t* sKV = smem + 2 * Cfg::TILE_BYTES;  // stage s: K at sKV + 2s*TILE, V at +TILE
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::TILE_BYTES * (2 + 2 * Cfg::STAGES));
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;                      // [STAGES]
-  uint64_t* v_full = k_full + Cfg::STAGES;          // [STAGES]
-  uint64_t* kv_empty = v_full + Cfg::STAGES;        // [STAGES]
-  uint64_t* s_full = kv_empty + Cfg::STAGES;        // [2]
-  uint64_t* p_full = s_full + 2;                    // [2]
-  uint64_t* o_full = p_full + 2;                    // [2]
-  uint64_t* o_empty = o_full + 2;                   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
+  uint64_t* k_full = bars + 1;               // [STAGES]
+  uint64_t* v_full = k_full + Cfg::STAGES;   // [STAGES]
+  uint64_t* kv_empty = v_full + Cfg::STAGES; // [STAGES]
+  uint64_t* s_full = kv_empty + Cfg::STAGES; // [2] per Q tile
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* o_done = p_full + 2;             // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
   const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * Cfg::BM;
+  const int q0 = blockIdx.x * 2 * Cfg::BM;
   const int n_kv = (Tk + Cfg::BN - 1) / Cfg::BN;
 
   if (threadIdx.x == 0) {
@@ -72,13 +79,12 @@ __global__ void __launch_bounds__(192, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
+      mbar_init(&o_done[i], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tmem_relinquish();
   }
@@ -87,17 +93,20 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       const int col0 = h * D;
-      mbar_arrive_expect_tx(q_full, Cfg::TILE_BYTES);
+      mbar_arrive_expect_tx(q_full, 2 * Cfg::TILE_BYTES);
 #pragma unroll
-      for (int j = 0; j < Cfg::SUB; ++j)
-        tma_load_2d(sQ + j * (Cfg::TILE_BYTES / Cfg::SUB), &tmQ, q_full, col0 + 64 * j, b * Tq + q0);
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < Cfg::SUB; ++j)
+          tma_load_2d(sQ + i * Cfg::TILE_BYTES + j * (Cfg::TILE_BYTES / Cfg::SUB), &tmQ, q_full, col0 + 64 * j,
+                      b * Tq + q0 + i * Cfg::BM);
       for (int t = 0; t < n_kv; ++t) {
         const int s = t % Cfg::STAGES;
         const uint32_t r = uint32_t(t / Cfg::STAGES);
@@ -115,172 +124,180 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_2d(sv + j * (Cfg::TILE_BYTES / Cfg::SUB), &tmV, &v_full[s], col0 + 64 * j, row);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------ MMA issuer ---------------------------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, 0);
       constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 1);
       const uint32_t q_addr = smem_u32(sQ);
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      // S[t%2] = Q K_t^T
-      auto issue_qk = [&](int t) -> bool {
+      auto issue_qk = [&](int i, int t) {
         const int s = t % Cfg::STAGES;
-        const uint32_t r = uint32_t(t / Cfg::STAGES);
-        if (!mbar_wait(&k_full[s], r & 1, abort_flag)) return false;
-        tc_fence_after();
         const uint32_t k_addr = smem_u32(sKV + (2 * s) * Cfg::TILE_BYTES);
-        const uint32_t d_tmem = tmem + uint32_t((t & 1) * 128);
+        const uint32_t qa = q_addr + uint32_t(i * Cfg::TILE_BYTES);
+        const uint32_t d_tmem = tmem + uint32_t(i * 128);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int j = kk >> 2, k4 = kk & 3;
           const uint32_t off = uint32_t(j * (Cfg::TILE_BYTES / Cfg::SUB) + k4 * 32);
-          umma_ss(d_tmem, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024), idesc_s,
+          umma_ss(d_tmem, umma_desc_sw128(qa + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024), idesc_s,
                   kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[t & 1]);
-        return true;
+        umma_commit(&s_full[i]);
       };
-      if (ok) ok = issue_qk(0);
-      if (ok && n_kv > 1) ok = issue_qk(1);
-      for (int t = 0; ok && t < n_kv; ++t) {
-        const int buf = t & 1;
-        const uint32_t u = uint32_t(t >> 1);
+      auto issue_pv = [&](int i, int t) {
         const int s = t % Cfg::STAGES;
-        const uint32_t r = uint32_t(t / Cfg::STAGES);
-        if (!mbar_wait(&p_full[buf], u & 1, abort_flag)) break;
-        if (!mbar_wait(&o_empty[buf], (u & 1) ^ 1, abort_flag)) break;
-        if (!mbar_wait(&v_full[s], r & 1, abort_flag)) break;
-        tc_fence_after();
         const uint32_t v_addr = smem_u32(sKV + (2 * s + 1) * Cfg::TILE_BYTES);
-        const uint32_t p_tmem = tmem + uint32_t(buf * 128);
-        const uint32_t o_tmem = tmem + Cfg::O_COL + uint32_t(buf * D);
+        const uint32_t p_tmem = tmem + uint32_t(i * 128);
+        const uint32_t o_tmem = tmem + Cfg::O_COL + uint32_t(i * D);
 #pragma unroll
         for (int kk = 0; kk < Cfg::BN / 16; ++kk) {
           // 16 keys per step: P columns [8kk, 8kk+8) (two bf16 per column), V rows
           // [16kk, 16kk+16) = two 8-row swizzle atoms of 1024 bytes.
           const uint64_t vd = umma_desc_sw128(v_addr + uint32_t(kk * 2048), Cfg::TILE_BYTES / Cfg::SUB, 1024);
-          umma_ts(o_tmem, p_tmem + uint32_t(kk * 8), vd, idesc_o, kk > 0 ? 1u : 0u);
+          umma_ts(o_tmem, p_tmem + uint32_t(kk * 8), vd, idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&o_full[buf]);
+        umma_commit(&o_done[i]);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        issue_qk(1, 0);
+      }
+      for (int t = 0; ok && t < n_kv; ++t) {
+        const int s = t % Cfg::STAGES;
+        const uint32_t r = uint32_t(t / Cfg::STAGES);
+        const bool more = t + 1 < n_kv;
+        const int s1 = (t + 1) % Cfg::STAGES;
+        const uint32_t r1 = uint32_t((t + 1) / Cfg::STAGES);
+        if (!mbar_wait(&v_full[s], r & 1, abort_flag)) break;
+        for (int i = 0; i < 2; ++i) {
+          if (!mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(i, t);
+          if (more) {
+            // S_i is rewritten by Q_i K_{t+1}^T after P_i V_t, issued in this order on
+            // this thread (tcgen05.mma of one CTA execute in issue order).
+            if (!mbar_wait(&k_full[s1], r1 & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_qk(i, t + 1);
+          }
+        }
         umma_commit(&kv_empty[s]);
-        if (t + 2 < n_kv) {
-          // S/P buffer `buf` is reused by Q K_{t+2}^T: wait until P V_t has read it.
-          if (!mbar_wait(&o_full[buf], u & 1, abort_flag)) break;
-          ok = issue_qk(t + 2);
-        }
       }
     }
   } else {
     // --------------------- softmax / correction / epilogue ---------------------
-    const int row = warp * 32 + lane;  // query row within the tile == TMEM lane
-    const uint32_t lane_off = uint32_t(warp * 32) << 16;
-    float o_acc[D];
-#pragma unroll
-    for (int c = 0; c < D; ++c) o_acc[c] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
+    const int qt = warp >> 2;                  // Q tile of this warpgroup
+    const int row = (warp & 3) * 32 + lane;    // row within the tile == TMEM lane
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+    const uint32_t s_tmem = tmem + uint32_t(qt * 128) + lane_off;
+    const uint32_t o_tmem = tmem + Cfg::O_COL + uint32_t(qt * D) + lane_off;
+    float m_ref = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int t = 0; t < n_kv; ++t) {
-      const int buf = t & 1;
-      const uint32_t u = uint32_t(t >> 1);
-      if (!mbar_wait(&s_full[buf], u & 1, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t s_tmem = tmem + uint32_t(buf * 128) + lane_off;
-      const int key0 = t * Cfg::BN;
-      const int valid = Tk - key0;  // keys in this tile that exist (may exceed 128)
-      // pass 1: row max
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
-        uint32_t rr[32];
-        tmem_ld32(s_tmem + uint32_t(c0), rr);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (c0 + e < valid) mx = fmaxf(mx, __uint_as_float(rr[e]));
+      if (!mbar_wait(&s_full[qt], uint32_t(t) & 1, abort_flag)) {
+        ok = false;
+        break;
       }
-      const float m_new = fmaxf(m_run, mx * scale_log2);
-      // pass 2: P = exp2(S*scale_log2 - m_new), packed to bf16 in place
+      tc_fence_after();
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + uint32_t(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+      tmem_wait_ld();
+      const int valid = Tk - t * Cfg::BN;
+      if (valid < Cfg::BN) {
+#pragma unroll
+        for (int e = 0; e < 128; ++e)
+          if (e >= valid) sv[e] = -INFINITY;
+      }
+      float mx = sv[0];
+#pragma unroll
+      for (int e = 1; e < 128; ++e) mx = fmaxf(mx, sv[e]);
+      const float m_cand = mx * scale_log2;
+      const bool need = (t == 0) || (m_cand > m_ref + Cfg::RESCALE_THRESHOLD);
+      float alpha = 1.f;
+      if (need) {
+        const float m_new = fmaxf(m_ref, m_cand);
+        alpha = (t == 0) ? 0.f : ex2_approx(m_ref - m_new);
+        m_ref = m_new;
+      }
       float rs = 0.f;
-#pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
-        uint32_t rr[32];
-        tmem_ld32(s_tmem + uint32_t(c0), rr);
-        tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p0 = (c0 + e < valid) ? exp2f(fmaf(__uint_as_float(rr[e]), scale_log2, -m_new)) : 0.f;
-          float p1 = (c0 + e + 1 < valid) ? exp2f(fmaf(__uint_as_float(rr[e + 1]), scale_log2, -m_new)) : 0.f;
+          const float p0 = ex2_approx(fmaf(sv[c * 32 + e], scale_log2, -m_ref));
+          const float p1 = ex2_approx(fmaf(sv[c * 32 + e + 1], scale_log2, -m_ref));
           rs += p0 + p1;
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
-        tmem_st16(s_tmem + uint32_t(c0 >> 1), pk);
+        tmem_st16(s_tmem + uint32_t(c * 16), pk);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[buf]);
-      const float alpha = (t == 0) ? 0.f : exp2f(m_run - m_new);
-      if (t > 0) {
-        const int pb = (t - 1) & 1;
-        const uint32_t pu = uint32_t((t - 1) >> 1);
-        if (!mbar_wait(&o_full[pb], pu & 1, abort_flag)) { ok = false; break; }
+      // Rescale this row's O accumulator when its reference max moved (warp-collective
+      // TMEM access: the whole warp takes the branch, rows that did not move use 1).
+      if (t > 0 && __any_sync(0xffffffffu, need)) {
+        if (!mbar_wait(&o_done[qt], uint32_t(t - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t o_tmem = tmem + Cfg::O_COL + uint32_t(pb * D) + lane_off;
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
           uint32_t rr[32];
           tmem_ld32(o_tmem + uint32_t(c0), rr);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o_acc[c0 + e] = (o_acc[c0 + e] + __uint_as_float(rr[e])) * alpha;
+          for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+          tmem_st32(o_tmem + uint32_t(c0), rr);
         }
-        tc_fence_before();
-        mbar_arrive(&o_empty[pb]);
       }
       l_run = l_run * alpha + rs;
-      m_run = m_new;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[qt]);
     }
-    if (ok) {
-      const int pb = (n_kv - 1) & 1;
-      const uint32_t pu = uint32_t((n_kv - 1) >> 1);
-      if (mbar_wait(&o_full[pb], pu & 1, abort_flag)) {
-        tc_fence_after();
-        const uint32_t o_tmem = tmem + Cfg::O_COL + uint32_t(pb * D) + lane_off;
+    if (ok && mbar_wait(&o_done[qt], uint32_t(n_kv - 1) & 1, abort_flag)) {
+      tc_fence_after();
+      const int qi = q0 + qt * Cfg::BM + row;
+      const float inv_l = 1.f / l_run;
+      float g = 1.f;
+      const int64_t orow = int64_t(b) * Tq + qi;
+      if (gate != nullptr && qi < Tq) {
+        const float lg = __bfloat162float(gate[orow * ld_gate + h]);
+        const float sg = round_bf16(1.f / (1.f + expf(-lg)));
+        g = round_bf16(2.f * sg);
+      }
+      __nv_bfloat16* op = O + orow * ldo + int64_t(h) * D;
 #pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t rr[32];
-          tmem_ld32(o_tmem + uint32_t(c0), rr);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o_acc[c0 + e] += __uint_as_float(rr[e]);
-        }
-        const int qi = q0 + row;
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t rr[32];
+        tmem_ld32(o_tmem + uint32_t(c0), rr);
+        tmem_wait_ld();
         if (qi < Tq) {
-          const int64_t orow = int64_t(b) * Tq + qi;
-          float g = 1.f;
-          if (gate != nullptr) {
-            const float lg = __bfloat162float(gate[orow * ld_gate + h]);
-            const float sg = round_bf16(1.f / (1.f + expf(-lg)));
-            g = round_bf16(2.f * sg);
-          }
-          const float inv_l = 1.f / l_run;
-          __nv_bfloat16* op = O + orow * ldo + int64_t(h) * D;
 #pragma unroll
-          for (int c0 = 0; c0 < D; c0 += 8) {
+          for (int e8 = 0; e8 < 32; e8 += 8) {
             float v[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float o = round_bf16(o_acc[c0 + e] * inv_l);
+              const float o = round_bf16(__uint_as_float(rr[e8 + e]) * inv_l);
               v[e] = gate != nullptr ? o * g : o;
             }
-            st8<__nv_bfloat16>(op + c0, v);
+            st8<__nv_bfloat16>(op + c0 + e8, v);
           }
         }
       }
     }
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
@@ -361,9 +378,9 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
     LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     attr_dev = dev;
   }
-  dim3 grid(unsigned((Tq + 127) / 128), unsigned(H), unsigned(B));
+  dim3 grid(unsigned((Tq + 2 * Cfg::BM - 1) / (2 * Cfg::BM)), unsigned(H), unsigned(B));
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, 192, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), scale_log2,
+  kern<<<grid, 320, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), scale_log2,
                                     static_cast<const __nv_bfloat16*>(gate), ld_gate), ltx::note_launch();
 }
 

@@ -302,6 +302,51 @@ __global__ void euler_kernel(const T* __restrict__ s, const T* __restrict__ d, i
   st_elem<T>(out + i, __fadd_rn(sv, __fmul_rn(vel, dt)));
 }
 
+// ---------------------------------------------------------------------------------
+// Sequence-parallel exchange layouts (all-to-all send / receive buffers).
+// pack:   dst[j][r][:] = concat over segments s of src[r][off_s + j*w_s : off_s + (j+1)*w_s]
+// unpack: dst[r][j*w : (j+1)*w] = src[j][r][:]
+// One thread moves 8 consecutive elements (16 bytes of bf16).
+// ---------------------------------------------------------------------------------
+struct SpSegments {
+  int n;
+  int off[4];
+  int w[4];
+  int W;  // sum of w
+};
+
+__global__ void sp_pack_kernel(const uint4* __restrict__ src, int64_t ld_src8, int64_t rows, int parts, SpSegments seg,
+                               uint4* __restrict__ dst) {
+  const int W8 = seg.W >> 3;
+  const int64_t total = int64_t(parts) * rows * W8;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t j = i / (rows * W8);
+    const int64_t rem = i - j * rows * W8;
+    const int64_t r = rem / W8;
+    int c8 = int(rem - r * W8);
+    int s = 0;
+    while (c8 >= (seg.w[s] >> 3)) {
+      c8 -= seg.w[s] >> 3;
+      ++s;
+    }
+    dst[i] = src[r * ld_src8 + ((seg.off[s] + int(j) * seg.w[s]) >> 3) + c8];
+  }
+}
+
+__global__ void sp_unpack_kernel(const uint4* __restrict__ src, int64_t rows, int parts, int w8,
+                                 uint4* __restrict__ dst, int64_t ld_dst8) {
+  const int64_t total = int64_t(parts) * rows * w8;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int64_t r = i / (int64_t(parts) * w8);
+    const int64_t rem = i - r * parts * w8;
+    const int64_t j = rem / w8;
+    const int64_t c8 = rem - j * w8;
+    dst[r * ld_dst8 + j * w8 + c8] = src[(j * rows + r) * w8 + c8];
+  }
+}
+
 inline unsigned grid_for(int64_t work, int threads) {
   int64_t g = (work + threads - 1) / threads;
   const int64_t cap = int64_t(num_sms()) * 16;

@@ -141,20 +141,40 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int64_t m = int64_t(m0) + row_in_tile;
       const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
+      const bool has_res = epi.kind == LTX_EPI_GATE_RESIDUAL;
+      // sample / token of this row, once per tile (32-bit division; M < 2^31)
+      const int64_t sb = int64_t(int(m) / int(epi.rows_per_batch));
+      const int64_t stok = m - sb * epi.rows_per_batch;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t rr[32];
-        tmem_ld32(tbase + uint32_t(c0), rr);
+      for (int c0 = 0; c0 < BN; c0 += 64) {
+        // Issue the slab's residual loads (8 x 16 B per row) before the TMEM load so
+        // their latency overlaps instead of serialising per 8 columns.
+        float res[64];
+        if (has_res && m < M) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            const int64_t col = int64_t(n0) + c0 + g * 8;
+            if (col + 8 <= N) {
+              float r8[8];
+              ld8<__nv_bfloat16>(epi.residual + m * epi.ld_res + col, r8);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) res[g * 8 + e] = r8[e];
+            }
+          }
+        }
+        uint32_t rr[64];
+        tmem_ld32(tbase + uint32_t(c0), *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+        tmem_ld32(tbase + uint32_t(c0 + 32), *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
         tmem_wait_ld();
         if (m < M) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
+          for (int g = 0; g < 8; ++g) {
             const int64_t col = int64_t(n0) + c0 + g * 8;
             if (col + 8 <= N) {
               float v[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(rr[g * 8 + e]);
-              epilogue8<__nv_bfloat16>(epi, m, col, v);
+              epilogue8<__nv_bfloat16>(epi, m, col, v, has_res ? &res[g * 8] : nullptr, sb, stok);
               st8<__nv_bfloat16>(C + m * ldc + col, v);
             } else {
 #pragma unroll

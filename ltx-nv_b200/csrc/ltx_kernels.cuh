@@ -88,11 +88,26 @@ LTX_DEVICE float gelu_tanh_f(float x) {
 }
 LTX_DEVICE float silu_f(float x) { return x / (1.f + expf(-x)); }
 
+// GELU-tanh with the hardware tanh approximation (relative error ~2^-11, below the
+// 2^-8 rounding of the bf16 result); the fp32 accuracy mode uses gelu_tanh_f.
+LTX_DEVICE float gelu_tanh_fast(float x) {
+  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
+  return 0.5f * x * (1.f + t);
+}
+template <typename T> LTX_DEVICE float gelu_act(float x);
+template <> LTX_DEVICE float gelu_act<float>(float x) { return gelu_tanh_f(x); }
+template <> LTX_DEVICE float gelu_act<__nv_bfloat16>(float x) { return gelu_tanh_fast(x); }
+
 // Apply the epilogue to 8 consecutive accumulator columns [col, col+8) of row `row`.
 // Rounding follows the reference's op-by-op dtype: the Linear result is rounded to
 // the activation dtype before the activation / gate / residual is applied.
+// `sb` / `st` are the row's sample and token index (row = sb * rows_per_batch + st);
+// pass sb < 0 to have them computed here (a 64-bit division: hoist it out of loops).
 template <typename T>
-LTX_DEVICE void epilogue8(const Epi<T>& e, int64_t row, int64_t col, float (&v)[8]) {
+LTX_DEVICE void epilogue8(const Epi<T>& e, int64_t row, int64_t col, float (&v)[8], const float* res_pre = nullptr,
+                          int64_t sb = -1, int64_t st = 0) {
   if (e.bias) {
     float b[8];
     ld8<T>(e.bias + col, b);
@@ -104,22 +119,30 @@ LTX_DEVICE void epilogue8(const Epi<T>& e, int64_t row, int64_t col, float (&v)[
   switch (e.kind) {
     case LTX_EPI_GELU_TANH:
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = gelu_tanh_f(v[i]);
+      for (int i = 0; i < 8; ++i) v[i] = gelu_act<T>(v[i]);
       break;
     case LTX_EPI_SILU:
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = silu_f(v[i]);
       break;
     case LTX_EPI_GATE_RESIDUAL: {
-      const int64_t b = row / e.rows_per_batch, t = row - b * e.rows_per_batch;
       float g[8], r[8];
       if (e.gate.on) {
-        e.gate.at8(b, t, col, g);
+        if (sb < 0) {
+          sb = row / e.rows_per_batch;
+          st = row - sb * e.rows_per_batch;
+        }
+        e.gate.at8(sb, st, col, g);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) g[i] = 1.f;
       }
-      ld8<T>(e.residual + row * e.ld_res + col, r);
+      if (res_pre != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = res_pre[i];
+      } else {
+        ld8<T>(e.residual + row * e.ld_res + col, r);
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = r[i] + round_to<T>(v[i] * g[i]);
       break;
@@ -145,7 +168,7 @@ LTX_DEVICE float epilogue1(const Epi<T>& e, int64_t row, int64_t col, float v) {
   v = round_to<T>(v);
   switch (e.kind) {
     case LTX_EPI_GELU_TANH:
-      return gelu_tanh_f(v);
+      return gelu_act<T>(v);
     case LTX_EPI_SILU:
       return silu_f(v);
     case LTX_EPI_GATE_RESIDUAL: {

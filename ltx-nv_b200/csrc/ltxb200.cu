@@ -5,3 +5,4 @@
 #include "elementwise.cu"
 #include "gemm.cu"
 #include "attention.cu"
+#include "parallel.cu"

@@ -226,6 +226,7 @@ class LTXModel(torch.nn.Module):
         self.av_ca_v2a_gate_adaln_single = AdaLayerNormSingle(a, 1)
         self.blocks = torch.nn.ModuleList([Block(cfg) for _ in range(cfg.num_layers)])
         self._rope_cache: dict = {}
+        self._sp = None  # ltx_parallel.SequenceParallel when the video tokens are sharded
 
     # ------------------------------------------------------------------ preparation
     def _rope(self, positions: torch.Tensor, dim: int, dtype: torch.dtype, max_pos: list, heads: int) -> RopeTables:
@@ -310,8 +311,12 @@ class LTXModel(torch.nn.Module):
         # self-attention
         nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_RMS, eps, st.mod(table, st.tmod, 0, 1))
         qkv = attn1.project_qkv(h, st.T, st.pe)
-        o = attn1.attend(qkv[:, :inner], qkv[:, inner:2 * inner], qkv[:, 2 * inner:3 * inner],
-                         qkv[:, 3 * inner:] if gated else None, st.B, st.T, st.T)
+        if self._sp is not None and not a:
+            # sequence-parallel: this rank holds st.T of the video tokens (ltx_parallel)
+            o = self._sp.self_attention(attn1, qkv, st)
+        else:
+            o = attn1.attend(qkv[:, :inner], qkv[:, inner:2 * inner], qkv[:, 2 * inner:3 * inner],
+                             qkv[:, 3 * inner:3 * inner + attn1.heads] if gated else None, st.B, st.T, st.T)
         nat.linear(o, attn1.to_out.weight, st.x,
                    nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn1.to_out.bias, residual=st.x,
                                 gate=st.mod(table, st.tmod, None, 2), rows_per_batch=st.T))

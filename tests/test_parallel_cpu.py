@@ -1,0 +1,104 @@
+"""Host-side logic of the multi-GPU step, on CPU with gloo ranks (world size 2 and 4):
+rank layouts, token shards, and the Ulysses all-to-all exchange pattern. The pack /
+unpack semantics of ltx_sp_pack / ltx_sp_unpack (include/ltxb200.h) are restated here
+in torch so the exchange can run without a GPU; attention over the exchanged buffers
+must equal attention over the full sequence."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+from ltx_parallel import Layout, qkv_segments
+
+
+def test_layouts():
+    lay = [Layout.make(8, r) for r in range(8)]
+    assert all(x.cfg == 2 and x.sp == 4 for x in lay)
+    assert [x.sample for x in lay] == [0, 0, 0, 0, 1, 1, 1, 1]
+    assert lay[5].sp_rank == 1 and lay[5].tokens(6144) == (1536, 3072)
+    assert lay[0].sp_groups() == [[0, 1, 2, 3], [4, 5, 6, 7]]
+    assert lay[0].cfg_groups() == [[0, 4], [1, 5], [2, 6], [3, 7]]
+    two = Layout.make(2, 1)
+    assert two.cfg == 2 and two.sp == 1 and two.sample == 1 and two.tokens(6144) == (0, 6144)
+    sp_only = Layout.make(2, 1, cfg=1)
+    assert sp_only.sample == -1 and sp_only.tokens(480) == (240, 480)
+    assert Layout.make(1, 0).sp == 1
+    with pytest.raises(ValueError):
+        Layout.make(8, 0).tokens(27588 * 2 + 2)
+    assert Layout.make(8, 3).tokens(27588) == (3 * 6897, 4 * 6897)
+
+
+def test_qkv_segments():
+    assert qkv_segments(2048, 32, 4, True) == [(0, 512), (2048, 512), (4096, 512), (6144, 8)]
+    assert qkv_segments(2048, 32, 2, False) == [(0, 1024), (2048, 1024), (4096, 1024)]
+
+
+def pack_ref(src, parts, segs):
+    return torch.stack([torch.cat([src[:, o + j * w:o + (j + 1) * w] for o, w in segs], dim=1) for j in range(parts)])
+
+
+def unpack_ref(src):
+    p, rows, w = src.shape
+    return src.permute(1, 0, 2).reshape(rows, p * w)
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(0)
+        heads, d, t = 8, 16, 24 * world
+        dim = heads * d
+        qkv_full = torch.randn(t, 3 * dim + heads)
+        lay = Layout.make(world, rank, cfg=1)
+        t0, t1 = lay.tokens(t)
+        local = qkv_full[t0:t1]
+        segs = qkv_segments(dim, heads, world, True)
+        w = sum(s[1] for s in segs)
+        send = pack_ref(local, world, segs)
+        recv = torch.empty(t, w)
+        dist.all_to_all_single(recv, send.reshape(world * (t1 - t0), w))
+        hp, dp = heads // world, dim // world
+        qh = recv[:, :dp].view(t, hp, d).transpose(0, 1)
+        kh = recv[:, dp:2 * dp].view(t, hp, d).transpose(0, 1)
+        vh = recv[:, 2 * dp:3 * dp].view(t, hp, d).transpose(0, 1)
+        gate = 2 * torch.sigmoid(recv[:, 3 * dp:3 * dp + hp])
+        out = (F.scaled_dot_product_attention(qh, kh, vh).transpose(0, 1) * gate[..., None]).reshape(t, dp)
+        back = torch.empty(t, dp)
+        dist.all_to_all_single(back, out.contiguous())
+        mine = unpack_ref(back.view(world, t1 - t0, dp))
+        # full-sequence reference on this rank's tokens
+        qf = qkv_full[:, :dim].view(t, heads, d).transpose(0, 1)
+        kf = qkv_full[:, dim:2 * dim].view(t, heads, d).transpose(0, 1)
+        vf = qkv_full[:, 2 * dim:3 * dim].view(t, heads, d).transpose(0, 1)
+        gf = 2 * torch.sigmoid(qkv_full[:, 3 * dim:])
+        ref = (F.scaled_dot_product_attention(qf, kf, vf).transpose(0, 1) * gf[..., None]).reshape(t, dim)[t0:t1]
+        q.put((rank, float((mine - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ulysses_exchange_equals_full_attention_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(err < 1e-5 for _, err in res), res
