@@ -19,8 +19,9 @@ Prints one JSON line on rank 0.
             on the launching stream, against MEASURED_PEAKS.json.
   cpu_baseline  the CPU oracle (the reference's PyTorch math restated) on this box's
             host cores for a bounded sample (one of the 28 blocks), scaled to a step.
-N > 1: every rank runs its own independent denoise job (one latent each; the CFG pair
-stays on one GPU) - "replicas", weak scaling.
+N > 1: the same single step split over the N GPUs (strong scaling): CFG cond/uncond on
+two GPU groups x Ulysses sequence parallelism over the video tokens inside each group
+(ltx_parallel.ParallelDenoiser, NCCL all-to-all / all-gather over NVLink).
 """
 
 from __future__ import annotations
@@ -161,19 +162,30 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
     c = CFG3
     t = c["f"] * c["h"] * c["w"]
     model, cfg = build_model(dev)
-    latent, ctx, pos, kf, sigmas = make_inputs(dev, seed=7 + rank)
+    latent, ctx, pos, kf, sigmas = make_inputs(dev, seed=7)
     cpos, cneg = ctx[:1], ctx[1:]
+    if world > 1:
+        import ltx_parallel
 
-    def step(lat):
-        return ltx_dit.cfg_denoise_step(model, lat, pos, cpos, cneg, sigmas, 0, c["cfg_scale"], keyframes_mask=kf)[2]
+        pdn = ltx_parallel.ParallelDenoiser(model)
+        layout = pdn.layout
+
+        def step(lat):
+            return pdn.step(lat, pos, cpos, cneg, sigmas, 0, c["cfg_scale"], keyframes_mask=kf)
+    else:
+        layout = None
+
+        def step(lat):
+            return ltx_dit.cfg_denoise_step(model, lat, pos, cpos, cneg, sigmas, 0, c["cfg_scale"],
+                                            keyframes_mask=kf)[2]
 
     stream = torch.cuda.current_stream(dev)
-    # warm-up (eager), then capture one step in a CUDA graph
+    # warm-up (eager), then capture one step in a CUDA graph (single GPU)
     for _ in range(max(args.warmup, 1)):
         step(latent)
     torch.cuda.synchronize(dev)
     graph = None
-    if not args.no_graph:
+    if not args.no_graph and world == 1:
         graph = torch.cuda.CUDAGraph()
         static_in = latent.clone()
         with torch.cuda.graph(graph):
@@ -210,8 +222,10 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
     ms_per_step = ms / args.steps
-    tokens_per_step_per_rank = 2 * t
-    value = tokens_per_step_per_rank * world / (ms_per_step / 1e3)
+    # one CFG step of one latent = 2 * T latent tokens for the whole job (all ranks
+    # together: CFG split x sequence parallel = strong scaling)
+    tokens_per_step = 2 * t
+    value = tokens_per_step / (ms_per_step / 1e3)
 
     # ---------------------------------------------------------------- e2e (public API, host buffers)
     host_in = torch.empty(1, t, 128, dtype=torch.bfloat16, pin_memory=True)
@@ -235,7 +249,7 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         tt = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
-    e2e_value = tokens_per_step_per_rank * world / (e2e_ms / e2e_steps / 1e3)
+    e2e_value = tokens_per_step / (e2e_ms / e2e_steps / 1e3)
 
     # ---------------------------------------------------------------- per-kernel breakdown
     with nat.profile() as prof:
@@ -264,17 +278,19 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
                  for k, v in sorted(kern.items(), key=lambda kv: -kv[1]["total_ms"])}
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak" if world > 1 else "weak",
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "BASELINE config 3: full-size video DiT CFG denoise step", "model": "LTX-2.5 video DiT "
-                   "28 blocks, hidden 2048, 32x64 heads, FFN 8192 (random-init N(0,0.02))", "global_batch": 2 * world,
-                   "latent_tokens": t, "seq_len": t, "text_tokens": CFG3["text"], "parallelism":
-                   f"replicas x{world} (each: CFG pair on one GPU)", "l2": "inputs larger than L2 (4.2 GB weights, "
-                   "~1 GB activations per step)", "cuda_graph": graph is not None},
-        "steps_per_s": 1e3 / ms_per_step * world, "step_tflops_per_gpu": tflops,
-        "pct_bf16_peak": tflops / peaks["bf16_tflops"], "pct_bf16_peak_sustained": tflops / peak,
+                   "28 blocks, hidden 2048, 32x64 heads, FFN 8192 (random-init N(0,0.02))", "global_batch": 2,
+                   "latent_tokens": t, "seq_len": t, "text_tokens": CFG3["text"],
+                   "parallelism": "single GPU" if world == 1 else f"cfg{layout.cfg} x sp{layout.sp} (Ulysses, NCCL)",
+                   "l2": "inputs larger than L2 (4.2 GB weights, ~1 GB activations per step)",
+                   "cuda_graph": graph is not None},
+        "steps_per_s": 1e3 / ms_per_step, "step_tflops_per_gpu": tflops / world,
+        "pct_bf16_peak": tflops / world / peaks["bf16_tflops"], "pct_bf16_peak_sustained": tflops / world / peak,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 2,
-                "d2h_bytes_per_step": host_out.numel() * 2, "steps": e2e_steps, "api": "ltx_dit.cfg_denoise_step"},
+                "d2h_bytes_per_step": host_out.numel() * 2, "steps": e2e_steps,
+                "api": "ltx_dit.cfg_denoise_step" if world == 1 else "ltx_parallel.ParallelDenoiser.step"},
         "roofline": roofline,
         "gpu_launches": launches_per_step * args.steps,
         "gpu_launches_per_step": launches_per_step,
@@ -469,6 +485,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attn-schedule", type=int, default=None, help="attention MMA schedule (0, 1, 2)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -482,6 +499,10 @@ def main():
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.attn_schedule is not None:
+        import _native
+
+        _native.attention_set_schedule(args.attn_schedule)
     if args.probe:
         print(json.dumps(run_probe(args, dev)), flush=True)
         return

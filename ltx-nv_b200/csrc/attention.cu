@@ -42,7 +42,9 @@ LTX_DEVICE uint8_t* fa_align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-template <int D>
+// SCHED: MMA-warp schedule. 0 = fixed order with blocking waits; 1 = readiness-driven
+// (non-blocking probes); 2 = readiness-driven with a short back-off when idle.
+template <int D, int SCHED>
 // 10 warps: three share one SM sub-partition's 16K registers, so <= 168 per thread.
 __global__ void __launch_bounds__(320, 1)
     fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -74,7 +76,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], 2);  // released by both Q tiles' P V
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -158,38 +160,84 @@ __global__ void __launch_bounds__(320, 1)
         }
         umma_commit(&o_done[i]);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(0, 0);
-        issue_qk(1, 0);
-      }
-      for (int t = 0; ok && t < n_kv; ++t) {
-        const int s = t % Cfg::STAGES;
-        const uint32_t r = uint32_t(t / Cfg::STAGES);
-        const bool more = t + 1 < n_kv;
-        const int s1 = (t + 1) % Cfg::STAGES;
-        const uint32_t r1 = uint32_t((t + 1) / Cfg::STAGES);
-        if (!mbar_wait(&v_full[s], r & 1, abort_flag)) break;
-        for (int i = 0; i < 2; ++i) {
-          if (!mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      if constexpr (SCHED == 0) {
+        // Fixed order per key tile t: P_0 V_t, S_0 <- Q_0 K_{t+1}^T, P_1 V_t,
+        // S_1 <- Q_1 K_{t+1}^T, each step waiting (suspended in hardware) for its inputs.
+        ok = ok && mbar_wait(&k_full[0], 0, abort_flag);
+        if (ok) {
           tc_fence_after();
-          issue_pv(i, t);
-          if (more) {
-            // S_i is rewritten by Q_i K_{t+1}^T after P_i V_t, issued in this order on
-            // this thread (tcgen05.mma of one CTA execute in issue order).
-            if (!mbar_wait(&k_full[s1], r1 & 1, abort_flag)) {
+          issue_qk(0, 0);
+          issue_qk(1, 0);
+        }
+        for (int t = 0; ok && t < n_kv; ++t) {
+          const int s = t % Cfg::STAGES;
+          if (!mbar_wait(&v_full[s], uint32_t(t / Cfg::STAGES) & 1, abort_flag)) break;
+          for (int i = 0; i < 2 && ok; ++i) {
+            if (!mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_qk(i, t + 1);
+            issue_pv(i, t);
+            umma_commit(&kv_empty[s]);
+            if (t + 1 < n_kv) {
+              if (!mbar_wait(&k_full[(t + 1) % Cfg::STAGES], uint32_t((t + 1) / Cfg::STAGES) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_qk(i, t + 1);
+            }
           }
         }
-        umma_commit(&kv_empty[s]);
+        ok = false;  // skip the readiness-driven loop below
+      }
+      // Readiness-driven schedule: serve the two Q tiles independently, in the order
+      // their inputs become ready, so their softmaxes drift apart and overlap the other
+      // tile's MMAs. Every wait here is a non-blocking probe (a tile waiting for a K/V
+      // stage still held by the other tile never blocks the other tile); an idle pass
+      // backs off briefly so the poll does not take issue slots from the softmax warps.
+      // Per tile i: next_qk[i] = next S_i = Q_i K_t^T to issue (needs K_t, and P_i V_{t-1}
+      // issued so S_i is free); next_pv[i] = next P_i V_t to issue (needs P_i(t) and V_t).
+      // A K/V stage is released once both tiles issued their P V on it (count 2).
+      int next_qk[2] = {0, 0}, next_pv[2] = {0, 0};
+      unsigned long long idle_since = clock64();
+      while (ok && (next_pv[0] < n_kv || next_pv[1] < n_kv)) {
+        bool progressed = false;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int tq = next_qk[i];
+          if (tq < n_kv && tq == next_pv[i] &&
+              mbar_test_wait(&k_full[tq % Cfg::STAGES], uint32_t(tq / Cfg::STAGES) & 1)) {
+            // S_i is rewritten by Q_i K_t^T after P_i V_{t-1}, issued earlier on this
+            // thread (tcgen05.mma of one CTA execute in issue order).
+            tc_fence_after();
+            issue_qk(i, tq);
+            next_qk[i] = tq + 1;
+            progressed = true;
+          }
+          const int tp = next_pv[i];
+          if (tp < next_qk[i] && mbar_test_wait(&p_full[i], uint32_t(tp) & 1) &&
+              mbar_test_wait(&v_full[tp % Cfg::STAGES], uint32_t(tp / Cfg::STAGES) & 1)) {
+            tc_fence_after();
+            issue_pv(i, tp);
+            umma_commit(&kv_empty[tp % Cfg::STAGES]);
+            next_pv[i] = tp + 1;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          idle_since = clock64();
+        } else if (*reinterpret_cast<volatile int*>(abort_flag)) {
+          ok = false;
+        } else if (clock64() - idle_since > LTX_WAIT_LIMIT_CYCLES) {
+          ltx_flag_error(LTX_DEVERR_MBAR_TIMEOUT);
+          *reinterpret_cast<volatile int*>(abort_flag) = 1;
+          ok = false;
+        } else if (SCHED == 2) {
+          __nanosleep(40);
+        }
       }
     }
   } else {
@@ -217,9 +265,15 @@ __global__ void __launch_bounds__(320, 1)
         for (int e = 0; e < 128; ++e)
           if (e >= valid) sv[e] = -INFINITY;
       }
-      float mx = sv[0];
+      // row max: 3-input max, 8 independent chains
+      float m8[8];
 #pragma unroll
-      for (int e = 1; e < 128; ++e) mx = fmaxf(mx, sv[e]);
+      for (int e = 0; e < 8; ++e) m8[e] = sv[e];
+#pragma unroll
+      for (int e = 8; e < 128; e += 16)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m8[j] = fmax3(m8[j], sv[e + j], sv[e + 8 + j]);
+      const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       const float m_cand = mx * scale_log2;
       const bool need = (t == 0) || (m_cand > m_ref + Cfg::RESCALE_THRESHOLD);
       float alpha = 1.f;
@@ -228,18 +282,37 @@ __global__ void __launch_bounds__(320, 1)
         alpha = (t == 0) ? 0.f : ex2_approx(m_ref - m_new);
         m_ref = m_new;
       }
-      float rs = 0.f;
+      // x = s * scale_log2 - m_ref and the row sum in packed fp32x2 (two lanes per
+      // instruction); on full tiles one pair in four takes the FMA-pipe exponential.
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
+      const uint64_t nm2 = f2_pack(-m_ref, -m_ref);
+      uint64_t rs2[4] = {0, 0, 0, 0};  // bit pattern of (0.f, 0.f)
+      const bool full = valid >= Cfg::BN;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2_approx(fmaf(sv[c * 32 + e], scale_log2, -m_ref));
-          const float p1 = ex2_approx(fmaf(sv[c * 32 + e + 1], scale_log2, -m_ref));
-          rs += p0 + p1;
+          float x0, x1, p0, p1;
+          f2_unpack(f2_fma(f2_pack(sv[c * 32 + e], sv[c * 32 + e + 1]), sc2, nm2), x0, x1);
+          if (full && ((e & 7) == 6)) {
+            ex2_poly2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
+          rs2[(e >> 1) & 3] = f2_add(rs2[(e >> 1) & 3], f2_pack(p0, p1));
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
         tmem_st16(s_tmem + uint32_t(c * 16), pk);
+      }
+      float rs;
+      {
+        float a0, a1, b0, b1;
+        f2_unpack(f2_add(f2_add(rs2[0], rs2[1]), f2_add(rs2[2], rs2[3])), a0, a1);
+        (void)b0;
+        (void)b1;
+        rs = a0 + a1;
       }
       // Rescale this row's O accumulator when its reference max moved (warp-collective
       // TMEM access: the whole warp takes the branch, rows that did not move use 1).
@@ -361,7 +434,10 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const float* __restrict_
   for (int c = 0; c < D; ++c) op[c] = (acc[c] / l) * g;
 }
 
-template <int D>
+// MMA-warp schedule of the bf16 attention kernel (ltx_attention_set_schedule).
+static int g_fmha_sched = 0;
+
+template <int D, int SCHED>
 void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
                     int64_t ldo, int B, int64_t Tq, int64_t Tk, int H, float scale, const void* gate,
                     int64_t ld_gate, cudaStream_t s) {
@@ -370,7 +446,7 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   const CUtensorMap tq = make_tmap_bf16_2d(q, cols, uint64_t(B) * Tq, uint64_t(ldq), 64, 128);
   const CUtensorMap tk = make_tmap_bf16_2d(k, cols, uint64_t(B) * Tk, uint64_t(ldk), 64, 128);
   const CUtensorMap tv = make_tmap_bf16_2d(v, cols, uint64_t(B) * Tk, uint64_t(ldv), 64, 128);
-  auto kern = fmha_tc_kernel<D>;
+  auto kern = fmha_tc_kernel<D, SCHED>;
   static int attr_dev = -1;
   int dev = 0;
   LTX_CUDA(cudaGetDevice(&dev));
@@ -409,10 +485,15 @@ extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t 
     check_vec_ptr(k, "k");
     check_vec_ptr(v, "v");
     check_vec_ptr(o, "o");
-    if (head_dim == 64)
-      launch_fmha_tc<64>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
-    else
-      launch_fmha_tc<128>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
+#define LTX_FMHA_CALL(DIM, SC) \
+  launch_fmha_tc<DIM, SC>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s)
+    const int sc = g_fmha_sched;
+    if (head_dim == 64) {
+      if (sc == 1) LTX_FMHA_CALL(64, 1); else if (sc == 2) LTX_FMHA_CALL(64, 2); else LTX_FMHA_CALL(64, 0);
+    } else {
+      if (sc == 1) LTX_FMHA_CALL(128, 1); else if (sc == 2) LTX_FMHA_CALL(128, 2); else LTX_FMHA_CALL(128, 0);
+    }
+#undef LTX_FMHA_CALL
   } else {
     dim3 grid(unsigned((Tq + 127) / 128), unsigned(heads), unsigned(B));
     auto Qp = static_cast<const float*>(q);

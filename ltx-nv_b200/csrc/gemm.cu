@@ -137,34 +137,45 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t u = uint32_t(local >> 1);
       const int m0 = (tile / n_tiles) * kBM;
       const int n0 = (tile % n_tiles) * BN;
+      const int64_t m = int64_t(m0) + row_in_tile;
+      const bool has_res = epi.kind == LTX_EPI_GATE_RESIDUAL && m < M;
+      // The residual does not depend on the accumulator: the first 64-column slab of it
+      // is loaded before waiting for the MMAs (overlapping the mainloop), and each later
+      // slab one slab ahead of its use.
+      uint4 rcur[8];
+      auto load_slab = [&](int c0, uint4 (&dst)[8]) {
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          const int64_t col = int64_t(n0) + c0 + g * 8;
+          dst[g] = (col + 8 <= N) ? *reinterpret_cast<const uint4*>(epi.residual + m * epi.ld_res + col)
+                                  : make_uint4(0, 0, 0, 0);
+        }
+      };
+      if (has_res) load_slab(0, rcur);
       if (!mbar_wait(&tfull[acc], u & 1, abort_flag)) break;
       tc_fence_after();
-      const int64_t m = int64_t(m0) + row_in_tile;
       const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
-      const bool has_res = epi.kind == LTX_EPI_GATE_RESIDUAL;
       // sample / token of this row, once per tile (32-bit division; M < 2^31)
       const int64_t sb = int64_t(int(m) / int(epi.rows_per_batch));
       const int64_t stok = m - sb * epi.rows_per_batch;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 64) {
-        // Issue the slab's residual loads (8 x 16 B per row) before the TMEM load so
-        // their latency overlaps instead of serialising per 8 columns.
-        float res[64];
-        if (has_res && m < M) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            const int64_t col = int64_t(n0) + c0 + g * 8;
-            if (col + 8 <= N) {
-              float r8[8];
-              ld8<__nv_bfloat16>(epi.residual + m * epi.ld_res + col, r8);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) res[g * 8 + e] = r8[e];
-            }
-          }
-        }
         uint32_t rr[64];
         tmem_ld32(tbase + uint32_t(c0), *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
         tmem_ld32(tbase + uint32_t(c0 + 32), *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
+        uint4 rnext[8];
+        if (has_res && c0 + 64 < BN) load_slab(c0 + 64, rnext);
+        float res[64];
+        if (has_res) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            unpack_bf16x2(rcur[g].x, res[g * 8 + 0], res[g * 8 + 1]);
+            unpack_bf16x2(rcur[g].y, res[g * 8 + 2], res[g * 8 + 3]);
+            unpack_bf16x2(rcur[g].z, res[g * 8 + 4], res[g * 8 + 5]);
+            unpack_bf16x2(rcur[g].w, res[g * 8 + 6], res[g * 8 + 7]);
+            rcur[g] = rnext[g];
+          }
+        }
         tmem_wait_ld();
         if (m < M) {
 #pragma unroll

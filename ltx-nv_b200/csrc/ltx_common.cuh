@@ -138,6 +138,19 @@ LTX_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probe (test_wait returns at once; try_wait may suspend the thread for
+// a while before reporting "not yet", which stalls a warp that polls several barriers).
+LTX_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Wait for the phase with the given parity to complete. Returns false (and flags the
 // device error word) if the wait exceeds the cycle budget; `abort` is a shared flag
 // that lets the other roles of the CTA give up promptly once one of them timed out.
@@ -285,6 +298,69 @@ LTX_DEVICE float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32x2 arithmetic (two lanes per instruction on sm_100).
+LTX_DEVICE uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+LTX_DEVICE void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+LTX_DEVICE uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+LTX_DEVICE uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+LTX_DEVICE uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// max of three fp32 values in one instruction.
+LTX_DEVICE float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x on the FMA / integer pipes, to take load off the special-function unit:
+// Cody-Waite range reduction x = n + f, n = round(x) (by the 1.5*2^23 shifter trick),
+// f in [-1/2, 1/2], 2^f by a cubic whose coefficients were fitted to minimise the
+// relative error on that interval (max relative error 7.6e-5), and 2^n added into the
+// exponent field. Valid for -126 <= x <= 127; callers pass finite x <= 8.
+LTX_DEVICE float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.0551708005f, f, 0.242609262f), f, 0.693260968f), f, 0.999928176f);
+  return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
+// The same for two values with packed fp32x2 arithmetic.
+LTX_DEVICE void ex2_poly2(float x0, float x1, float& y0, float& y1) {
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  const uint64_t shifter = f2_pack(12582912.f, 12582912.f);
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t t = f2_add(x, shifter);
+  const uint64_t f = f2_sub(x, f2_sub(t, shifter));
+  uint64_t p = f2_fma(f2_pack(0.0551708005f, 0.0551708005f), f, f2_pack(0.242609262f, 0.242609262f));
+  p = f2_fma(p, f, f2_pack(0.693260968f, 0.693260968f));
+  p = f2_fma(p, f, f2_pack(0.999928176f, 0.999928176f));
+  float t0, t1, p0, p1;
+  f2_unpack(t, t0, t1);
+  f2_unpack(p, p0, p1);
+  y0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - 0x4B400000) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - 0x4B400000) << 23));
 }
 LTX_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 

@@ -39,6 +39,16 @@ from ltx_nn import AdaLayerNormSingle, Attention, FeedForward, RopeTables, rope_
 
 DEVICE = torch.device("cuda")
 
+
+def _version(t: torch.Tensor) -> int:
+    """In-place modification counter of a tensor; -1 for inference-mode tensors, which do
+    not track one (the caches below then rely on the documented contract that positions
+    and text contexts are not modified in place while a model reuses them)."""
+    try:
+        return t._version
+    except RuntimeError:
+        return -1
+
 # ---------------------------------------------------------------------------------------
 # Config (ltx_dit.py:28-82)
 # ---------------------------------------------------------------------------------------
@@ -152,6 +162,7 @@ class _Stream:
     cross_ss: torch.Tensor | None  # (N, 4D)
     cross_gate: torch.Tensor | None  # (B, D)
     enabled: bool
+    context_src: torch.Tensor | None = None  # the caller's context tensor (cache identity)
 
     def mod(self, table: torch.Tensor, tmod: torch.Tensor, shift: int | None, scale: int | None,
             n_total: int | None = None, ld_tok: int | None = None) -> nat.Modulation:
@@ -226,18 +237,54 @@ class LTXModel(torch.nn.Module):
         self.av_ca_v2a_gate_adaln_single = AdaLayerNormSingle(a, 1)
         self.blocks = torch.nn.ModuleList([Block(cfg) for _ in range(cfg.num_layers)])
         self._rope_cache: dict = {}
+        self._kv_cache: dict = {}
+        self._cat_cache = None
         self._sp = None  # ltx_parallel.SequenceParallel when the video tokens are sharded
 
     # ------------------------------------------------------------------ preparation
     def _rope(self, positions: torch.Tensor, dim: int, dtype: torch.dtype, max_pos: list, heads: int) -> RopeTables:
-        key = (positions.data_ptr(), positions._version, tuple(positions.shape), dim, dtype, tuple(max_pos), heads)
-        tabs = self._rope_cache.get(key)
-        if tabs is None:
+        """RoPE tables, cached per positions tensor (positions are constant across the
+        denoise steps). The entry keeps a reference to the positions storage, so a new
+        tensor cannot reuse its address while the entry lives."""
+        key = (positions.data_ptr(), _version(positions), tuple(positions.shape), tuple(positions.stride()), dim,
+               dtype, tuple(max_pos), heads)
+        hit = self._rope_cache.get(key)
+        if hit is None:
             if len(self._rope_cache) > 16:
                 self._rope_cache.clear()
             tabs = rope_tables(positions, dim, dtype, self.cfg.theta, max_pos, heads, self.cfg.double_rope)
-            self._rope_cache[key] = tabs
-        return tabs
+            hit = (positions, tabs)
+            self._rope_cache[key] = hit
+        return hit[1]
+
+    def _text_kv(self, attn: Attention, ctx: torch.Tensor, rows: int, src: torch.Tensor) -> torch.Tensor:
+        """K/V projection of the text context with the k RMSNorm applied. Without
+        cross-adaLN it depends only on the context and the weights, both constant across
+        the denoise steps, so it is cached per (module, caller's context tensor `src`,
+        weights); the entry keeps `src` alive so its address cannot be reused."""
+        inner = attn.heads * attn.dim_head
+        wkv, bkv = attn.packed_kv()
+        key = id(attn)
+        hit = self._kv_cache.get(key)
+        if hit is not None:
+            c_ref, c_ver, shape, w_ptr, kv = hit
+            if c_ref is src and c_ver == _version(src) and shape == tuple(ctx.shape) and w_ptr == wkv.data_ptr():
+                return kv
+        kv = torch.empty(ctx.shape[0], wkv.shape[0], device=ctx.device, dtype=ctx.dtype)
+        nat.linear(ctx, wkv, kv, nat.epilogue(bias=bkv))
+        attn._norm_rope(kv[:, :inner], rows, attn.k_norm.weight, None)
+        self._kv_cache[key] = (src, _version(src), tuple(ctx.shape), wkv.data_ptr(), kv)
+        return kv
+
+    def cached_cat(self, a: torch.Tensor, b: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        """torch.cat([a, b]).to(dtype), reused while a and b are unchanged (the CFG
+        context pair is constant across the denoise loop)."""
+        c = self._cat_cache
+        if c is not None and c[0] is a and c[1] is b and c[2] == (_version(a), _version(b), dtype):
+            return c[3]
+        out = torch.cat([a, b], dim=0).to(dtype).contiguous()
+        self._cat_cache = (a, b, (_version(a), _version(b), dtype), out)
+        return out
 
     @staticmethod
     def _per_sample_timesteps(ts: torch.Tensor) -> torch.Tensor | None:
@@ -295,7 +342,7 @@ class LTXModel(torch.nn.Module):
             factor = cfg.av_ca_timestep_scale_multiplier / cfg.timestep_scale_multiplier
             cross_gate, _ = g_mod(cross.sigma.to(torch.float32).reshape(-1).contiguous(), dtype, scale * factor)
         return _Stream(stream, b, t, dim, heads, hd, x, tmod, 0 if t_sample is not None else 1, emb, prompt,
-                       context, s_len, pe, cross_pe, cross_ss, cross_gate, m.enabled)
+                       context, s_len, pe, cross_pe, cross_ss, cross_gate, m.enabled, context_src=m.context)
 
     # ------------------------------------------------------------------ block pieces
     def _self_and_text(self, blk: Block, st: _Stream, h: torch.Tensor):
@@ -338,11 +385,12 @@ class LTXModel(torch.nn.Module):
             nat.norm_modulate(ctx, enc, st.S, nat.LTX_NORM_NONE, eps,
                               nat.modulation(psst, st.prompt_mod, shift=(0, 0), scale=(d, d),
                                              mod_ld_batch=st.prompt_mod.shape[-1]))
-            ctx = enc
-        wkv, bkv = attn2.packed_kv()
-        kv = torch.empty(ctx.shape[0], wkv.shape[0], device=h.device, dtype=h.dtype)
-        nat.linear(ctx, wkv, kv, nat.epilogue(bias=bkv))
-        attn2._norm_rope(kv[:, :inner], st.S, attn2.k_norm.weight, None)
+            wkv, bkv = attn2.packed_kv()
+            kv = torch.empty(enc.shape[0], wkv.shape[0], device=h.device, dtype=h.dtype)
+            nat.linear(enc, wkv, kv, nat.epilogue(bias=bkv))
+            attn2._norm_rope(kv[:, :inner], st.S, attn2.k_norm.weight, None)
+        else:
+            kv = self._text_kv(attn2, ctx, st.S, st.context_src if st.context_src is not None else ctx)
         o = attn2.attend(qg[:, :inner], kv[:, :inner], kv[:, inner:2 * inner], qg[:, inner:] if gated else None,
                          st.B, st.T, st.S)
         gate = st.mod(table, st.tmod, None, 8) if cfg.cross_attention_adaln else None
@@ -689,7 +737,7 @@ def cfg_denoise_step(model: LTXModel, latent: torch.Tensor, positions: torch.Ten
     ts = torch.full((2, t, 1), sigma, device=dev, dtype=torch.float32)
     lat = latent.to(dtype)
     video = Modality(latent=lat.expand(2, -1, -1), sigma=sig, timesteps=ts, positions=positions.expand(2, -1, -1, -1),
-                     context=torch.cat([context_pos, context_neg], dim=0).to(dtype),
+                     context=model.cached_cat(context_pos, context_neg, dtype),
                      keyframes_mask=keyframes_mask.expand(2, -1, -1) if keyframes_mask is not None else None)
     va, _ = model.prepare(video, None, uniform_timesteps=True)
     model.run_blocks(va, None)

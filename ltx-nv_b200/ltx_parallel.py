@@ -153,7 +153,7 @@ class ParallelDenoiser:
         if lay.cfg == 2:
             ctx = context_pos if lay.sample == 0 else context_neg
         else:
-            ctx = torch.cat([context_pos, context_neg], dim=0)
+            ctx = model.cached_cat(context_pos, context_neg, dtype)
         video = ltx_dit.Modality(
             latent=lat_l.expand(nb, -1, -1), sigma=torch.full((nb,), sigma, device=dev),
             timesteps=torch.full((nb, tl, 1), sigma, device=dev), positions=positions[:, :, t0:t1].expand(nb, -1, -1, -1),

@@ -1,0 +1,86 @@
+"""Multi-GPU step (ltx_parallel) against the single-GPU step on the same inputs: each
+rank runs the same kernels on the same rows, so the next latent must be identical.
+Needs >= 2 (or 4) visible GPUs; skipped otherwise."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, cfg_split, q):
+    import sys
+    from datetime import timedelta
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    for p in (str(root), str(root / "ltx-nv_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        import ltx_dit
+        import ltx_parallel
+
+        cfg = ltx_dit.DiTConfig.video_only(num_layers=2, heads=32, head_dim=64, cross_dim=4096)
+        with torch.device("meta"):
+            model = ltx_dit.LTXModel(cfg)
+        gen = ltx_dit.PhiloxGenerator(11, dev)
+        sd = {}
+        for name, p in model.named_parameters():
+            w = gen.randn(*p.shape, dtype=torch.bfloat16).mul_(0.02)
+            if name.endswith(("q_norm.weight", "k_norm.weight")):
+                w.add_(1.0)
+            sd[name] = w
+        model.load_state_dict(sd, assign=True)
+        f, h, w_ = 8, 16, 16
+        t = f * h * w_
+        latent = gen.randn(1, t, 128, dtype=torch.bfloat16)
+        ctx = gen.randn(2, 128, 4096, dtype=torch.bfloat16)
+        pos = ltx_dit.video_positions(1, f, h, w_, 24.0, dev)
+        kf = torch.zeros(1, t, 1, device=dev)
+        kf[:, : h * w_] = 1
+        sigmas = torch.tensor([0.5, 0.25])
+        ref = ltx_dit.cfg_denoise_step(model, latent, pos, ctx[:1], ctx[1:], sigmas, 0, 3.0, keyframes_mask=kf,
+                                       fused_head=False)[2]
+        pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=cfg_split)
+        out = pdn.step(latent, pos, ctx[:1], ctx[1:], sigmas, 0, 3.0, keyframes_mask=kf)
+        torch.cuda.synchronize()
+        model._sp = None
+        diff = (out.float() - ref.float()).abs().max().item()
+        q.put((rank, diff, pdn.layout.cfg, pdn.layout.sp))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,cfg_split", [(2, 2), (2, 1), (4, 2)])
+def test_parallel_step_equals_single_gpu(world, cfg_split):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_split, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(d == 0.0 for _, d, _, _ in res), res
