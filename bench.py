@@ -485,7 +485,6 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--attn-schedule", type=int, default=None, help="attention MMA schedule (0, 1, 2)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -499,10 +498,6 @@ def main():
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if args.attn_schedule is not None:
-        import _native
-
-        _native.attention_set_schedule(args.attn_schedule)
     if args.probe:
         print(json.dumps(run_probe(args, dev)), flush=True)
         return

@@ -176,11 +176,6 @@ int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const 
                   int64_t ldo, int B, int64_t Tq, int64_t Tk, int heads, int head_dim, float scale,
                   const void* gate_logits, int64_t ld_gate, int dtype, void* stream);
 
-/* Tuning knob (process-wide): MMA-warp schedule of the bf16 attention kernel, 0 =
- * fixed order (default), 1 = readiness-driven, 2 = readiness-driven with back-off. No
- * counterpart in the reference. */
-int ltx_attention_set_schedule(int schedule);
-
 /* ---------------------------------------------------------------------------------- */
 /* Denoise update: X0 conversion + CFG guidance + Euler step.                          */
 /* Replaces guided_denoise_step's X0 (ltx_dit.py:591-593), guide (ltx_dit.py:551-562,  */

@@ -91,7 +91,6 @@ _SIGNATURES = {
     "ltx_linear": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64,
                                   ctypes.POINTER(Epilogue), ctypes.c_int, c_vp]),
     "ltx_gemm_set_tile_n": (ctypes.c_int, [ctypes.c_int]),
-    "ltx_attention_set_schedule": (ctypes.c_int, [ctypes.c_int]),
     "ltx_attention": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, ctypes.c_int, c_i64, c_i64,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, ctypes.c_int, c_vp]),
     "ltx_cfg_euler": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_float,
@@ -344,9 +343,6 @@ def linear(a: torch.Tensor, w: torch.Tensor, c: torch.Tensor, epi: Epilogue | No
 def gemm_set_tile_n(bn: int) -> None:
     _call("ltx_gemm_set_tile_n", bn)
 
-
-def attention_set_schedule(schedule: int) -> None:
-    _call("ltx_attention_set_schedule", schedule)
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, batch: int, tq: int, tk: int,

@@ -7,12 +7,18 @@
 //   warp 8      TMA producer: both Q tiles once, then K and V tiles of 128 keys into a
 //               STAGES-deep ring
 //   warp 9      tcgen05.mma issuer and TMEM owner
-// TMEM (512 columns): S_i at [128 i, 128 i + 128) receives S = Q_i K^T in fp32; the softmax
-// of tile i reads it once and writes P as packed bf16 over its first 64 columns; O_i at
-// [256 + D i, 256 + D (i+1)) accumulates P V across all key tiles (A operand read from
-// TMEM, V as an MN-major 128B-swizzled smem operand).
-// MMA issue order per key tile j: P_0 V_j, S_0 <- Q_0 K_{j+1}^T, P_1 V_j, S_1 <- Q_1 K_{j+1}^T,
-// so the softmax of one tile overlaps the MMAs of the other.
+// S_i = Q_i K^T lands in TMEM as fp32; the softmax of tile i writes P_i as packed bf16;
+// O_i accumulates P_i V over all key tiles in TMEM (A operand read from TMEM, V as an
+// MN-major 128B-swizzled smem operand).
+//
+// TMEM (512 columns):
+//   head_dim 64:  S_0, S_1 at [0,128), [128,256); P_0, P_1 at [256,320), [320,384);
+//                 O_0, O_1 at [384,448), [448,512). P has its own columns, so the softmax
+//                 releases S_i as soon as it has loaded it and the MMA warp computes
+//                 S_i(t+1) = Q_i K_{t+1}^T while the softmax of key tile t still runs: the
+//                 MMA round trip is off the softmax's critical path.
+//   head_dim 128: S_i at [128 i, 128 i + 128) with P_i written over its first 64 columns,
+//                 O_i at [256 + 128 i, ...); S_i(t+1) is issued after P_i V_t.
 // Lazy rescaling: each row keeps a reference max m_ref and only moves it (rescaling its
 // O row and l) when the tile max exceeds it by more than 8 (log2 units); P = 2^(s - m_ref)
 // then stays <= 256, and O / l is unchanged by the choice of reference.
@@ -34,7 +40,10 @@ struct FaCfg {
   static constexpr int STAGES = D == 64 ? 3 : 2;
   static constexpr int SMEM = TILE_BYTES * (2 + 2 * STAGES) + 512 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t O_COL = 256;
+  static constexpr bool SEP_P = D == 64;            // P in its own TMEM columns
+  static constexpr uint32_t s_col(int i) { return uint32_t(128 * i); }
+  static constexpr uint32_t p_col(int i) { return SEP_P ? uint32_t(256 + 64 * i) : uint32_t(128 * i); }
+  static constexpr uint32_t o_col(int i) { return SEP_P ? uint32_t(384 + 64 * i) : uint32_t(256 + D * i); }
   static constexpr float RESCALE_THRESHOLD = 8.f;
 };
 
@@ -42,9 +51,7 @@ LTX_DEVICE uint8_t* fa_align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// SCHED: MMA-warp schedule. 0 = fixed order with blocking waits; 1 = readiness-driven
-// (non-blocking probes); 2 = readiness-driven with a short back-off when idle.
-template <int D, int SCHED>
+template <int D>
 // 10 warps: three share one SM sub-partition's 16K registers, so <= 168 per thread.
 __global__ void __launch_bounds__(320, 1)
     fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -59,10 +66,11 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;               // [STAGES]
   uint64_t* v_full = k_full + Cfg::STAGES;   // [STAGES]
-  uint64_t* kv_empty = v_full + Cfg::STAGES; // [STAGES]
-  uint64_t* s_full = kv_empty + Cfg::STAGES; // [2] per Q tile
-  uint64_t* p_full = s_full + 2;             // [2]
-  uint64_t* o_done = p_full + 2;             // [2]
+  uint64_t* kv_empty = v_full + Cfg::STAGES; // [STAGES] released by both tiles' P V
+  uint64_t* s_full = kv_empty + Cfg::STAGES; // [2] S_i(t) computed
+  uint64_t* s_free = s_full + 2;             // [2] S_i(t) loaded by the softmax (SEP_P only)
+  uint64_t* p_full = s_free + 2;             // [2] P_i(t) stored
+  uint64_t* o_done = p_full + 2;             // [2] P_i V_t completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -76,10 +84,11 @@ __global__ void __launch_bounds__(320, 1)
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 2);  // released by both Q tiles' P V
+      mbar_init(&kv_empty[s], 2);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
     }
@@ -136,7 +145,7 @@ __global__ void __launch_bounds__(320, 1)
         const int s = t % Cfg::STAGES;
         const uint32_t k_addr = smem_u32(sKV + (2 * s) * Cfg::TILE_BYTES);
         const uint32_t qa = q_addr + uint32_t(i * Cfg::TILE_BYTES);
-        const uint32_t d_tmem = tmem + uint32_t(i * 128);
+        const uint32_t d_tmem = tmem + Cfg::s_col(i);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int j = kk >> 2, k4 = kk & 3;
@@ -149,8 +158,8 @@ __global__ void __launch_bounds__(320, 1)
       auto issue_pv = [&](int i, int t) {
         const int s = t % Cfg::STAGES;
         const uint32_t v_addr = smem_u32(sKV + (2 * s + 1) * Cfg::TILE_BYTES);
-        const uint32_t p_tmem = tmem + uint32_t(i * 128);
-        const uint32_t o_tmem = tmem + Cfg::O_COL + uint32_t(i * D);
+        const uint32_t p_tmem = tmem + Cfg::p_col(i);
+        const uint32_t o_tmem = tmem + Cfg::o_col(i);
 #pragma unroll
         for (int kk = 0; kk < Cfg::BN / 16; ++kk) {
           // 16 keys per step: P columns [8kk, 8kk+8) (two bf16 per column), V rows
@@ -159,19 +168,45 @@ __global__ void __launch_bounds__(320, 1)
           umma_ts(o_tmem, p_tmem + uint32_t(kk * 8), vd, idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&o_done[i]);
+        umma_commit(&kv_empty[s]);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      if constexpr (SCHED == 0) {
-        // Fixed order per key tile t: P_0 V_t, S_0 <- Q_0 K_{t+1}^T, P_1 V_t,
-        // S_1 <- Q_1 K_{t+1}^T, each step waiting (suspended in hardware) for its inputs.
-        ok = ok && mbar_wait(&k_full[0], 0, abort_flag);
-        if (ok) {
-          tc_fence_after();
-          issue_qk(0, 0);
-          issue_qk(1, 0);
-        }
-        for (int t = 0; ok && t < n_kv; ++t) {
-          const int s = t % Cfg::STAGES;
+      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        issue_qk(1, 0);
+      }
+      for (int t = 0; ok && t < n_kv; ++t) {
+        const int s = t % Cfg::STAGES;
+        const bool more = t + 1 < n_kv;
+        const int s1 = (t + 1) % Cfg::STAGES;
+        const uint32_t r1 = uint32_t((t + 1) / Cfg::STAGES);
+        if constexpr (Cfg::SEP_P) {
+          // S_i(t+1) as soon as the softmax has loaded S_i(t) and K_{t+1} is in smem,
+          // then P_i V_t as each softmax finishes.
+          if (more) {
+            if (!mbar_wait(&k_full[s1], r1 & 1, abort_flag)) break;
+            for (int i = 0; i < 2 && ok; ++i) {
+              if (!mbar_wait(&s_free[i], uint32_t(t) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_qk(i, t + 1);
+            }
+          }
+          if (!ok || !mbar_wait(&v_full[s], uint32_t(t / Cfg::STAGES) & 1, abort_flag)) break;
+          for (int i = 0; i < 2 && ok; ++i) {
+            if (!mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(i, t);
+          }
+        } else {
+          // P_i aliases S_i: S_i(t+1) may only be issued after P_i V_t (tcgen05.mma of
+          // one CTA execute in issue order).
           if (!mbar_wait(&v_full[s], uint32_t(t / Cfg::STAGES) & 1, abort_flag)) break;
           for (int i = 0; i < 2 && ok; ++i) {
             if (!mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag)) {
@@ -180,9 +215,8 @@ __global__ void __launch_bounds__(320, 1)
             }
             tc_fence_after();
             issue_pv(i, t);
-            umma_commit(&kv_empty[s]);
-            if (t + 1 < n_kv) {
-              if (!mbar_wait(&k_full[(t + 1) % Cfg::STAGES], uint32_t((t + 1) / Cfg::STAGES) & 1, abort_flag)) {
+            if (more) {
+              if (!mbar_wait(&k_full[s1], r1 & 1, abort_flag)) {
                 ok = false;
                 break;
               }
@@ -191,53 +225,6 @@ __global__ void __launch_bounds__(320, 1)
             }
           }
         }
-        ok = false;  // skip the readiness-driven loop below
-      }
-      // Readiness-driven schedule: serve the two Q tiles independently, in the order
-      // their inputs become ready, so their softmaxes drift apart and overlap the other
-      // tile's MMAs. Every wait here is a non-blocking probe (a tile waiting for a K/V
-      // stage still held by the other tile never blocks the other tile); an idle pass
-      // backs off briefly so the poll does not take issue slots from the softmax warps.
-      // Per tile i: next_qk[i] = next S_i = Q_i K_t^T to issue (needs K_t, and P_i V_{t-1}
-      // issued so S_i is free); next_pv[i] = next P_i V_t to issue (needs P_i(t) and V_t).
-      // A K/V stage is released once both tiles issued their P V on it (count 2).
-      int next_qk[2] = {0, 0}, next_pv[2] = {0, 0};
-      unsigned long long idle_since = clock64();
-      while (ok && (next_pv[0] < n_kv || next_pv[1] < n_kv)) {
-        bool progressed = false;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int tq = next_qk[i];
-          if (tq < n_kv && tq == next_pv[i] &&
-              mbar_test_wait(&k_full[tq % Cfg::STAGES], uint32_t(tq / Cfg::STAGES) & 1)) {
-            // S_i is rewritten by Q_i K_t^T after P_i V_{t-1}, issued earlier on this
-            // thread (tcgen05.mma of one CTA execute in issue order).
-            tc_fence_after();
-            issue_qk(i, tq);
-            next_qk[i] = tq + 1;
-            progressed = true;
-          }
-          const int tp = next_pv[i];
-          if (tp < next_qk[i] && mbar_test_wait(&p_full[i], uint32_t(tp) & 1) &&
-              mbar_test_wait(&v_full[tp % Cfg::STAGES], uint32_t(tp / Cfg::STAGES) & 1)) {
-            tc_fence_after();
-            issue_pv(i, tp);
-            umma_commit(&kv_empty[tp % Cfg::STAGES]);
-            next_pv[i] = tp + 1;
-            progressed = true;
-          }
-        }
-        if (progressed) {
-          idle_since = clock64();
-        } else if (*reinterpret_cast<volatile int*>(abort_flag)) {
-          ok = false;
-        } else if (clock64() - idle_since > LTX_WAIT_LIMIT_CYCLES) {
-          ltx_flag_error(LTX_DEVERR_MBAR_TIMEOUT);
-          *reinterpret_cast<volatile int*>(abort_flag) = 1;
-          ok = false;
-        } else if (SCHED == 2) {
-          __nanosleep(40);
-        }
       }
     }
   } else {
@@ -245,8 +232,9 @@ __global__ void __launch_bounds__(320, 1)
     const int qt = warp >> 2;                  // Q tile of this warpgroup
     const int row = (warp & 3) * 32 + lane;    // row within the tile == TMEM lane
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
-    const uint32_t s_tmem = tmem + uint32_t(qt * 128) + lane_off;
-    const uint32_t o_tmem = tmem + Cfg::O_COL + uint32_t(qt * D) + lane_off;
+    const uint32_t s_tmem = tmem + Cfg::s_col(qt) + lane_off;
+    const uint32_t p_tmem = tmem + Cfg::p_col(qt) + lane_off;
+    const uint32_t o_tmem = tmem + Cfg::o_col(qt) + lane_off;
     float m_ref = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int t = 0; t < n_kv; ++t) {
@@ -259,6 +247,11 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + uint32_t(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
       tmem_wait_ld();
+      if constexpr (Cfg::SEP_P) {
+        // S_i is in registers: let the MMA warp compute the next S_i now.
+        tc_fence_before();
+        mbar_arrive(&s_free[qt]);
+      }
       const int valid = Tk - t * Cfg::BN;
       if (valid < Cfg::BN) {
 #pragma unroll
@@ -282,6 +275,15 @@ __global__ void __launch_bounds__(320, 1)
         alpha = (t == 0) ? 0.f : ex2_approx(m_ref - m_new);
         m_ref = m_new;
       }
+      // Separate P: P_i V_{t-1} must be complete before P_i(t) overwrites P_i; by now it
+      // normally is.
+      if (Cfg::SEP_P && t > 0) {
+        if (!mbar_wait(&o_done[qt], uint32_t(t - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
       // x = s * scale_log2 - m_ref and the row sum in packed fp32x2 (two lanes per
       // instruction); on full tiles one pair in four takes the FMA-pipe exponential.
       const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
@@ -304,24 +306,21 @@ __global__ void __launch_bounds__(320, 1)
           rs2[(e >> 1) & 3] = f2_add(rs2[(e >> 1) & 3], f2_pack(p0, p1));
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
-        tmem_st16(s_tmem + uint32_t(c * 16), pk);
+        tmem_st16(p_tmem + uint32_t(c * 16), pk);
       }
-      float rs;
-      {
-        float a0, a1, b0, b1;
-        f2_unpack(f2_add(f2_add(rs2[0], rs2[1]), f2_add(rs2[2], rs2[3])), a0, a1);
-        (void)b0;
-        (void)b1;
-        rs = a0 + a1;
-      }
+      float r0, r1;
+      f2_unpack(f2_add(f2_add(rs2[0], rs2[1]), f2_add(rs2[2], rs2[3])), r0, r1);
       // Rescale this row's O accumulator when its reference max moved (warp-collective
       // TMEM access: the whole warp takes the branch, rows that did not move use 1).
+      // Done after the P store so that the S registers are dead.
       if (t > 0 && __any_sync(0xffffffffu, need)) {
-        if (!mbar_wait(&o_done[qt], uint32_t(t - 1) & 1, abort_flag)) {
-          ok = false;
-          break;
+        if (!Cfg::SEP_P) {
+          if (!mbar_wait(&o_done[qt], uint32_t(t - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
         }
-        tc_fence_after();
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
           uint32_t rr[32];
@@ -332,7 +331,7 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st32(o_tmem + uint32_t(c0), rr);
         }
       }
-      l_run = l_run * alpha + rs;
+      l_run = l_run * alpha + (r0 + r1);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[qt]);
@@ -434,10 +433,7 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const float* __restrict_
   for (int c = 0; c < D; ++c) op[c] = (acc[c] / l) * g;
 }
 
-// MMA-warp schedule of the bf16 attention kernel (ltx_attention_set_schedule).
-static int g_fmha_sched = 0;
-
-template <int D, int SCHED>
+template <int D>
 void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
                     int64_t ldo, int B, int64_t Tq, int64_t Tk, int H, float scale, const void* gate,
                     int64_t ld_gate, cudaStream_t s) {
@@ -446,7 +442,7 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   const CUtensorMap tq = make_tmap_bf16_2d(q, cols, uint64_t(B) * Tq, uint64_t(ldq), 64, 128);
   const CUtensorMap tk = make_tmap_bf16_2d(k, cols, uint64_t(B) * Tk, uint64_t(ldk), 64, 128);
   const CUtensorMap tv = make_tmap_bf16_2d(v, cols, uint64_t(B) * Tk, uint64_t(ldv), 64, 128);
-  auto kern = fmha_tc_kernel<D, SCHED>;
+  auto kern = fmha_tc_kernel<D>;
   static int attr_dev = -1;
   int dev = 0;
   LTX_CUDA(cudaGetDevice(&dev));
@@ -485,15 +481,10 @@ extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t 
     check_vec_ptr(k, "k");
     check_vec_ptr(v, "v");
     check_vec_ptr(o, "o");
-#define LTX_FMHA_CALL(DIM, SC) \
-  launch_fmha_tc<DIM, SC>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s)
-    const int sc = g_fmha_sched;
-    if (head_dim == 64) {
-      if (sc == 1) LTX_FMHA_CALL(64, 1); else if (sc == 2) LTX_FMHA_CALL(64, 2); else LTX_FMHA_CALL(64, 0);
-    } else {
-      if (sc == 1) LTX_FMHA_CALL(128, 1); else if (sc == 2) LTX_FMHA_CALL(128, 2); else LTX_FMHA_CALL(128, 0);
-    }
-#undef LTX_FMHA_CALL
+    if (head_dim == 64)
+      launch_fmha_tc<64>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
+    else
+      launch_fmha_tc<128>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
   } else {
     dim3 grid(unsigned((Tq + 127) / 128), unsigned(heads), unsigned(B));
     auto Qp = static_cast<const float*>(q);

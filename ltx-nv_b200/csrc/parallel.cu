@@ -70,10 +70,3 @@ extern "C" int ltx_sp_unpack(const void* src, int64_t rows, int parts, int w, vo
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
-
-extern "C" int ltx_attention_set_schedule(int schedule) {
-  LTX_API_BEGIN
-  LTX_REQUIRE(schedule >= 0 && schedule <= 2, "schedule must be 0, 1 or 2");
-  ltx::detail::g_fmha_sched = schedule;
-  LTX_API_END
-}
