@@ -37,7 +37,7 @@ struct FaCfg {
   static constexpr int BN = 128;                    // keys per K/V tile
   static constexpr int SUB = D / 64;                // 64-column (128-byte) sub-tiles per row
   static constexpr int TILE_BYTES = 128 * D * 2;    // one Q, K or V tile
-  static constexpr int STAGES = D == 64 ? 3 : 2;
+  static constexpr int STAGES = D == 64 ? 5 : 2;     // K/V ring: ~5 tile periods of TMA lead at d 64
   static constexpr int SMEM = TILE_BYTES * (2 + 2 * STAGES) + 512 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr bool SEP_P = D == 64;            // P in its own TMEM columns
@@ -275,38 +275,47 @@ __global__ void __launch_bounds__(320, 1)
         alpha = (t == 0) ? 0.f : ex2_approx(m_ref - m_new);
         m_ref = m_new;
       }
-      // Separate P: P_i V_{t-1} must be complete before P_i(t) overwrites P_i; by now it
-      // normally is.
-      if (Cfg::SEP_P && t > 0) {
-        if (!mbar_wait(&o_done[qt], uint32_t(t - 1) & 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
       // x = s * scale_log2 - m_ref and the row sum in packed fp32x2 (two lanes per
-      // instruction); on full tiles one pair in four takes the FMA-pipe exponential.
+      // instruction); on full tiles 3 pairs in 8 take the FMA-pipe exponential, which
+      // balances the special-function unit against the issue slots.
       const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
       const uint64_t nm2 = f2_pack(-m_ref, -m_ref);
       uint64_t rs2[4] = {0, 0, 0, 0};  // bit pattern of (0.f, 0.f)
       const bool full = valid >= Cfg::BN;
+      uint32_t pk[64];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float x0, x1, p0, p1;
           f2_unpack(f2_fma(f2_pack(sv[c * 32 + e], sv[c * 32 + e + 1]), sc2, nm2), x0, x1);
-          if (full && ((e & 7) == 6)) {
+          const int q = (e >> 1) & 7;
+          if (full && (q == 1 || q == 4 || q == 6)) {
             ex2_poly2(x0, x1, p0, p1);
           } else {
             p0 = ex2_approx(x0);
             p1 = ex2_approx(x1);
           }
           rs2[(e >> 1) & 3] = f2_add(rs2[(e >> 1) & 3], f2_pack(p0, p1));
-          pk[e >> 1] = pack_bf16x2(p0, p1);
+          pk[c * 16 + (e >> 1)] = pack_bf16x2(p0, p1);
         }
-        tmem_st16(p_tmem + uint32_t(c * 16), pk);
+        // Aliased P: S_i(t) is in registers and P_i V_{t-1} completed before Q_i K_t^T
+        // wrote S_i, so each chunk is stored at once.
+        if constexpr (!Cfg::SEP_P) tmem_st16(p_tmem + uint32_t(c * 16), *reinterpret_cast<uint32_t(*)[16]>(&pk[c * 16]));
+      }
+      if constexpr (Cfg::SEP_P) {
+        // Separate P: P_i V_{t-1} must be complete before P_i(t) overwrites P_i. Waiting
+        // only now, after the exponentials, leaves that MMA the whole softmax to finish.
+        if (t > 0) {
+          if (!mbar_wait(&o_done[qt], uint32_t(t - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tmem_st16(p_tmem + uint32_t(c * 16), *reinterpret_cast<uint32_t(*)[16]>(&pk[c * 16]));
       }
       float r0, r1;
       f2_unpack(f2_add(f2_add(rs2[0], rs2[1]), f2_add(rs2[2], rs2[3])), r0, r1);

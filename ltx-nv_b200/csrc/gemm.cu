@@ -31,8 +31,12 @@ struct TcCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr int VEC_BYTES = 3 * BN * 2;  // bias, gate table, row_vec of one tile
+  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + VEC_BYTES + 1024;
 };
+
+// Named barrier 1 over the 4 epilogue warps (128 threads) of gemm_tc_kernel.
+LTX_DEVICE void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 LTX_DEVICE uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -128,9 +132,20 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5 -> TMEM lane quadrants 2, 3, 0, 1.
+    // Epilogue warps 2..5 -> TMEM lane quadrants 2, 3, 0, 1; one accumulator row per
+    // thread.
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
+    const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+    // Per-column vectors of the epilogue (bias, gate table, row_vec), staged per tile.
+    __nv_bfloat16* s_vec = reinterpret_cast<__nv_bfloat16*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES);
+    const bool gres = epi.kind == LTX_EPI_GATE_RESIDUAL;
+    const __nv_bfloat16* gtab = (gres && epi.gate.table != nullptr) ? epi.gate.table + epi.gate.toff : nullptr;
+    const __nv_bfloat16* vsrc0 = epi.bias;
+    const __nv_bfloat16* vsrc2 = epi.kind == LTX_EPI_ROW_MASK_ADD ? epi.row_vec : nullptr;
+    // A thread whose wait failed keeps iterating (skipping the work) so that every
+    // epilogue thread reaches the same named barriers.
+    bool ok = true;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -138,61 +153,151 @@ __global__ void __launch_bounds__(192, 1)
       const int m0 = (tile / n_tiles) * kBM;
       const int n0 = (tile % n_tiles) * BN;
       const int64_t m = int64_t(m0) + row_in_tile;
-      const bool has_res = epi.kind == LTX_EPI_GATE_RESIDUAL && m < M;
-      // The residual does not depend on the accumulator: the first 64-column slab of it
-      // is loaded before waiting for the MMAs (overlapping the mainloop), and each later
-      // slab one slab ahead of its use.
-      uint4 rcur[8];
-      auto load_slab = [&](int c0, uint4 (&dst)[8]) {
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const int64_t col = int64_t(n0) + c0 + g * 8;
-          dst[g] = (col + 8 <= N) ? *reinterpret_cast<const uint4*>(epi.residual + m * epi.ld_res + col)
-                                  : make_uint4(0, 0, 0, 0);
-        }
-      };
-      if (has_res) load_slab(0, rcur);
-      if (!mbar_wait(&tfull[acc], u & 1, abort_flag)) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
       // sample / token of this row, once per tile (32-bit division; M < 2^31)
       const int64_t sb = int64_t(int(m) / int(epi.rows_per_batch));
       const int64_t stok = m - sb * epi.rows_per_batch;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 64) {
-        uint32_t rr[64];
-        tmem_ld32(tbase + uint32_t(c0), *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
-        tmem_ld32(tbase + uint32_t(c0 + 32), *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
-        uint4 rnext[8];
-        if (has_res && c0 + 64 < BN) load_slab(c0 + 64, rnext);
-        float res[64];
-        if (has_res) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            unpack_bf16x2(rcur[g].x, res[g * 8 + 0], res[g * 8 + 1]);
-            unpack_bf16x2(rcur[g].y, res[g * 8 + 2], res[g * 8 + 3]);
-            unpack_bf16x2(rcur[g].z, res[g * 8 + 4], res[g * 8 + 5]);
-            unpack_bf16x2(rcur[g].w, res[g * 8 + 6], res[g * 8 + 7]);
-            rcur[g] = rnext[g];
-          }
+      if (n0 + BN <= N) {
+        // Full-width tile. The per-column vectors go to shared memory once per tile;
+        // the per-row operands (residual, per-token gate) do not depend on the
+        // accumulator and are loaded one 32-column slab ahead of their use, the first
+        // slab before waiting for the MMAs. No global load is left between the TMEM
+        // read and the store of a slab.
+        epi_bar_sync();
+        for (int i = et; i < 3 * (BN / 8); i += 128) {
+          const int w = i / (BN / 8), c = (i - w * (BN / 8)) * 8;
+          const __nv_bfloat16* src = w == 0 ? vsrc0 : (w == 1 ? gtab : vsrc2);
+          if (src != nullptr)
+            *reinterpret_cast<uint4*>(s_vec + w * BN + c) = *reinterpret_cast<const uint4*>(src + n0 + c);
         }
-        tmem_wait_ld();
-        if (m < M) {
+        epi_bar_sync();
+        const bool live = m < M;
+        const __nv_bfloat16* resp = (gres && live) ? epi.residual + m * epi.ld_res + n0 : nullptr;
+        const __nv_bfloat16* gmod = (gres && live && epi.gate.mod != nullptr)
+                                        ? epi.gate.mod + sb * epi.gate.ldb + stok * epi.gate.ldt + epi.gate.moff + n0
+                                        : nullptr;
+        const float rmask = (epi.kind == LTX_EPI_ROW_MASK_ADD && live) ? epi.row_mask[m] : 0.f;
+        auto load_row = [&](int c0, uint4 (&r)[4], uint4 (&g)[4]) {
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            const int64_t col = int64_t(n0) + c0 + g * 8;
-            if (col + 8 <= N) {
+          for (int j = 0; j < 4; ++j) {
+            r[j] = resp != nullptr ? *reinterpret_cast<const uint4*>(resp + c0 + j * 8) : make_uint4(0, 0, 0, 0);
+            g[j] = gmod != nullptr ? *reinterpret_cast<const uint4*>(gmod + c0 + j * 8) : make_uint4(0, 0, 0, 0);
+          }
+        };
+        uint4 rc[4], gc[4];
+        load_row(0, rc, gc);
+        if (ok && !mbar_wait(&tfull[acc], u & 1, abort_flag)) ok = false;
+        if (!ok) continue;
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
+        __nv_bfloat16* crow = C + m * ldc + n0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t rr[32];
+          tmem_ld32(tbase + uint32_t(c0), rr);
+          uint4 rn[4], gn[4];
+          if (c0 + 32 < BN) load_row(c0 + 32, rn, gn);
+          tmem_wait_ld();
+          if (live) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int cl = c0 + j * 8;
               float v[8];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(rr[g * 8 + e]);
-              epilogue8<__nv_bfloat16>(epi, m, col, v, has_res ? &res[g * 8] : nullptr, sb, stok);
-              st8<__nv_bfloat16>(C + m * ldc + col, v);
-            } else {
+              for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(rr[j * 8 + e]);
+              if (vsrc0 != nullptr) {
+                float b[8];
+                ld8<__nv_bfloat16>(s_vec + cl, b);
 #pragma unroll
-              for (int e = 0; e < 8; ++e)
-                if (col + e < N)
-                  C[m * ldc + col + e] =
-                      __float2bfloat16_rn(epilogue1<__nv_bfloat16>(epi, m, col + e, __uint_as_float(rr[g * 8 + e])));
+                for (int e = 0; e < 8; ++e) v[e] += b[e];
+              }
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = round_bf16(v[e]);
+              if (epi.kind == LTX_EPI_GELU_TANH) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = gelu_act<__nv_bfloat16>(v[e]);
+              } else if (epi.kind == LTX_EPI_SILU) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = silu_f(v[e]);
+              } else if (gres) {
+                // ltx_kernels.cuh epilogue8: residual + round(round(acc + bias) * gate),
+                // gate = round(table + mod).
+                float g[8], r[8];
+                if (epi.gate.on) {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) g[e] = 0.f;
+                  if (gtab != nullptr) {
+                    float a[8];
+                    ld8<__nv_bfloat16>(s_vec + BN + cl, a);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) g[e] += a[e];
+                  }
+                  if (gmod != nullptr) {
+                    unpack_bf16x2(gc[j].x, r[0], r[1]);
+                    unpack_bf16x2(gc[j].y, r[2], r[3]);
+                    unpack_bf16x2(gc[j].z, r[4], r[5]);
+                    unpack_bf16x2(gc[j].w, r[6], r[7]);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) g[e] += r[e];
+                  }
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) g[e] = round_bf16(g[e]);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) g[e] = 1.f;
+                }
+                unpack_bf16x2(rc[j].x, r[0], r[1]);
+                unpack_bf16x2(rc[j].y, r[2], r[3]);
+                unpack_bf16x2(rc[j].z, r[4], r[5]);
+                unpack_bf16x2(rc[j].w, r[6], r[7]);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = r[e] + round_bf16(v[e] * g[e]);
+              } else if (epi.kind == LTX_EPI_ROW_MASK_ADD && rmask > 0.f) {
+                float a[8];
+                ld8<__nv_bfloat16>(s_vec + 2 * BN + cl, a);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] += a[e];
+              }
+              st8<__nv_bfloat16>(crow + cl, v);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            rc[j] = rn[j];
+            gc[j] = gn[j];
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        continue;
+      }
+      // Ragged last column tile (N not a multiple of BN): generic epilogue per 8 columns.
+      if (ok && !mbar_wait(&tfull[acc], u & 1, abort_flag)) ok = false;
+      if (!ok) continue;
+      tc_fence_after();
+      {
+        const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += 32) {
+          uint32_t rr[32];
+          tmem_ld32(tbase + uint32_t(c0), rr);
+          tmem_wait_ld();
+          if (m < M) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int64_t col = int64_t(n0) + c0 + g * 8;
+              if (col + 8 <= N) {
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(rr[g * 8 + e]);
+                epilogue8<__nv_bfloat16>(epi, m, col, v, nullptr, sb, stok);
+                st8<__nv_bfloat16>(C + m * ldc + col, v);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  if (col + e < N)
+                    C[m * ldc + col + e] =
+                        __float2bfloat16_rn(epilogue1<__nv_bfloat16>(epi, m, col + e, __uint_as_float(rr[g * 8 + e])));
+              }
             }
           }
         }

@@ -336,13 +336,14 @@ LTX_DEVICE float fmax3(float a, float b, float c) {
 // f in [-1/2, 1/2], 2^f by a cubic whose coefficients were fitted to minimise the
 // relative error on that interval (max relative error 7.6e-5), and 2^n added into the
 // exponent field. Valid for -126 <= x <= 127; callers pass finite x <= 8.
+// The shifted sum t = x + 1.5*2^23 has the bit pattern 0x4B400000 + n, and
+// 0x4B400000 << 23 wraps to 0 in 32 bits, so (bits(t) << 23) == (n << 23).
 LTX_DEVICE float ex2_poly(float x) {
   x = fmaxf(x, -126.f);
   const float t = x + 12582912.f;
-  const int n = __float_as_int(t) - 0x4B400000;
   const float f = x - (t - 12582912.f);
   const float p = fmaf(fmaf(fmaf(0.0551708005f, f, 0.242609262f), f, 0.693260968f), f, 0.999928176f);
-  return __int_as_float(__float_as_int(p) + (n << 23));
+  return __int_as_float(__float_as_int(p) + int(uint32_t(__float_as_int(t)) << 23));
 }
 
 // The same for two values with packed fp32x2 arithmetic.
@@ -359,8 +360,8 @@ LTX_DEVICE void ex2_poly2(float x0, float x1, float& y0, float& y1) {
   float t0, t1, p0, p1;
   f2_unpack(t, t0, t1);
   f2_unpack(p, p0, p1);
-  y0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - 0x4B400000) << 23));
-  y1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - 0x4B400000) << 23));
+  y0 = __int_as_float(__float_as_int(p0) + int(uint32_t(__float_as_int(t0)) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + int(uint32_t(__float_as_int(t1)) << 23));
 }
 LTX_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
