@@ -26,6 +26,8 @@
 // stored.
 //
 // fp32 path: CUDA-core online-softmax kernel, one query per thread (accuracy mode).
+#include <algorithm>
+
 #include "ltx_kernels.cuh"
 
 namespace ltx {
@@ -37,7 +39,7 @@ struct FaCfg {
   static constexpr int BN = 128;                    // keys per K/V tile
   static constexpr int SUB = D / 64;                // 64-column (128-byte) sub-tiles per row
   static constexpr int TILE_BYTES = 128 * D * 2;    // one Q, K or V tile
-  static constexpr int STAGES = D == 64 ? 5 : 2;     // K/V ring: ~5 tile periods of TMA lead at d 64
+  static constexpr int STAGES = D == 64 ? 3 : 2;
   static constexpr int SMEM = TILE_BYTES * (2 + 2 * STAGES) + 512 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr bool SEP_P = D == 64;            // P in its own TMEM columns
@@ -276,8 +278,7 @@ __global__ void __launch_bounds__(320, 1)
         m_ref = m_new;
       }
       // x = s * scale_log2 - m_ref and the row sum in packed fp32x2 (two lanes per
-      // instruction); on full tiles 3 pairs in 8 take the FMA-pipe exponential, which
-      // balances the special-function unit against the issue slots.
+      // instruction); on full tiles one pair in four takes the FMA-pipe exponential.
       const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
       const uint64_t nm2 = f2_pack(-m_ref, -m_ref);
       uint64_t rs2[4] = {0, 0, 0, 0};  // bit pattern of (0.f, 0.f)
@@ -290,7 +291,7 @@ __global__ void __launch_bounds__(320, 1)
           float x0, x1, p0, p1;
           f2_unpack(f2_fma(f2_pack(sv[c * 32 + e], sv[c * 32 + e + 1]), sc2, nm2), x0, x1);
           const int q = (e >> 1) & 7;
-          if (full && (q == 1 || q == 4 || q == 6)) {
+          if (full && (q & 3) == 3) {
             ex2_poly2(x0, x1, p0, p1);
           } else {
             p0 = ex2_approx(x0);
@@ -385,6 +386,254 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 // ---------------------------------------------------------------------------------
+// Short-context attention (Tk <= 128: all keys in one tile), the cross-attention to the
+// text context. Persistent CTAs walk a contiguous range of tasks (sample, head, 128-row
+// Q tile), ordered so that consecutive tasks share (sample, head): K and V of a
+// (sample, head) are loaded once per run of tasks (two generations double-buffered),
+// Q tiles are double-buffered, and the two softmax warpgroups take alternate tasks, so
+// the output of task j is normalised and stored while task j+1 is in its softmax and
+// the tensor core and TMA work ahead. Same roles as fmha_tc_kernel: warps 0-3 and 4-7
+// softmax + epilogue, warp 8 TMA, warp 9 MMA.
+// TMEM: S_w at [128 w, 128 w + 128) with P_w written over its first 64 columns,
+// O_w at [256 + D w, 256 + D w + D).
+// ---------------------------------------------------------------------------------
+template <int D>
+struct Kv1Cfg {
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int SUB = D / 64;
+  static constexpr int SMEM = TILE * 2 + TILE * 4 + 512 + 1024;  // Q x 2, (K, V) x 2
+  static constexpr uint32_t TMEM_COLS = 512;
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    fmha_kv1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
+                    int Tk, int H, int n_qt, int64_t n_tasks, float scale_log2,
+                    const __nv_bfloat16* __restrict__ gate, int64_t ld_gate) {
+  using Cfg = Kv1Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = fa_align1024(smem_raw);
+  uint8_t* sQ = smem;                        // slot w at sQ + w * TILE
+  uint8_t* sKV = smem + 2 * Cfg::TILE;       // generation buffer g: K at sKV + 2g*TILE, V at +TILE
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * Cfg::TILE);
+  uint64_t* q_full = bars;          // [2]
+  uint64_t* q_empty = bars + 2;     // [2]
+  uint64_t* kv_full = bars + 4;     // [2]
+  uint64_t* kv_empty = bars + 6;    // [2]
+  uint64_t* s_full = bars + 8;      // [2]
+  uint64_t* p_full = bars + 10;     // [2]
+  uint64_t* o_full = bars + 12;     // [2]
+  uint64_t* slot_free = bars + 14;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int64_t t0 = int64_t(blockIdx.x) * n_tasks / gridDim.x;
+  const int n_local = int(int64_t(blockIdx.x + 1) * n_tasks / gridDim.x - t0);
+  // task -> (sample, head, Q tile); bh = sample * H + head
+  auto task_bh = [&](int j) { return int((t0 + j) / n_qt); };
+  auto task_qt = [&](int j) { return int((t0 + j) % n_qt); };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&slot_free[i], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int gen = -1, prev_bh = -1;
+      for (int j = 0; j < n_local; ++j) {
+        const int bh = task_bh(j);
+        const int b = bh / H, h = bh - b * H;
+        if (bh != prev_bh) {
+          ++gen;
+          prev_bh = bh;
+          const int kb = gen & 1;
+          if (gen >= 2 && !mbar_wait(&kv_empty[kb], uint32_t((gen >> 1) - 1) & 1, abort_flag)) break;
+          uint8_t* sk = sKV + (2 * kb) * Cfg::TILE;
+          mbar_arrive_expect_tx(&kv_full[kb], 2 * Cfg::TILE);
+#pragma unroll
+          for (int jj = 0; jj < Cfg::SUB; ++jj) {
+            tma_load_2d(sk + jj * (Cfg::TILE / Cfg::SUB), &tmK, &kv_full[kb], h * D + 64 * jj, b * Tk);
+            tma_load_2d(sk + Cfg::TILE + jj * (Cfg::TILE / Cfg::SUB), &tmV, &kv_full[kb], h * D + 64 * jj, b * Tk);
+          }
+        }
+        const int w = j & 1;
+        if (j >= 2 && !mbar_wait(&q_empty[w], uint32_t((j >> 1) - 1) & 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&q_full[w], Cfg::TILE);
+#pragma unroll
+        for (int jj = 0; jj < Cfg::SUB; ++jj)
+          tma_load_2d(sQ + w * Cfg::TILE + jj * (Cfg::TILE / Cfg::SUB), &tmQ, &q_full[w], h * D + 64 * jj,
+                      b * Tq + task_qt(j) * 128);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------ MMA issuer ---------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, 0);
+      constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 1);
+      int gen = -1, prev_bh = -1;
+      bool ok = true;
+      for (int j = 0; ok && j <= n_local; ++j) {
+        const int gen_prev = gen;  // generation of task j - 1
+        if (j < n_local) {
+          const int bh = task_bh(j);
+          const int w = j & 1;
+          if (bh != prev_bh) {
+            ++gen;
+            prev_bh = bh;
+            if (!mbar_wait(&kv_full[gen & 1], uint32_t(gen >> 1) & 1, abort_flag)) break;
+          }
+          if (!mbar_wait(&q_full[w], uint32_t(j >> 1) & 1, abort_flag)) break;
+          // S_w / P_w / O_w are free once the softmax warpgroup finished task j - 2.
+          if (j >= 2 && !mbar_wait(&slot_free[w], uint32_t((j >> 1) - 1) & 1, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t qa = smem_u32(sQ + w * Cfg::TILE);
+          const uint32_t ka = smem_u32(sKV + (2 * (gen & 1)) * Cfg::TILE);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = uint32_t((kk >> 2) * (Cfg::TILE / Cfg::SUB) + (kk & 3) * 32);
+            umma_ss(tmem + uint32_t(128 * w), umma_desc_sw128(qa + off, 16, 1024),
+                    umma_desc_sw128(ka + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[w]);
+          umma_commit(&q_empty[w]);
+        }
+        if (j >= 1) {
+          const int jp = j - 1, wp = jp & 1;
+          if (!mbar_wait(&p_full[wp], uint32_t(jp >> 1) & 1, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t va = smem_u32(sKV + (2 * (gen_prev & 1) + 1) * Cfg::TILE);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t vd = umma_desc_sw128(va + uint32_t(kk * 2048), Cfg::TILE / Cfg::SUB, 1024);
+            umma_ts(tmem + uint32_t(256 + D * wp), tmem + uint32_t(128 * wp + kk * 8), vd, idesc_o, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&o_full[wp]);
+          // last task of its generation: K / V buffer free once this completes
+          if (j == n_local || gen != gen_prev) umma_commit(&kv_empty[gen_prev & 1]);
+        }
+      }
+    }
+  } else {
+    // --------------------- softmax / normalisation / store ---------------------
+    const int w = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+    const uint32_t s_tmem = tmem + uint32_t(128 * w) + lane_off;
+    const uint32_t o_tmem = tmem + uint32_t(256 + D * w) + lane_off;
+    for (int j = w; j < n_local; j += 2) {
+      const int bh = task_bh(j);
+      const int b = bh / H, h = bh - b * H;
+      const uint32_t par = uint32_t(j >> 1) & 1;
+      if (!mbar_wait(&s_full[w], par, abort_flag)) break;
+      tc_fence_after();
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + uint32_t(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+      tmem_wait_ld();
+      if (Tk < 128) {
+#pragma unroll
+        for (int e = 0; e < 128; ++e)
+          if (e >= Tk) sv[e] = -INFINITY;
+      }
+      float m8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m8[e] = sv[e];
+#pragma unroll
+      for (int e = 8; e < 128; e += 16)
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) m8[jj] = fmax3(m8[jj], sv[e + jj], sv[e + 8 + jj]);
+      const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+      const float m_ref = mx * scale_log2;
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
+      const uint64_t nm2 = f2_pack(-m_ref, -m_ref);
+      uint64_t rs2[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(sv[c * 32 + e], sv[c * 32 + e + 1]), sc2, nm2), x0, x1);
+          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          rs2[(e >> 1) & 3] = f2_add(rs2[(e >> 1) & 3], f2_pack(p0, p1));
+          pk[e >> 1] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(s_tmem + uint32_t(c * 16), pk);
+      }
+      float r0, r1;
+      f2_unpack(f2_add(f2_add(rs2[0], rs2[1]), f2_add(rs2[2], rs2[3])), r0, r1);
+      const float l_run = r0 + r1;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[w]);
+      // gate logit load overlaps the P V MMA
+      const int qi = task_qt(j) * 128 + row;
+      const int64_t orow = int64_t(b) * Tq + qi;
+      float g = 1.f;
+      if (gate != nullptr && qi < Tq) {
+        const float lg = __bfloat162float(gate[orow * ld_gate + h]);
+        const float sg = round_bf16(1.f / (1.f + expf(-lg)));
+        g = round_bf16(2.f * sg);
+      }
+      const float inv_l = 1.f / l_run;
+      if (!mbar_wait(&o_full[w], par, abort_flag)) break;
+      tc_fence_after();
+      __nv_bfloat16* op = O + orow * ldo + int64_t(h) * D;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t rr[32];
+        tmem_ld32(o_tmem + uint32_t(c0), rr);
+        tmem_wait_ld();
+        if (qi < Tq) {
+#pragma unroll
+          for (int e8 = 0; e8 < 32; e8 += 8) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float o = round_bf16(__uint_as_float(rr[e8 + e]) * inv_l);
+              v[e] = gate != nullptr ? o * g : o;
+            }
+            st8<__nv_bfloat16>(op + c0 + e8, v);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&slot_free[w]);
+    }
+  }
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------
 // fp32 attention on CUDA cores: one query per thread, K/V tiles of 32 keys in smem.
 // ---------------------------------------------------------------------------------
 template <int D>
@@ -465,6 +714,32 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
                                     static_cast<const __nv_bfloat16*>(gate), ld_gate), ltx::note_launch();
 }
 
+template <int D>
+void launch_fmha_kv1(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
+                     int64_t ldo, int B, int64_t Tq, int64_t Tk, int H, float scale, const void* gate,
+                     int64_t ld_gate, cudaStream_t s) {
+  using Cfg = Kv1Cfg<D>;
+  const uint64_t cols = uint64_t(H) * D;
+  const CUtensorMap tq = make_tmap_bf16_2d(q, cols, uint64_t(B) * Tq, uint64_t(ldq), 64, 128);
+  const CUtensorMap tk = make_tmap_bf16_2d(k, cols, uint64_t(B) * Tk, uint64_t(ldk), 64, 128);
+  const CUtensorMap tv = make_tmap_bf16_2d(v, cols, uint64_t(B) * Tk, uint64_t(ldv), 64, 128);
+  auto kern = fmha_kv1_kernel<D>;
+  static int attr_dev = -1;
+  int dev = 0;
+  LTX_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    attr_dev = dev;
+  }
+  const int n_qt = int((Tq + 127) / 128);
+  const int64_t n_tasks = int64_t(B) * H * n_qt;
+  const int grid = int(std::min<int64_t>(n_tasks, num_sms()));
+  const float scale_log2 = scale * 1.4426950408889634f;
+  kern<<<grid, 320, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), H, n_qt,
+                                    n_tasks, scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate),
+      ltx::note_launch();
+}
+
 }  // namespace detail
 }  // namespace ltx
 
@@ -490,7 +765,12 @@ extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t 
     check_vec_ptr(k, "k");
     check_vec_ptr(v, "v");
     check_vec_ptr(o, "o");
-    if (head_dim == 64)
+    // one key tile (the text context): persistent short-context kernel
+    if (Tk <= 128 && head_dim == 64)
+      launch_fmha_kv1<64>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
+    else if (Tk <= 128)
+      launch_fmha_kv1<128>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
+    else if (head_dim == 64)
       launch_fmha_tc<64>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
     else
       launch_fmha_tc<128>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
