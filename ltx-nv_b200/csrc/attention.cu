@@ -1,12 +1,14 @@
 // Attention core softmax(Q K^T * scale) V with the per-(token, head) output gate
 // 2*sigmoid(logit) fused in (ltx_nn.py:22-26 sdpa, 227-235 gating).
 //
-// bf16 path: one CTA per (256 queries, head, sample) = two 128-row Q tiles, 10 warps:
+// bf16 path: one CTA per (256 queries, head, sample) = two 128-row Q tiles, 11 warps:
 //   warps 0-3   softmax of Q tile 0 (one query row per thread = TMEM lane)
 //   warps 4-7   softmax of Q tile 1
 //   warp 8      TMA producer: both Q tiles once, then K and V tiles of 128 keys into a
 //               STAGES-deep ring
-//   warp 9      tcgen05.mma issuer and TMEM owner
+//   warp 9      tcgen05.mma issuer of Q tile 0, TMEM owner
+//   warp 10     tcgen05.mma issuer of Q tile 1 (on another SM sub-partition, so the
+//               two issue streams and their waits overlap)
 // S_i = Q_i K^T lands in TMEM as fp32; the softmax of tile i writes P_i as packed bf16;
 // O_i accumulates P_i V over all key tiles in TMEM (A operand read from TMEM, V as an
 // MN-major 128B-swizzled smem operand).
@@ -14,9 +16,9 @@
 // TMEM (512 columns):
 //   head_dim 64:  S_0, S_1 at [0,128), [128,256); P_0, P_1 at [256,320), [320,384);
 //                 O_0, O_1 at [384,448), [448,512). P has its own columns, so the softmax
-//                 releases S_i as soon as it has loaded it and the MMA warp computes
-//                 S_i(t+1) = Q_i K_{t+1}^T while the softmax of key tile t still runs: the
-//                 MMA round trip is off the softmax's critical path.
+//                 releases S_i as soon as it has loaded it and the issuer computes
+//                 S_i(t+2) = Q_i K_{t+2}^T right after P_i V_t, while the softmax of key
+//                 tile t+1 runs: the MMA round trip is off the softmax's critical path.
 //   head_dim 128: S_i at [128 i, 128 i + 128) with P_i written over its first 64 columns,
 //                 O_i at [256 + 128 i, ...); S_i(t+1) is issued after P_i V_t.
 // Lazy rescaling: each row keeps a reference max m_ref and only moves it (rescaling its
@@ -39,7 +41,7 @@ struct FaCfg {
   static constexpr int BN = 128;                    // keys per K/V tile
   static constexpr int SUB = D / 64;                // 64-column (128-byte) sub-tiles per row
   static constexpr int TILE_BYTES = 128 * D * 2;    // one Q, K or V tile
-  static constexpr int STAGES = D == 64 ? 3 : 2;
+  static constexpr int STAGES = D == 64 ? 5 : 2;  // d 64: K is needed two tiles ahead
   static constexpr int SMEM = TILE_BYTES * (2 + 2 * STAGES) + 512 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr bool SEP_P = D == 64;            // P in its own TMEM columns
@@ -54,8 +56,8 @@ LTX_DEVICE uint8_t* fa_align1024(uint8_t* p) {
 }
 
 template <int D>
-// 10 warps: three share one SM sub-partition's 16K registers, so <= 168 per thread.
-__global__ void __launch_bounds__(320, 1)
+// 11 warps: three share one SM sub-partition's 16K registers, so <= 168 per thread.
+__global__ void __launch_bounds__(352, 1)
     fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
                    int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate) {
@@ -137,31 +139,34 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_2d(sv + j * (Cfg::TILE_BYTES / Cfg::SUB), &tmV, &v_full[s], col0 + 64 * j, row);
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------ MMA issuer ---------------------------------
+  } else if (warp == 9 || warp == 10) {
+    // ------------------------- MMA issuers (one per Q tile) ------------------------
+    // Warp 9 issues every MMA of Q tile 0, warp 10 every MMA of Q tile 1: the two
+    // chains interleave in the tensor pipe, so one issuer's waits and bookkeeping
+    // overlap the other's MMAs.
+    const int i = warp - 9;
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, 128, 0);
       constexpr uint32_t idesc_o = umma_idesc_bf16(128, D, 1);
-      const uint32_t q_addr = smem_u32(sQ);
-      auto issue_qk = [&](int i, int t) {
+      const uint32_t qa = smem_u32(sQ) + uint32_t(i * Cfg::TILE_BYTES);
+      const uint32_t s_tmem = tmem + Cfg::s_col(i);
+      const uint32_t p_tmem = tmem + Cfg::p_col(i);
+      const uint32_t o_tmem = tmem + Cfg::o_col(i);
+      auto issue_qk = [&](int t) {
         const int s = t % Cfg::STAGES;
         const uint32_t k_addr = smem_u32(sKV + (2 * s) * Cfg::TILE_BYTES);
-        const uint32_t qa = q_addr + uint32_t(i * Cfg::TILE_BYTES);
-        const uint32_t d_tmem = tmem + Cfg::s_col(i);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int j = kk >> 2, k4 = kk & 3;
           const uint32_t off = uint32_t(j * (Cfg::TILE_BYTES / Cfg::SUB) + k4 * 32);
-          umma_ss(d_tmem, umma_desc_sw128(qa + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024), idesc_s,
+          umma_ss(s_tmem, umma_desc_sw128(qa + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024), idesc_s,
                   kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[i]);
       };
-      auto issue_pv = [&](int i, int t) {
+      auto issue_pv = [&](int t) {
         const int s = t % Cfg::STAGES;
         const uint32_t v_addr = smem_u32(sKV + (2 * s + 1) * Cfg::TILE_BYTES);
-        const uint32_t p_tmem = tmem + Cfg::p_col(i);
-        const uint32_t o_tmem = tmem + Cfg::o_col(i);
 #pragma unroll
         for (int kk = 0; kk < Cfg::BN / 16; ++kk) {
           // 16 keys per step: P columns [8kk, 8kk+8) (two bf16 per column), V rows
@@ -170,61 +175,54 @@ __global__ void __launch_bounds__(320, 1)
           umma_ts(o_tmem, p_tmem + uint32_t(kk * 8), vd, idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&o_done[i]);
-        umma_commit(&kv_empty[s]);
+        umma_commit(&kv_empty[s]);  // count 2: both Q tiles' P V of this stage
       };
       bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
       if (ok) {
         tc_fence_after();
-        issue_qk(0, 0);
-        issue_qk(1, 0);
+        issue_qk(0);
       }
-      for (int t = 0; ok && t < n_kv; ++t) {
-        const int s = t % Cfg::STAGES;
-        const bool more = t + 1 < n_kv;
-        const int s1 = (t + 1) % Cfg::STAGES;
-        const uint32_t r1 = uint32_t((t + 1) / Cfg::STAGES);
-        if constexpr (Cfg::SEP_P) {
-          // S_i(t+1) as soon as the softmax has loaded S_i(t) and K_{t+1} is in smem,
-          // then P_i V_t as each softmax finishes.
-          if (more) {
-            if (!mbar_wait(&k_full[s1], r1 & 1, abort_flag)) break;
-            for (int i = 0; i < 2 && ok; ++i) {
-              if (!mbar_wait(&s_free[i], uint32_t(t) & 1, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_qk(i, t + 1);
-            }
-          }
-          if (!ok || !mbar_wait(&v_full[s], uint32_t(t / Cfg::STAGES) & 1, abort_flag)) break;
-          for (int i = 0; i < 2 && ok; ++i) {
-            if (!mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag)) {
-              ok = false;
-              break;
-            }
+      if constexpr (Cfg::SEP_P) {
+        // Order per key tile t: P_i V_t, then Q_i K_{t+2}^T. S_i is computed two tiles
+        // ahead (S_i is free as soon as the softmax has loaded it), so the softmax
+        // never waits for its next S, and P_i V_t runs while the softmax of tile t+1
+        // computes its exponentials.
+        if (ok && n_kv > 1) {
+          ok = mbar_wait(&k_full[1 % Cfg::STAGES], uint32_t(1 / Cfg::STAGES) & 1, abort_flag) &&
+               mbar_wait(&s_free[i], 0, abort_flag);
+          if (ok) {
             tc_fence_after();
-            issue_pv(i, t);
+            issue_qk(1);
           }
-        } else {
-          // P_i aliases S_i: S_i(t+1) may only be issued after P_i V_t (tcgen05.mma of
-          // one CTA execute in issue order).
-          if (!mbar_wait(&v_full[s], uint32_t(t / Cfg::STAGES) & 1, abort_flag)) break;
-          for (int i = 0; i < 2 && ok; ++i) {
-            if (!mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag)) {
-              ok = false;
+        }
+        for (int t = 0; ok && t < n_kv; ++t) {
+          const int t2 = t + 2;
+          if (!mbar_wait(&v_full[t % Cfg::STAGES], uint32_t(t / Cfg::STAGES) & 1, abort_flag) ||
+              !mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag))
+            break;
+          tc_fence_after();
+          issue_pv(t);
+          if (t2 < n_kv) {
+            if (!mbar_wait(&k_full[t2 % Cfg::STAGES], uint32_t(t2 / Cfg::STAGES) & 1, abort_flag) ||
+                !mbar_wait(&s_free[i], uint32_t(t + 1) & 1, abort_flag))
               break;
-            }
             tc_fence_after();
-            issue_pv(i, t);
-            if (more) {
-              if (!mbar_wait(&k_full[s1], r1 & 1, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_qk(i, t + 1);
-            }
+            issue_qk(t2);
+          }
+        }
+      } else {
+        // P_i aliases S_i: S_i(t+1) may only be issued after P_i V_t (tcgen05.mma of
+        // one thread execute in issue order).
+        for (int t = 0; ok && t < n_kv; ++t) {
+          if (!mbar_wait(&v_full[t % Cfg::STAGES], uint32_t(t / Cfg::STAGES) & 1, abort_flag) ||
+              !mbar_wait(&p_full[i], uint32_t(t) & 1, abort_flag))
+            break;
+          tc_fence_after();
+          issue_pv(t);
+          if (t + 1 < n_kv) {
+            if (!mbar_wait(&k_full[(t + 1) % Cfg::STAGES], uint32_t((t + 1) / Cfg::STAGES) & 1, abort_flag)) break;
+            tc_fence_after();
+            issue_qk(t + 1);
           }
         }
       }
@@ -278,7 +276,8 @@ __global__ void __launch_bounds__(320, 1)
         m_ref = m_new;
       }
       // x = s * scale_log2 - m_ref and the row sum in packed fp32x2 (two lanes per
-      // instruction); on full tiles one pair in four takes the FMA-pipe exponential.
+      // instruction); on full tiles 9 pairs in 32 take the FMA-pipe exponential (one in
+      // four, plus one: the measured optimum of this loop's schedule).
       const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
       const uint64_t nm2 = f2_pack(-m_ref, -m_ref);
       uint64_t rs2[4] = {0, 0, 0, 0};  // bit pattern of (0.f, 0.f)
@@ -291,7 +290,7 @@ __global__ void __launch_bounds__(320, 1)
           float x0, x1, p0, p1;
           f2_unpack(f2_fma(f2_pack(sv[c * 32 + e], sv[c * 32 + e + 1]), sc2, nm2), x0, x1);
           const int q = (e >> 1) & 7;
-          if (full && (q & 3) == 3) {
+          if (full && ((q & 3) == 3 || (c == 1 && q == 1))) {
             ex2_poly2(x0, x1, p0, p1);
           } else {
             p0 = ex2_approx(x0);
@@ -710,7 +709,7 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   }
   dim3 grid(unsigned((Tq + 2 * Cfg::BM - 1) / (2 * Cfg::BM)), unsigned(H), unsigned(B));
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, 320, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), scale_log2,
+  kern<<<grid, 352, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), scale_log2,
                                     static_cast<const __nv_bfloat16*>(gate), ld_gate), ltx::note_launch();
 }
 

@@ -138,6 +138,20 @@ LTX_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// The same with a suspend-time hint (ns): the thread sleeps until the phase completes
+// or the hint expires instead of polling, leaving the issue slots of its SM
+// sub-partition to the warps that do the work.
+LTX_DEVICE bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 // Non-blocking probe (test_wait returns at once; try_wait may suspend the thread for
 // a while before reporting "not yet", which stalls a warp that polls several barriers).
 LTX_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
@@ -158,7 +172,7 @@ LTX_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if (abort != nullptr && *abort) return false;
     if (clock64() - t0 > LTX_WAIT_LIMIT_CYCLES) {
       ltx_flag_error(LTX_DEVERR_MBAR_TIMEOUT);
