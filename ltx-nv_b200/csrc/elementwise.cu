@@ -7,6 +7,9 @@
 // shared-memory exchange. Arithmetic is fp32; the storage dtype's rounding is applied
 // at the points where the reference's op-by-op PyTorch code rounds (each torch op on a
 // bf16 tensor returns a rounded bf16 tensor).
+#include <algorithm>
+#include <type_traits>
+
 #include "ltx_kernels.cuh"
 
 namespace ltx {
@@ -81,6 +84,106 @@ __global__ void __launch_bounds__(1024) norm_modulate_kernel(const T* __restrict
   }
 }
 
+// Fast path of the same op for bf16 rows of D = 256 * NC with per-sample (or no)
+// modulation: one warp per row, no block-wide reduction. A CTA's rows all belong to
+// one sample, so round(1 + scale) and round(shift) are built once per CTA in shared
+// memory; a row then costs its load, its store and three bf16 roundings per element
+// (two of them packed two to an instruction). Same rounding sequence as
+// norm_modulate_kernel.
+template <int NC>
+__global__ void __launch_bounds__(256) norm_rows_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                             __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                             int64_t rows, int64_t rows_per_batch,
+                                                             int chunks_per_sample, int rows_per_chunk, int kind,
+                                                             float eps,
+                                                             ModVec<__nv_bfloat16> shift, ModVec<__nv_bfloat16> scale) {
+  constexpr int D = 256 * NC;
+  __shared__ float s1p[D];  // round(1 + scale)
+  __shared__ float shf[D];  // round(shift)
+  const int64_t b = blockIdx.x / chunks_per_sample;
+  const int chunk = int(blockIdx.x - b * chunks_per_sample);
+  const int64_t r0 = b * rows_per_batch + int64_t(chunk) * rows_per_chunk;
+  const int64_t r1 = min(min(r0 + rows_per_chunk, (b + 1) * rows_per_batch), rows);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The first row of each warp is loaded before the vectors are built, and every
+  // later row one row ahead of its use.
+  uint4 raw[NC];
+  auto load_row = [&](int64_t r) {
+    const __nv_bfloat16* xr = x + r * ldx;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) raw[i] = *reinterpret_cast<const uint4*>(xr + (i * 32 + lane) * 8);
+  };
+  if (r0 + warp < r1) load_row(r0 + warp);
+  for (int c8 = threadIdx.x; c8 < D / 8; c8 += blockDim.x) {
+    float a[8];
+    if (scale.on) {
+      scale.at8(b, 0, c8 * 8, a);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s1p[c8 * 8 + k] = round_bf16(1.f + a[k]);
+    }
+    if (shift.on) {
+      shift.at8(b, 0, c8 * 8, a);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) shf[c8 * 8 + k] = a[k];
+    }
+  }
+  __syncthreads();
+  for (int64_t r = r0 + warp; r < r1; r += 8) {
+    float v[NC][8];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      unpack_bf16x2(raw[i].x, v[i][0], v[i][1]);
+      unpack_bf16x2(raw[i].y, v[i][2], v[i][3]);
+      unpack_bf16x2(raw[i].z, v[i][4], v[i][5]);
+      unpack_bf16x2(raw[i].w, v[i][6], v[i][7]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s += (kind == LTX_NORM_LAYER) ? v[i][k] : v[i][k] * v[i][k];
+    }
+    if (r + 8 < r1) load_row(r + 8);
+    float mean = 0.f, rstd = 1.f;
+    if (kind == LTX_NORM_LAYER) {
+      mean = warp_sum(s) / float(D);
+      float s2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < NC; ++i)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float d = v[i][k] - mean;
+          s2 += d * d;
+        }
+      rstd = rsqrtf(warp_sum(s2) / float(D) + eps);
+    } else if (kind == LTX_NORM_RMS) {
+      rstd = rsqrtf(warp_sum(s) / float(D) + eps);
+    }
+    __nv_bfloat16* yr = y + r * ldy;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = (i * 32 + lane) * 8;
+      float o[8];
+#pragma unroll
+      for (int k = 0; k < 8; k += 2) {
+        o[k] = (v[i][k] - mean) * rstd;
+        o[k + 1] = (v[i][k + 1] - mean) * rstd;
+        round_bf16_pair(o[k], o[k + 1]);
+      }
+      if (scale.on) {
+#pragma unroll
+        for (int k = 0; k < 8; k += 2) {
+          o[k] *= s1p[c + k];
+          o[k + 1] *= s1p[c + k + 1];
+          round_bf16_pair(o[k], o[k + 1]);
+        }
+      }
+      if (shift.on) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] += shf[c + k];
+      }
+      st8<__nv_bfloat16>(yr + c, o);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------
 // q/k RMSNorm over the whole inner dim (with weight) + split RoPE, in place
 // (ltx_nn.py:186-187,214-218 and 99-115). Thread -> (head h, 8 pair indices j0..j0+7):
@@ -142,6 +245,106 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(T* __restrict__ x, i
   } else {
     st8<T>(xr + c1, a);
     st8<T>(xr + c2, bb);
+  }
+}
+
+// Fast path of the same op for bf16: one warp per row, NI slots of (head, 8 pairs) per
+// lane, no block-wide reduction, the roundings done two to a packed conversion. Same
+// rounding sequence as above. Rows stay packed in registers between the sum-of-squares
+// pass and the output pass, which keeps enough warps resident to cover the load
+// latency.
+template <int NI>
+__global__ void __launch_bounds__(256, 2) qk_rows_bf16_kernel(__nv_bfloat16* __restrict__ x, int64_t ldx, int64_t rows,
+                                                           int64_t rows_per_batch, int rows_per_cta, int d,
+                                                           const __nv_bfloat16* __restrict__ w, float eps,
+                                                           const __nv_bfloat16* __restrict__ cos_t,
+                                                           const __nv_bfloat16* __restrict__ sin_t, int64_t ld_rope,
+                                                           int64_t rope_ld_batch) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r0 = int64_t(blockIdx.x) * rows_per_cta;
+  const int64_t r1 = min(r0 + rows_per_cta, rows);
+  const int per_head = d >> 4;
+  const float inv_D = 1.f / float(32 * NI * 16);
+  for (int64_t r = r0 + warp; r < r1; r += 8) {
+    __nv_bfloat16* xr = x + r * ldx;
+    const int64_t b = r / rows_per_batch, t = r - b * rows_per_batch;
+    const int64_t ro = b * rope_ld_batch + t * ld_rope;
+    uint4 ra[NI], rb[NI], rc[NI], rs[NI];
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int u = i * 32 + lane;
+      const int h = u / per_head, j0 = (u - h * per_head) * 8;
+      ra[i] = *reinterpret_cast<const uint4*>(xr + h * d + j0);
+      rb[i] = *reinterpret_cast<const uint4*>(xr + h * d + j0 + (d >> 1));
+      if (cos_t != nullptr) {
+        rc[i] = *reinterpret_cast<const uint4*>(cos_t + ro + h * (d >> 1) + j0);
+        rs[i] = *reinterpret_cast<const uint4*>(sin_t + ro + h * (d >> 1) + j0);
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&ra[i]);
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&rb[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float a0, a1, b0, b1;
+        unpack_bf16x2(pa[k], a0, a1);
+        unpack_bf16x2(pb[k], b0, b1);
+        s += a0 * a0 + a1 * a1 + b0 * b0 + b1 * b1;
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(s) * inv_D + eps);
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int u = i * 32 + lane;
+      const int h = u / per_head, j0 = (u - h * per_head) * 8;
+      const int c1 = h * d + j0;
+      float a[8], bb[8];
+      const uint32_t* pa = reinterpret_cast<const uint32_t*>(&ra[i]);
+      const uint32_t* pb = reinterpret_cast<const uint32_t*>(&rb[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        unpack_bf16x2(pa[k], a[2 * k], a[2 * k + 1]);
+        unpack_bf16x2(pb[k], bb[2 * k], bb[2 * k + 1]);
+      }
+      if (w != nullptr) {
+        float w1[8], w2[8];
+        ld8<__nv_bfloat16>(w + c1, w1);
+        ld8<__nv_bfloat16>(w + c1 + (d >> 1), w2);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          a[k] = a[k] * rstd * w1[k];
+          bb[k] = bb[k] * rstd * w2[k];
+          round_bf16_pair(a[k], bb[k]);
+        }
+      }
+      if (cos_t != nullptr) {
+        float cs[8], sn[8], o1[8], o2[8];
+        const uint32_t* pc = reinterpret_cast<const uint32_t*>(&rc[i]);
+        const uint32_t* ps = reinterpret_cast<const uint32_t*>(&rs[i]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          unpack_bf16x2(pc[k], cs[2 * k], cs[2 * k + 1]);
+          unpack_bf16x2(ps[k], sn[2 * k], sn[2 * k + 1]);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          // first*c - second*s ; second*c + first*s, each product rounded (no FMA)
+          float p1 = __fmul_rn(a[k], cs[k]), p2 = __fmul_rn(bb[k], sn[k]);
+          float p3 = __fmul_rn(bb[k], cs[k]), p4 = __fmul_rn(a[k], sn[k]);
+          round_bf16_pair(p1, p2);
+          round_bf16_pair(p3, p4);
+          o1[k] = __fsub_rn(p1, p2);
+          o2[k] = __fadd_rn(p3, p4);
+        }
+        st8<__nv_bfloat16>(xr + c1, o1);
+        st8<__nv_bfloat16>(xr + c1 + (d >> 1), o2);
+      } else {
+        st8<__nv_bfloat16>(xr + c1, a);
+        st8<__nv_bfloat16>(xr + c1 + (d >> 1), bb);
+      }
+    }
   }
 }
 
@@ -369,6 +572,35 @@ void launch_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ldy, int6
   ModVec<T> sh = make_modvec<T>(m, 0), sc = make_modvec<T>(m, 1);
   auto xp = static_cast<const T*>(x);
   auto yp = static_cast<T*>(y);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const bool per_sample = (!sh.on || sh.mod == nullptr || sh.ldt == 0) && (!sc.on || sc.mod == nullptr || sc.ldt == 0);
+    const int nc = D / 256;
+    if (per_sample && D % 256 == 0 && nc >= 1 && nc <= 8 && (rows % rpb == 0 || rows <= rpb)) {
+      // two resident CTAs per SM, each streaming an even share of one sample's rows
+      const int64_t target = int64_t(num_sms()) * 2;
+      const int64_t n_samples = (rows + rpb - 1) / rpb;
+      int64_t per = std::max<int64_t>(8, (rows + target - 1) / target);
+      per = std::min<int64_t>(per, std::min<int64_t>(rpb, rows));
+      const int64_t chunks = (std::min<int64_t>(rpb, rows) + per - 1) / per;
+      const unsigned grid = unsigned(n_samples * chunks);
+#define LTX_NORM_ROWS(NCV)                                                                                  \
+  norm_rows_bf16_kernel<NCV><<<grid, 256, 0, s>>>(xp, ldx, yp, ldy, rows, rpb, int(chunks), int(per), kind, eps, \
+                                                  sh, sc),                                                    \
+      ltx::note_launch()
+      switch (nc) {
+        case 1: LTX_NORM_ROWS(1); break;
+        case 2: LTX_NORM_ROWS(2); break;
+        case 3: LTX_NORM_ROWS(3); break;
+        case 4: LTX_NORM_ROWS(4); break;
+        case 5: LTX_NORM_ROWS(5); break;
+        case 6: LTX_NORM_ROWS(6); break;
+        case 7: LTX_NORM_ROWS(7); break;
+        default: LTX_NORM_ROWS(8); break;
+      }
+#undef LTX_NORM_ROWS
+      return;
+    }
+  }
   switch (nv) {
     case 1: norm_modulate_kernel<T, 1><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc), ltx::note_launch(); break;
     case 2: norm_modulate_kernel<T, 2><<<unsigned(rows), threads, 0, s>>>(xp, ldx, yp, ldy, rpb, D, kind, eps, sh, sc), ltx::note_launch(); break;
@@ -432,7 +664,28 @@ extern "C" int ltx_qk_norm_rope(void* x, int64_t ldx, int64_t rows, int64_t rows
     qk_norm_rope_kernel<float><<<unsigned(rows), threads, 0, s>>>(
         static_cast<float*>(x), ldx, rows_per_batch, heads, head_dim, static_cast<const float*>(weight), eps,
         static_cast<const float*>(cos_tab), static_cast<const float*>(sin_tab), ld_rope, rope_ld_batch), ltx::note_launch();
-  else
+  else if ((nthr % 32) == 0 && nthr / 32 <= 4) {
+    // one warp per row; 2 CTAs of 8 warps per SM, an even share of rows each
+    const int ni = nthr / 32;
+    const int64_t target = int64_t(num_sms()) * 2;
+    const int per = int(std::max<int64_t>(8, (rows + target - 1) / target));
+    const unsigned grid = unsigned((rows + per - 1) / per);
+    auto xb = static_cast<__nv_bfloat16*>(x);
+    auto wb = static_cast<const __nv_bfloat16*>(weight);
+    auto cb = static_cast<const __nv_bfloat16*>(cos_tab);
+    auto sb = static_cast<const __nv_bfloat16*>(sin_tab);
+#define LTX_QK_ROWS(NIV)                                                                                    \
+  qk_rows_bf16_kernel<NIV><<<grid, 256, 0, s>>>(xb, ldx, rows, rows_per_batch, per, head_dim, wb, eps, cb, sb, \
+                                                ld_rope, rope_ld_batch),                                      \
+      ltx::note_launch()
+    switch (ni) {
+      case 1: LTX_QK_ROWS(1); break;
+      case 2: LTX_QK_ROWS(2); break;
+      case 3: LTX_QK_ROWS(3); break;
+      default: LTX_QK_ROWS(4); break;
+    }
+#undef LTX_QK_ROWS
+  } else
     qk_norm_rope_kernel<__nv_bfloat16><<<unsigned(rows), threads, 0, s>>>(
         static_cast<__nv_bfloat16*>(x), ldx, rows_per_batch, heads, head_dim,
         static_cast<const __nv_bfloat16*>(weight), eps, static_cast<const __nv_bfloat16*>(cos_tab),

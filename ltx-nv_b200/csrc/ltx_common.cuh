@@ -32,6 +32,12 @@ LTX_DEVICE __nv_bfloat16 f32_to_bf16(float v) { return __float2bfloat16_rn(v); }
 // Round an fp32 value to the nearest bf16 and widen it again (models a torch .to(bf16)).
 LTX_DEVICE float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// Round two fp32 values to bf16 and widen them again with one packed conversion.
+LTX_DEVICE void round_bf16_pair(float& a, float& b) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  a = __low2float(p);
+  b = __high2float(p);
+}
 LTX_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&p);
