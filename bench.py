@@ -405,6 +405,7 @@ PROBES = {
     "ffn_out": "FFN-out tcgen05 GEMM + gate*out+residual epilogue, M=12288, N=2048, K=8192",
     "attn_out": "attention out-projection tcgen05 GEMM + gate*out+residual epilogue, M=12288, N=2048, K=2048",
     "norm": "RMSNorm + adaLN modulate, [2*6144, 2048] bf16",
+    "qknorm": "q RMSNorm (with weight) + split RoPE in place on the packed QKV buffer, [2*6144, 2048] bf16",
 }
 
 
@@ -452,6 +453,12 @@ def run_probe(args, dev: torch.device) -> dict:
         mm = nat.modulation(table, mod, shift=(0, 0), scale=(d, d), mod_ld_batch=6 * d)
         fn = lambda: nat.norm_modulate(x, y, t, nat.LTX_NORM_RMS, 1e-6, mm)  # noqa: E731
         flops, nbytes = None, 2 * (x.numel() + y.numel())
+    elif args.probe == "qknorm":
+        qkv = rnd(m, 3 * d + c["heads"])
+        wq = (1 + rnd(d, scale=0.02).float()).to(torch.bfloat16)
+        cos, sin = rnd(t, d // 2), rnd(t, d // 2)
+        fn = lambda: nat.qk_norm_rope(qkv[:, :d], t, c["heads"], c["head_dim"], wq, 1e-6, cos, sin, 0)  # noqa
+        flops, nbytes = None, 2 * (2 * m * d + cos.numel() + sin.numel())
     else:
         raise SystemExit(f"unknown probe {args.probe}")
     for _ in range(args.warmup):

@@ -35,15 +35,15 @@ struct TcCfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + VEC_BYTES + 1024;
 };
 
-// Named barrier 1 over the 4 epilogue warps (128 threads) of gemm_tc_kernel.
-LTX_DEVICE void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier 1 over the 8 epilogue warps (256 threads) of gemm_tc_kernel.
+LTX_DEVICE void epi_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 LTX_DEVICE uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    __nv_bfloat16* __restrict__ C, int64_t ldc, int M, int N, int K, Epi<__nv_bfloat16> epi) {
   using Cfg = TcCfg<BN>;
@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 256);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -115,8 +115,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
           const int s = it % Cfg::STAGES;
-          const uint32_t r = uint32_t(it / Cfg::STAGES);
-          if (!mbar_wait(&full[s], r & 1, abort_flag)) goto done;
+          if (!mbar_wait(&full[s], uint32_t(it / Cfg::STAGES) & 1, abort_flag)) goto done;
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + s * Cfg::STAGE_BYTES);
           const uint32_t b_addr = a_addr + Cfg::A_BYTES;
@@ -132,11 +131,13 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5 -> TMEM lane quadrants 2, 3, 0, 1; one accumulator row per
-    // thread.
+    // Epilogue warps 2..9: warp w reads TMEM lane quadrant w % 4 (one accumulator row
+    // per thread) and column half (w - 2) / 4 of the tile, so two warps share each SM
+    // sub-partition and hide each other's latencies.
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
-    const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+    const int c_lo = ((warp - 2) >> 2) * (BN / 2), c_hi = c_lo + BN / 2;
+    const int et = threadIdx.x - 64;  // 0..255 among the epilogue threads
     // Per-column vectors of the epilogue (bias, gate table, row_vec), staged per tile.
     __nv_bfloat16* s_vec = reinterpret_cast<__nv_bfloat16*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES);
     const bool gres = epi.kind == LTX_EPI_GATE_RESIDUAL;
@@ -163,7 +164,7 @@ __global__ void __launch_bounds__(192, 1)
         // slab before waiting for the MMAs. No global load is left between the TMEM
         // read and the store of a slab.
         epi_bar_sync();
-        for (int i = et; i < 3 * (BN / 8); i += 128) {
+        for (int i = et; i < 3 * (BN / 8); i += 256) {
           const int w = i / (BN / 8), c = (i - w * (BN / 8)) * 8;
           const __nv_bfloat16* src = w == 0 ? vsrc0 : (w == 1 ? gtab : vsrc2);
           if (src != nullptr)
@@ -184,18 +185,18 @@ __global__ void __launch_bounds__(192, 1)
           }
         };
         uint4 rc[4], gc[4];
-        load_row(0, rc, gc);
+        load_row(c_lo, rc, gc);
         if (ok && !mbar_wait(&tfull[acc], u & 1, abort_flag)) ok = false;
         if (!ok) continue;
         tc_fence_after();
         const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
         __nv_bfloat16* crow = C + m * ldc + n0;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
           uint32_t rr[32];
           tmem_ld32(tbase + uint32_t(c0), rr);
           uint4 rn[4], gn[4];
-          if (c0 + 32 < BN) load_row(c0 + 32, rn, gn);
+          if (c0 + 32 < c_hi) load_row(c0 + 32, rn, gn);
           tmem_wait_ld();
           if (live) {
 #pragma unroll
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(192, 1)
       {
         const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += 32) {
+        for (int c0 = c_lo; c0 < c_hi && n0 + c0 < N; c0 += 32) {
           uint32_t rr[32];
           tmem_ld32(tbase + uint32_t(c0), rr);
           tmem_wait_ld();
@@ -467,7 +468,7 @@ void launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, 
     LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     attr_dev = dev;
   }
-  kern<<<unsigned(grid), 192, Cfg::SMEM, s>>>(ta, tb, static_cast<__nv_bfloat16*>(C), ldc, int(M), int(N), int(K), epi), ltx::note_launch();
+  kern<<<unsigned(grid), 320, Cfg::SMEM, s>>>(ta, tb, static_cast<__nv_bfloat16*>(C), ldc, int(M), int(N), int(K), epi), ltx::note_launch();
 }
 
 
