@@ -159,8 +159,9 @@ typedef struct {
 
 int ltx_linear(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, int64_t ldc, int64_t M, int64_t N,
                int64_t K, const ltx_epilogue* epi, int dtype, void* stream);
-/* Tuning knob (process-wide): force the tcgen05 tile width to 128 or 256 columns, or 0
- * for the automatic choice. No counterpart in the reference (cuBLASLt picks its own). */
+/* Tuning knob (process-wide): force single-CTA tcgen05 tiles of 128 or 256 columns, or 0
+ * for the automatic choice (256-column tiles computed by CTA pairs when N >= 512 and
+ * M >= 256). No counterpart in the reference (cuBLASLt picks its own). */
 int ltx_gemm_set_tile_n(int bn);
 
 /* ---------------------------------------------------------------------------------- */

@@ -15,6 +15,8 @@
 // bf16 or fp32, M < 32: weight-streaming kernel (the per-sample adaLN / timestep MLPs,
 //   where the problem is reading W once from HBM).
 // fp32, M >= 32: CUDA-core tiled kernel (the accuracy mode).
+#include <algorithm>
+
 #include "ltx_kernels.cuh"
 
 namespace ltx {
@@ -23,11 +25,16 @@ namespace detail {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 
-template <int BN>
+// PAIR: a cluster of two CTAs on neighbouring SMs computes a 256 x BN tile with
+// tcgen05 cta_group::2 MMAs (M = 256): each CTA loads its 128 rows of A and half of
+// the BN rows of B, so a stage holds 16 + 16 KB per SM instead of 16 + 32 KB and the
+// ring is six stages deep.
+template <int BN, bool PAIR = false>
 struct TcCfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int STAGES = PAIR ? 6 : (BN == 256 ? 4 : 6);
   static constexpr int A_BYTES = kBM * kBK * 2;
-  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B rows loaded by one CTA
+  static constexpr int B_BYTES = B_ROWS * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
@@ -42,11 +49,11 @@ LTX_DEVICE uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    __nv_bfloat16* __restrict__ C, int64_t ldc, int M, int N, int K, Epi<__nv_bfloat16> epi) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
@@ -57,10 +64,17 @@ __global__ void __launch_bounds__(320, 1)
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
-  const int m_tiles = (M + kBM - 1) / kBM;
+  // CTA pair: rank 0 (leader) issues the MMAs and owns full[] and tempty[]; tiles are
+  // 256 rows, rank r takes rows [128 r, 128 r + 128) and B rows [BN/2 r, BN/2 r + BN/2).
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  constexpr int TM = PAIR ? 2 * kBM : kBM;
+  const int m_tiles = (M + TM - 1) / TM;
   const int n_tiles = (N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + kBK - 1) / kBK;
+  const int tile0 = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
+  const int tile_step = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::STAGES; ++s) {
@@ -69,7 +83,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 256);
+      mbar_init(&tempty[a], PAIR ? 16 : 8);  // one arrival per epilogue warp (of both CTAs)
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -77,37 +91,56 @@ __global__ void __launch_bounds__(320, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    // both CTAs' barriers initialised and TMEM allocated before any cross-CTA use
+    __syncwarp();
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * kBM;
-        const int n0 = (tile % n_tiles) * BN;
+      for (int tile = tile0; tile < num_tiles; tile += tile_step) {
+        const int m0 = (tile / n_tiles) * TM + int(rank) * kBM;
+        const int n0 = (tile % n_tiles) * BN + int(rank) * Cfg::B_ROWS;
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
           const int s = it % Cfg::STAGES;
           const uint32_t r = uint32_t(it / Cfg::STAGES);
           if (!mbar_wait(&empty[s], (r & 1) ^ 1, abort_flag)) goto done;
           uint8_t* sa = smem + s * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
-          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full[s], kb * kBK, m0);
-          tma_load_2d(sb, &tmB, &full[s], kb * kBK, n0);
+          if constexpr (PAIR) {
+            // both CTAs' bytes complete on the leader's full[s]
+            const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+            tma_load_2d_pair(sa, &tmA, fb, kb * kBK, m0);
+            tma_load_2d_pair(sb, &tmB, fb, kb * kBK, n0);
+          } else {
+            mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+            tma_load_2d(sa, &tmA, &full[s], kb * kBK, m0);
+            tma_load_2d(sb, &tmB, &full[s], kb * kBK, n0);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN, 0);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = umma_idesc_bf16(TM, BN, 0);
       int it = 0, local = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      for (int tile = tile0; tile < num_tiles; tile += tile_step, ++local) {
         const int acc = local & 1;
         const uint32_t u = uint32_t(local >> 1);
         if (!mbar_wait(&tempty[acc], (u & 1) ^ 1, abort_flag)) goto done;
@@ -123,11 +156,20 @@ __global__ void __launch_bounds__(320, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
-            umma_ss(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_ss_pair(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              umma_ss(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          if constexpr (PAIR)
+            umma_commit_pair(&empty[s], 3);
+          else
+            umma_commit(&empty[s]);
         }
-        umma_commit(&tfull[acc]);
+        if constexpr (PAIR)
+          umma_commit_pair(&tfull[acc], 3);
+        else
+          umma_commit(&tfull[acc]);
       }
     }
   } else {
@@ -148,10 +190,21 @@ __global__ void __launch_bounds__(320, 1)
     // epilogue thread reaches the same named barriers.
     bool ok = true;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    // this warp's arrival on tempty (the leader's barrier for a CTA pair)
+    auto release_acc = [&](int acc) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        else
+          mbar_arrive(&tempty[acc]);
+      }
+    };
+    for (int tile = tile0; tile < num_tiles; tile += tile_step, ++local) {
       const int acc = local & 1;
       const uint32_t u = uint32_t(local >> 1);
-      const int m0 = (tile / n_tiles) * kBM;
+      const int m0 = (tile / n_tiles) * TM + int(rank) * kBM;
       const int n0 = (tile % n_tiles) * BN;
       const int64_t m = int64_t(m0) + row_in_tile;
       // sample / token of this row, once per tile (32-bit division; M < 2^31)
@@ -267,8 +320,7 @@ __global__ void __launch_bounds__(320, 1)
             gc[j] = gn[j];
           }
         }
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        release_acc(acc);
         continue;
       }
       // Ragged last column tile (N not a multiple of BN): generic epilogue per 8 columns.
@@ -303,15 +355,25 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      release_acc(acc);
     }
   }
 done:
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  __syncwarp();
+  if constexpr (PAIR) {
+    // no CTA of the pair leaves while the other may still signal its barriers
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    }
+  } else {
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    }
   }
 }
 
@@ -451,16 +513,15 @@ void launch_skinny(const T* A, int64_t lda, const T* W, int64_t ldw, T* C, int64
   }
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 void launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, int64_t ldc, int64_t M, int64_t N,
                int64_t K, const Epi<__nv_bfloat16>& epi, cudaStream_t s) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, PAIR>;
   const CUtensorMap ta = make_tmap_bf16_2d(A, uint64_t(K), uint64_t(M), uint64_t(lda), kBK, kBM);
-  const CUtensorMap tb = make_tmap_bf16_2d(W, uint64_t(K), uint64_t(N), uint64_t(ldw), kBK, BN);
-  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
-  int64_t grid = num_sms();
-  if (tiles < grid) grid = tiles;
-  auto kern = gemm_tc_kernel<BN>;
+  const CUtensorMap tb = make_tmap_bf16_2d(W, uint64_t(K), uint64_t(N), uint64_t(ldw), kBK, Cfg::B_ROWS);
+  constexpr int64_t TM = PAIR ? 2 * kBM : kBM;
+  const int64_t tiles = ((M + TM - 1) / TM) * ((N + BN - 1) / BN);
+  auto kern = gemm_tc_kernel<BN, PAIR>;
   static int attr_dev = -1;
   int dev = 0;
   LTX_CUDA(cudaGetDevice(&dev));
@@ -468,7 +529,29 @@ void launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, 
     LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     attr_dev = dev;
   }
-  kern<<<unsigned(grid), 320, Cfg::SMEM, s>>>(ta, tb, static_cast<__nv_bfloat16*>(C), ldc, int(M), int(N), int(K), epi), ltx::note_launch();
+  auto Cp = static_cast<__nv_bfloat16*>(C);
+  if constexpr (PAIR) {
+    // one CTA pair per two SMs, persistent over the 256-row tiles
+    const int64_t pairs = std::min<int64_t>(num_sms() / 2, tiles);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(2 * pairs));
+    cfg.blockDim = dim3(320);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LTX_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, Cp, ldc, int(M), int(N), int(K), epi));
+    ltx::note_launch();
+  } else {
+    int64_t grid = num_sms();
+    if (tiles < grid) grid = tiles;
+    kern<<<unsigned(grid), 320, Cfg::SMEM, s>>>(ta, tb, Cp, ldc, int(M), int(N), int(K), epi), ltx::note_launch();
+  }
 }
 
 
@@ -603,7 +686,8 @@ __global__ void __launch_bounds__(192, 1)
 
 }  // namespace detail
 
-// Tile-width override for tuning / tests: 0 = automatic, 128 or 256 forces BN.
+// Tile-width override for tuning / tests: 0 = automatic (256-column tiles on CTA pairs
+// when N >= 512 and M >= 256, else 128), 128 or 256 force single-CTA tiles of that width.
 static int g_gemm_bn_override = 0;
 
 }  // namespace ltx
@@ -659,10 +743,12 @@ extern "C" int ltx_linear(const void* A, int64_t lda, const void* W, int64_t ldw
     } else {
       int bn = g_gemm_bn_override;
       if (bn == 0) bn = (N >= 512) ? 256 : 128;
-      if (bn == 256)
-        launch_tc<256>(A, lda, W, ldw, C, ldc, M, N, K, e, s);
+      if (bn == 256 && M >= 2 * kBM && g_gemm_bn_override == 0)
+        launch_tc<256, true>(A, lda, W, ldw, C, ldc, M, N, K, e, s);
+      else if (bn == 256)
+        launch_tc<256, false>(A, lda, W, ldw, C, ldc, M, N, K, e, s);
       else
-        launch_tc<128>(A, lda, W, ldw, C, ldc, M, N, K, e, s);
+        launch_tc<128, false>(A, lda, W, ldw, C, ldc, M, N, K, e, s);
     }
   }
   LTX_CUDA(cudaGetLastError());

@@ -244,6 +244,46 @@ def test_linear_bf16_tcgen05(m, n, k, bn):
     assert rel_l2(c, _lin_ref(a, w, bias)) < 4e-3
 
 
+@pytest.mark.parametrize("m,n,k", [(1000, 2080, 512), (12288, 2048, 2048), (300, 512, 128)])
+def test_linear_bf16_cta_pair_matches_single(m, n, k):
+    """The automatic choice runs N >= 512, M >= 256 on CTA pairs (cta_group::2, 256-row
+    tiles); forcing 256-column single-CTA tiles runs the same K order per output, so the
+    two must agree bit for bit for every epilogue kind, ragged M and N included."""
+    torch.manual_seed(12)
+    b = 2
+    t = m // b
+    a = torch.randn(m, k, device=DEV, dtype=torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * k ** -0.5).to(torch.bfloat16)
+    bias = torch.randn(n, device=DEV, dtype=torch.bfloat16)
+    table = torch.randn(6, n, device=DEV, dtype=torch.bfloat16) * 0.1
+    mod = torch.randn(b, 6 * n, device=DEV, dtype=torch.bfloat16) * 0.1
+    mask = (torch.arange(m, device=DEV) % 5 == 0).float()
+    vec = torch.randn(n, device=DEV, dtype=torch.bfloat16)
+    res = torch.randn(m, n, device=DEV, dtype=torch.bfloat16)
+    epis = {
+        "none": lambda c: nat.epilogue(bias=bias),
+        "gelu": lambda c: nat.epilogue(nat.EPI_GELU_TANH, bias=bias),
+        "gate_residual": lambda c: nat.epilogue(
+            nat.EPI_GATE_RESIDUAL, bias=bias, residual=c,
+            gate=nat.modulation(table, mod, shift=None, scale=(5 * n, 5 * n), mod_ld_batch=6 * n), rows_per_batch=t),
+        "row_mask_add": lambda c: nat.epilogue(nat.EPI_ROW_MASK_ADD, bias=bias, row_mask=mask, row_vec=vec),
+    }
+    for name, mk in epis.items():
+        outs = []
+        for bn in (0, 256):
+            c = res.clone()
+            nat.gemm_set_tile_n(bn)
+            try:
+                nat.linear(a, w, c, mk(c))
+            finally:
+                nat.gemm_set_tile_n(0)
+            outs.append(c)
+        torch.cuda.synchronize()
+        assert nat.device_error_flags() == 0
+        assert torch.equal(outs[0], outs[1]), name
+    assert rel_l2(outs[0], res.float() * 0 + _lin_ref(a, w, bias) + mask[:, None] * vec.float()) < 4e-3
+
+
 def test_linear_bf16_strided_operands_and_epilogues():
     torch.manual_seed(6)
     b, t, d, k = 2, 200, 256, 512
