@@ -185,7 +185,10 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         step(latent)
     torch.cuda.synchronize(dev)
     graph = None
-    if not args.no_graph and world == 1:
+    if not args.no_graph:
+        # one step captured in a CUDA graph (N > 1: the NCCL collectives of the step are
+        # captured too; every rank captures the same sequence after the eager warm-up
+        # has initialised the communicators)
         graph = torch.cuda.CUDAGraph()
         static_in = latent.clone()
         with torch.cuda.graph(graph):
@@ -256,6 +259,10 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         step(latent)
     kern = prof.summary()
     step_ms_instr = sum(v["total_ms"] for v in kern.values())
+    # a graph that holds NCCL calls is released before the process group goes away
+    used_graph = graph is not None
+    del graph
+    torch.cuda.synchronize(dev)
 
     if rank != 0:
         return None
@@ -285,7 +292,7 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
                    "latent_tokens": t, "seq_len": t, "text_tokens": CFG3["text"],
                    "parallelism": "single GPU" if world == 1 else f"cfg{layout.cfg} x sp{layout.sp} (Ulysses, NCCL)",
                    "l2": "inputs larger than L2 (4.2 GB weights, ~1 GB activations per step)",
-                   "cuda_graph": graph is not None},
+                   "cuda_graph": used_graph},
         "steps_per_s": 1e3 / ms_per_step, "step_tflops_per_gpu": tflops / world,
         "pct_bf16_peak": tflops / world / peaks["bf16_tflops"], "pct_bf16_peak_sustained": tflops / world / peak,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 2,
@@ -508,6 +515,11 @@ def main():
     if args.probe:
         print(json.dumps(run_probe(args, dev)), flush=True)
         return
+    # Libraries (NCCL's banner among them) write to file descriptor 1; keep stdout for the
+    # one JSON line by pointing fd 1 at stderr until it is printed.
+    sys.stdout.flush()
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if world > 1:
         from datetime import timedelta
 
@@ -519,7 +531,8 @@ def main():
             cb.pop("block_sec", None)
             line["cpu_baseline"] = cb
         if line is not None:
-            print(json.dumps(line), flush=True)
+            json_out.write(json.dumps(line) + "\n")
+            json_out.flush()
     finally:
         if world > 1:
             torch.distributed.barrier()
