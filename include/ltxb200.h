@@ -192,6 +192,17 @@ int ltx_cfg_euler(const void* vel, const void* latent, const float* timesteps, i
  * out = cond + (cfg-1)(cond-uncond) + stg(cond-ptb) + (modality-1)(cond-mod). */
 int ltx_guide(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n, float cfg_scale,
               float stg_scale, float modality_scale, void* out, int dtype, void* stream);
+/* Guidance blend with std rescale (ltx_dit.py:551-562, rescale_scale != 0): pred as in
+ * ltx_guide (fp32), factor = rescale*std(cond)/std(pred) + (1-rescale) with the unbiased
+ * std over all n elements, out = round(pred*factor). Two kernels on `stream`. The
+ * workspace (ltx_guide_rescale_workspace_bytes(n) bytes, 16-byte aligned, device memory
+ * owned by the caller) holds per-block partial sums and a completion counter that must
+ * be zero before the first call; every call leaves it zero again. Calls that share a
+ * workspace must not run concurrently. */
+size_t ltx_guide_rescale_workspace_bytes(int64_t n);
+int ltx_guide_rescale(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
+                      float cfg_scale, float stg_scale, float modality_scale, float rescale_scale, void* out,
+                      void* workspace, size_t workspace_bytes, int dtype, void* stream);
 /* Euler step (ltx_dit.py:602-606): v = round((sample-denoised)/sigma);
  * out = sample + v*(sigma_next - sigma). */
 int ltx_euler(const void* sample, const void* denoised, int64_t n, float sigma, float sigma_next, void* out,

@@ -494,6 +494,121 @@ __global__ void guide_kernel(const T* __restrict__ c, const T* __restrict__ u, c
   st_elem<T>(out + i, r);
 }
 
+// Guidance with std rescale (ltx_dit.py:558-561): factor = rescale * std(cond) / std(pred)
+// + (1 - rescale) over all n elements (unbiased), out = round(pred * factor).
+// Pass 1 (guide_stats_kernel): each block accumulates sum and sum of squares of cond
+// and pred in double and writes them to its slot of the workspace; the last block to
+// finish (completion counter in the workspace) adds the slots in block order, so the
+// result does not depend on scheduling, stores the factor and resets the counter to 0.
+// Pass 2 (guide_scale_kernel) recomputes pred and scales it.
+struct GuideWs {
+  unsigned int counter;  // blocks of pass 1 finished; 0 between calls
+  float factor;
+  double pad;            // keeps the partials 16-byte aligned
+  // double partials[blocks][4] follow
+};
+constexpr int kGuideThreads = 256;
+constexpr int64_t kGuideElemsPerBlock = 4096;
+constexpr int kGuideMaxBlocks = 1024;
+
+inline int guide_rescale_blocks(int64_t n) {
+  return int(std::min<int64_t>(kGuideMaxBlocks, std::max<int64_t>(1, (n + kGuideElemsPerBlock - 1) / kGuideElemsPerBlock)));
+}
+inline size_t guide_rescale_ws_bytes(int64_t n) {
+  return sizeof(GuideWs) + size_t(guide_rescale_blocks(n)) * 4 * sizeof(double);
+}
+
+template <typename T>
+LTX_DEVICE float guide_pred(const T* c, const T* u, const T* p, const T* m, int64_t i, float cfg_m1, float stg,
+                            float mod_m1, float& cv) {
+  cv = ld_elem<T>(c + i);
+  float r = __fadd_rn(cv, __fmul_rn(cfg_m1, __fsub_rn(cv, ld_elem<T>(u + i))));
+  r = __fadd_rn(r, __fmul_rn(stg, __fsub_rn(cv, ld_elem<T>(p + i))));
+  return __fadd_rn(r, __fmul_rn(mod_m1, __fsub_rn(cv, ld_elem<T>(m + i))));
+}
+
+LTX_DEVICE double block_sum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = (lane < int(blockDim.x >> 5)) ? red[lane] : 0.0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return t;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGuideThreads) guide_stats_kernel(const T* __restrict__ c, const T* __restrict__ u,
+                                                                    const T* __restrict__ p, const T* __restrict__ m,
+                                                                    int64_t n, float cfg_m1, float stg, float mod_m1,
+                                                                    float rescale, GuideWs* __restrict__ ws) {
+  __shared__ double red[kGuideThreads / 32];
+  __shared__ bool last;
+  double* parts = reinterpret_cast<double*>(ws + 1);
+  double a[4] = {0.0, 0.0, 0.0, 0.0};  // sum c, sum c^2, sum pred, sum pred^2
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    float cv;
+    const float pv = guide_pred<T>(c, u, p, m, i, cfg_m1, stg, mod_m1, cv);
+    a[0] += double(cv);
+    a[1] += double(cv) * double(cv);
+    a[2] += double(pv);
+    a[3] += double(pv) * double(pv);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const double t = block_sum_d(a[k], red);
+    if (threadIdx.x == 0) parts[blockIdx.x * 4 + k] = t;
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(&ws->counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    double s[4] = {0.0, 0.0, 0.0, 0.0};
+    for (unsigned b = 0; b < gridDim.x; ++b)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) s[k] += reinterpret_cast<volatile double*>(parts)[b * 4 + k];
+    const double nn = double(n);
+    const double var_c = (s[1] - s[0] * s[0] / nn) / (nn - 1.0);
+    const double var_p = (s[3] - s[2] * s[2] / nn) / (nn - 1.0);
+    const float ratio = float(sqrt(fmax(var_c, 0.0)) / sqrt(fmax(var_p, 0.0)));
+    ws->factor = __fadd_rn(__fmul_rn(rescale, ratio), 1.f - rescale);
+    ws->counter = 0u;
+  }
+}
+
+template <typename T>
+__global__ void guide_scale_kernel(const T* __restrict__ c, const T* __restrict__ u, const T* __restrict__ p,
+                                   const T* __restrict__ m, int64_t n, float cfg_m1, float stg, float mod_m1,
+                                   const GuideWs* __restrict__ ws, T* __restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float cv;
+  const float pv = guide_pred<T>(c, u, p, m, i, cfg_m1, stg, mod_m1, cv);
+  st_elem<T>(out + i, __fmul_rn(pv, ws->factor));
+}
+
+template <typename T>
+void launch_guide_rescale(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
+                          float cfg_m1, float stg, float mod_m1, float rescale, void* out, GuideWs* ws,
+                          cudaStream_t s) {
+  auto c = static_cast<const T*>(cond);
+  auto u = static_cast<const T*>(uncond);
+  auto p = static_cast<const T*>(ptb);
+  auto m = static_cast<const T*>(mod);
+  guide_stats_kernel<T><<<unsigned(guide_rescale_blocks(n)), kGuideThreads, 0, s>>>(c, u, p, m, n, cfg_m1, stg,
+                                                                                   mod_m1, rescale, ws),
+      ltx::note_launch();
+  guide_scale_kernel<T><<<unsigned((n + 255) / 256), 256, 0, s>>>(c, u, p, m, n, cfg_m1, stg, mod_m1, ws,
+                                                                  static_cast<T*>(out)),
+      ltx::note_launch();
+}
+
 // velocity = round((sample - denoised) / sigma); out = round(sample + velocity * dt).
 template <typename T>
 __global__ void euler_kernel(const T* __restrict__ s, const T* __restrict__ d, int64_t n, float sigma, float dt,
@@ -822,6 +937,29 @@ extern "C" int ltx_guide(const void* cond, const void* uncond, const void* ptb, 
         static_cast<const __nv_bfloat16*>(cond), static_cast<const __nv_bfloat16*>(uncond),
         static_cast<const __nv_bfloat16*>(ptb), static_cast<const __nv_bfloat16*>(mod), n, cfg_scale - 1.f,
         stg_scale, modality_scale - 1.f, static_cast<__nv_bfloat16*>(out)), ltx::note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" size_t ltx_guide_rescale_workspace_bytes(int64_t n) { return n > 0 ? guide_rescale_ws_bytes(n) : 0; }
+
+extern "C" int ltx_guide_rescale(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
+                                 float cfg_scale, float stg_scale, float modality_scale, float rescale_scale,
+                                 void* out, void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(cond && uncond && ptb && mod && out && workspace, "NULL argument");
+  LTX_REQUIRE(n > 1, "n must be at least 2 (unbiased std)");
+  LTX_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 16 == 0, "workspace must be 16-byte aligned");
+  LTX_REQUIRE(workspace_bytes >= guide_rescale_ws_bytes(n), "workspace too small (ltx_guide_rescale_workspace_bytes)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto ws = static_cast<GuideWs*>(workspace);
+  if (dtype == LTX_F32)
+    launch_guide_rescale<float>(cond, uncond, ptb, mod, n, cfg_scale - 1.f, stg_scale, modality_scale - 1.f,
+                                rescale_scale, out, ws, s);
+  else
+    launch_guide_rescale<__nv_bfloat16>(cond, uncond, ptb, mod, n, cfg_scale - 1.f, stg_scale,
+                                        modality_scale - 1.f, rescale_scale, out, ws, s);
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

@@ -756,14 +756,23 @@ def cfg_denoise_step(model: LTXModel, latent: torch.Tensor, positions: torch.Ten
     return vel.view(2, t, c), den.view(1, t, c), nxt.view(1, t, c)
 
 
+_guide_ws: dict = {}
+
+
 def guide(cond, uncond, ptb, mod, p: GuiderParams) -> torch.Tensor:
     """Guidance blend cond + (cfg-1)(cond-uncond) + stg(cond-ptb) + (mod-1)(cond-mod)
-    (ltx_dit.py:551-562) as one device kernel. Rescale (a global std) is not supported yet."""
-    if p.rescale_scale != 0:
-        raise NotImplementedError("guidance rescale is not supported yet")
+    (ltx_dit.py:551-562): one device kernel, or with rescale_scale != 0 the two-pass
+    std rescale (factor = r*std(cond)/std(pred) + 1 - r) through a cached workspace."""
     out = torch.empty_like(cond)
-    nat.guide(cond.contiguous(), uncond.contiguous(), ptb.contiguous(), mod.contiguous(), p.cfg_scale, p.stg_scale,
-              p.modality_scale, out)
+    args = (cond.contiguous(), uncond.contiguous(), ptb.contiguous(), mod.contiguous())
+    if p.rescale_scale == 0:
+        nat.guide(*args, p.cfg_scale, p.stg_scale, p.modality_scale, out)
+        return out
+    key = (cond.device, cond.numel())
+    ws = _guide_ws.get(key)
+    if ws is None:
+        ws = _guide_ws[key] = nat.guide_rescale_workspace(cond.numel(), cond.device)
+    nat.guide_rescale(*args, p.cfg_scale, p.stg_scale, p.modality_scale, p.rescale_scale, out, ws)
     return out
 
 

@@ -357,6 +357,18 @@ def scheduler_sigmas(steps, tokens=4096, max_shift=2.05, base_shift=0.95, termin
     return s.to(torch.float32)
 
 
+def guide(cond, uncond, ptb, mod, cfg_scale, stg_scale, rescale_scale, modality_scale):
+    """ltx_dit.py:551-562: the four-way blend in fp32, optional std rescale, cast back."""
+    c = cond.float()
+    pred = c + (cfg_scale - 1) * (c - uncond.float()) + stg_scale * (c - ptb.float()) \
+        + (modality_scale - 1) * (c - mod.float())
+    if rescale_scale != 0:
+        factor = c.std() / pred.std()
+        factor = rescale_scale * factor + (1 - rescale_scale)
+        pred = pred * factor
+    return pred.to(cond.dtype)
+
+
 def guide_cfg(cond, uncond, cfg_scale):
     """ltx_dit.py:551-562 with ptb = mod = cond, stg = 0, rescale = 0."""
     c = cond.float()

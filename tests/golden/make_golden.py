@@ -18,6 +18,7 @@ Fixtures written:
                       reference's outputs for LTXModel.forward and for two CFG denoise
                       steps (X0 + guide + Euler).
   sched.pt            ltx2_scheduler_sigmas(30), video/audio positions.
+  guide.pt            guide() with and without the std rescale on seeded x0 predictions.
 
 Weights are N(0, 0.02) from numpy's PCG64 (platform independent) in the reference's
 named_parameters() order, q/k RMSNorm gains offset by +1 (oracle.synthetic_state_dict).
@@ -192,13 +193,35 @@ def make_sched(ld):
                 "audio_positions": ld.audio_positions(1, 7, "cpu")}, OUT / "sched.pt")
 
 
+GUIDE_PARAMS = [  # (cfg, stg, rescale, modality)
+    (3.0, 1.0, 0.7, 3.0),
+    (4.5, 0.0, 1.0, 1.0),
+    (3.0, 1.0, 0.0, 3.0),
+]
+
+
+def make_guide(ld):
+    """The reference's guide() (ltx_dit.py:551-562), std rescale included, on seeded
+    (1, 384, 128) x0 predictions in fp32 and bf16."""
+    rec = {"params": GUIDE_PARAMS, "cases": {}}
+    for dtype in (torch.float32, torch.bfloat16):
+        xs = [rng_normal((1, 384, 128), 500 + i, scale=1.0 + 0.1 * i, dtype=dtype) for i in range(4)]
+        outs = [ld.guide(*xs, ld.GuiderParams(cfg, stg, rs, mod, ())) for cfg, stg, rs, mod in GUIDE_PARAMS]
+        rec["cases"][str(dtype).replace("torch.", "")] = {"inputs": xs, "outputs": outs}
+    torch.save(rec, OUT / "guide.pt")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=["guide"], default=None, help="regenerate one fixture only")
     args = ap.parse_args()
     ref_root = Path(args.reference)
     ld = _import_reference(ref_root)
     patch_context_view(ld)
+    make_guide(ld)
+    if args.only == "guide":
+        return
     make_philox(ref_root)
     make_sched(ld)
     for name, ov in CASES.items():

@@ -391,6 +391,50 @@ def test_attention_fp32(b, tq, tk, h, d):
     assert rel_l2(o, ref) < 1e-5
 
 
+# ------------------------------------------------------------------- guidance
+
+
+def test_guide_rescale_vs_reference_golden():
+    """The reference's guide() outputs (std rescale on and off) against the device
+    kernels through ltx_dit.guide; the workspace is reused across calls (its completion
+    counter is left at zero by every call)."""
+    import ltx_dit
+
+    rec = torch.load(gc.GOLDEN / "guide.pt", weights_only=False)
+    for dt, case in rec["cases"].items():
+        xs = [x.to(DEV) for x in case["inputs"]]
+        for (cfg, stg, rs, mod), ref in zip(rec["params"], case["outputs"]):
+            p = ltx_dit.GuiderParams(cfg, stg, rs, mod, ())
+            out1 = ltx_dit.guide(*xs, p)
+            out2 = ltx_dit.guide(*xs, p)
+            torch.cuda.synchronize()
+            assert nat.device_error_flags() == 0
+            assert torch.equal(out1, out2)
+            tol = 1e-6 if dt == "float32" else 4e-3
+            assert rel_l2(out1, ref.to(DEV)) < tol, (dt, cfg, stg, rs, mod)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_guide_rescale_zero_equals_plain_guide(dtype):
+    torch.manual_seed(13)
+    n = 3 * 4096 + 77
+    xs = [torch.randn(n, device=DEV).to(dtype) for _ in range(4)]
+    plain = torch.empty_like(xs[0])
+    nat.guide(*xs, 3.0, 1.0, 2.0, plain)
+    ws = nat.guide_rescale_workspace(n, xs[0].device)
+    res = torch.empty_like(xs[0])
+    nat.guide_rescale(*xs, 3.0, 1.0, 2.0, 0.0, res, ws)
+    assert torch.equal(plain, res)
+    # a large input (more blocks than the partial-sum table holds: grid-stride)
+    n = 9_000_000
+    xs = [torch.randn(n, device=DEV) for _ in range(4)]
+    ws = nat.guide_rescale_workspace(n, xs[0].device)
+    res = torch.empty_like(xs[0])
+    nat.guide_rescale(*xs, 3.0, 1.0, 2.0, 0.5, res, ws)
+    ref = ltx_oracle.guide(*[x.double() for x in xs], 3.0, 1.0, 0.5, 2.0)
+    assert rel_l2(res, ref) < 1e-6
+
+
 # ------------------------------------------------------------------- fused head + Euler
 
 

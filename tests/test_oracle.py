@@ -85,3 +85,11 @@ def test_oracle_schedule_and_positions_match_reference():
     assert torch.equal(ltx_oracle.scheduler_sigmas(8, 480), s["sigmas8_tokens480"])
     assert torch.equal(ltx_oracle.video_positions(1, 3, 4, 5, 24.0), s["video_positions"])
     assert torch.equal(ltx_oracle.audio_positions(1, 7), s["audio_positions"])
+
+
+def test_oracle_guide_matches_reference():
+    """guide() with and without the std rescale (ltx_dit.py:551-562), fp32 and bf16."""
+    rec = torch.load(gc.GOLDEN / "guide.pt", weights_only=False)
+    for case in rec["cases"].values():
+        for (cfg, stg, rs, mod), out in zip(rec["params"], case["outputs"]):
+            assert torch.equal(ltx_oracle.guide(*case["inputs"], cfg, stg, rs, mod), out)
