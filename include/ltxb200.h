@@ -203,6 +203,17 @@ size_t ltx_guide_rescale_workspace_bytes(int64_t n);
 int ltx_guide_rescale(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
                       float cfg_scale, float stg_scale, float modality_scale, float rescale_scale, void* out,
                       void* workspace, size_t workspace_bytes, int dtype, void* stream);
+/* ltx_guide_rescale without a caller workspace: the same two kernels, same results, with
+ * the scratch in a static device array of 8208 bytes, so the call allocates nothing. It
+ * takes n <= 1,048,576 elements (one video latent of the benchmark configurations is
+ * 786,432) and rejects larger n with an error. The scratch's completion counter starts
+ * at zero at module load and every call leaves it zero. One scratch per device: calls
+ * that overlap in time on the same device (several streams or threads) race on it. The
+ * first call on a device looks up the scratch's address (cudaGetSymbolAddress); make
+ * that first call before any stream capture. No counterpart in the reference. */
+int ltx_guide_rescale_noalloc(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
+                              float cfg_scale, float stg_scale, float modality_scale, float rescale_scale, void* out,
+                              int dtype, void* stream);
 /* Euler step (ltx_dit.py:602-606): v = round((sample-denoised)/sigma);
  * out = sample + v*(sigma_next - sigma). */
 int ltx_euler(const void* sample, const void* denoised, int64_t n, float sigma, float sigma_next, void* out,

@@ -102,6 +102,8 @@ _SIGNATURES = {
                                  ctypes.c_int, c_vp]),
     "ltx_euler": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
     "ltx_guide_rescale_workspace_bytes": (ctypes.c_size_t, [c_i64]),
+    "ltx_guide_rescale_noalloc": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float,
+                                                 ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
     "ltx_guide_rescale": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                          ctypes.c_float, c_vp, c_vp, ctypes.c_size_t, ctypes.c_int, c_vp]),
     "ltx_proj_out_cfg_euler": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, ctypes.c_int, c_i64, c_vp, c_vp,
@@ -395,6 +397,14 @@ def guide_rescale(cond: torch.Tensor, uncond: torch.Tensor, ptb: torch.Tensor, m
                   workspace: torch.Tensor) -> None:
     _call("ltx_guide_rescale", _ptr(cond), _ptr(uncond), _ptr(ptb), _ptr(mod), cond.numel(), cfg_scale, stg_scale,
           modality_scale, rescale_scale, _ptr(out), _ptr(workspace), workspace.numel(), _dt(cond), _stream(cond))
+
+
+def guide_rescale_noalloc(cond: torch.Tensor, uncond: torch.Tensor, ptb: torch.Tensor, mod: torch.Tensor,
+                          cfg_scale: float, stg_scale: float, modality_scale: float, rescale_scale: float,
+                          out: torch.Tensor) -> None:
+    """guide_rescale with the library's static scratch (no workspace, n <= 1,048,576)."""
+    _call("ltx_guide_rescale_noalloc", _ptr(cond), _ptr(uncond), _ptr(ptb), _ptr(mod), cond.numel(), cfg_scale,
+          stg_scale, modality_scale, rescale_scale, _ptr(out), _dt(cond), _stream(cond))
 
 
 def euler(sample: torch.Tensor, denoised: torch.Tensor, sigma: float, sigma_next: float, out: torch.Tensor) -> None:

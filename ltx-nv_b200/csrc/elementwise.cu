@@ -8,6 +8,7 @@
 // at the points where the reference's op-by-op PyTorch code rounds (each torch op on a
 // bf16 tensor returns a rounded bf16 tensor).
 #include <algorithm>
+#include <string>
 #include <type_traits>
 
 #include "ltx_kernels.cuh"
@@ -954,6 +955,47 @@ extern "C" int ltx_guide_rescale(const void* cond, const void* uncond, const voi
   LTX_REQUIRE(workspace_bytes >= guide_rescale_ws_bytes(n), "workspace too small (ltx_guide_rescale_workspace_bytes)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto ws = static_cast<GuideWs*>(workspace);
+  if (dtype == LTX_F32)
+    launch_guide_rescale<float>(cond, uncond, ptb, mod, n, cfg_scale - 1.f, stg_scale, modality_scale - 1.f,
+                                rescale_scale, out, ws, s);
+  else
+    launch_guide_rescale<__nv_bfloat16>(cond, uncond, ptb, mod, n, cfg_scale - 1.f, stg_scale,
+                                        modality_scale - 1.f, rescale_scale, out, ws, s);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+// Allocation-free variant: the scratch is a file-scope device array. Static device
+// memory starts zeroed at module load, so the completion counter starts at zero and each
+// call leaves it at zero. One scratch per device: overlapping calls race on it.
+constexpr int kGuideStaticBlocks = 256;  // n <= 256 * kGuideElemsPerBlock = 1,048,576
+constexpr size_t kGuideStaticBytes = sizeof(GuideWs) + size_t(kGuideStaticBlocks) * 4 * sizeof(double);
+static __device__ __align__(256) unsigned char g_guide_scratch[kGuideStaticBytes];
+
+extern "C" int ltx_guide_rescale_noalloc(const void* cond, const void* uncond, const void* ptb, const void* mod,
+                                         int64_t n, float cfg_scale, float stg_scale, float modality_scale,
+                                         float rescale_scale, void* out, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(cond && uncond && ptb && mod && out, "NULL argument");
+  LTX_REQUIRE(n > 1, "n must be at least 2 (unbiased std)");
+  if (guide_rescale_ws_bytes(n) > kGuideStaticBytes)
+    throw ApiError{LTX_ERR_INVALID, "n = " + std::to_string(n) + " exceeds the static scratch of " +
+                                        std::to_string(kGuideStaticBytes) + " bytes (at most " +
+                                        std::to_string(int64_t(kGuideStaticBlocks) * kGuideElemsPerBlock) +
+                                        " elements); use ltx_guide_rescale with a workspace"};
+  // device address of the scratch, looked up once per device
+  static void* scratch_ptr[64] = {};
+  int dev = 0;
+  LTX_CUDA(cudaGetDevice(&dev));
+  LTX_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range");
+  if (scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    LTX_CUDA(cudaGetSymbolAddress(&ptr, g_guide_scratch));
+    scratch_ptr[dev] = ptr;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto ws = static_cast<GuideWs*>(scratch_ptr[dev]);
   if (dtype == LTX_F32)
     launch_guide_rescale<float>(cond, uncond, ptb, mod, n, cfg_scale - 1.f, stg_scale, modality_scale - 1.f,
                                 rescale_scale, out, ws, s);
