@@ -188,6 +188,13 @@ int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const 
 int ltx_cfg_euler(const void* vel, const void* latent, const float* timesteps, int64_t T, int C, float cfg_scale,
                   float sigma, float sigma_next, void* denoised, void* new_latent, int dtype, void* stream);
 
+/* Perturbed self-attention (STG, ltx_nn.py:209-210 and the 0/1 blend at 229-230): the
+ * attention output of `rows` rows is V itself, then gated per (token, head) by
+ * 2*sigmoid(logit) like a real attention output (231-235; gate_logits may be NULL). The
+ * caller passes the rows of the perturbed samples. */
+int ltx_value_gate(const void* v, int64_t ldv, const void* gate_logits, int64_t ld_gate, void* o, int64_t ldo,
+                   int64_t rows, int heads, int head_dim, int dtype, void* stream);
+
 /* Guidance blend of four x0 predictions (ltx_dit.py:551-557, rescale_scale = 0):
  * out = cond + (cfg-1)(cond-uncond) + stg(cond-ptb) + (modality-1)(cond-mod). */
 int ltx_guide(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n, float cfg_scale,
@@ -214,6 +221,10 @@ int ltx_guide_rescale(const void* cond, const void* uncond, const void* ptb, con
 int ltx_guide_rescale_noalloc(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
                               float cfg_scale, float stg_scale, float modality_scale, float rescale_scale, void* out,
                               int dtype, void* stream);
+/* X0 of a velocity prediction (ltx_dit.py:591-593, X0Model): out = round(latent - v *
+ * timesteps[row]) with fp32 math; latent, velocity and out are (rows, C), timesteps fp32 (rows). */
+int ltx_x0(const void* latent, const void* velocity, const float* timesteps, int64_t rows, int C, void* out,
+           int dtype, void* stream);
 /* Euler step (ltx_dit.py:602-606): v = round((sample-denoised)/sigma);
  * out = sample + v*(sigma_next - sigma). */
 int ltx_euler(const void* sample, const void* denoised, int64_t n, float sigma, float sigma_next, void* out,

@@ -101,6 +101,9 @@ _SIGNATURES = {
     "ltx_guide": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp,
                                  ctypes.c_int, c_vp]),
     "ltx_euler": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
+    "ltx_value_gate": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int, c_vp]),
+    "ltx_x0": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, c_vp, ctypes.c_int, c_vp]),
     "ltx_guide_rescale_workspace_bytes": (ctypes.c_size_t, [c_i64]),
     "ltx_guide_rescale_noalloc": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float,
                                                  ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
@@ -383,6 +386,22 @@ def guide(cond: torch.Tensor, uncond: torch.Tensor, ptb: torch.Tensor, mod: torc
           stg_scale: float, modality_scale: float, out: torch.Tensor) -> None:
     _call("ltx_guide", _ptr(cond), _ptr(uncond), _ptr(ptb), _ptr(mod), cond.numel(), cfg_scale, stg_scale,
           modality_scale, _ptr(out), _dt(cond), _stream(cond))
+
+
+def value_gate(v: torch.Tensor, gate_logits: torch.Tensor | None, o: torch.Tensor, heads: int, head_dim: int) -> None:
+    """o = V gated by 2*sigmoid(logit) per (row, head): the STG-perturbed attention output.
+    v / o (rows, >= H*d) row-major views, gate (rows, >= H)."""
+    _call("ltx_value_gate", _ptr(v), _ld(v), _ptr(gate_logits), _ld(gate_logits) if gate_logits is not None else 0,
+          _ptr(o), _ld(o), v.shape[0], heads, head_dim, _dt(v), _stream(v))
+
+
+def x0(latent: torch.Tensor, velocity: torch.Tensor, timesteps: torch.Tensor, out: torch.Tensor) -> None:
+    """out = round(latent - velocity * timesteps) over (rows, C); timesteps fp32 (rows,)."""
+    c = latent.shape[-1]
+    rows = latent.numel() // c
+    if timesteps.dtype != torch.float32 or not timesteps.is_contiguous() or timesteps.numel() != rows:
+        raise ValueError("timesteps must be a contiguous float32 tensor with one entry per row")
+    _call("ltx_x0", _ptr(latent), _ptr(velocity), _ptr(timesteps), rows, c, _ptr(out), _dt(latent), _stream(latent))
 
 
 def guide_rescale_workspace(n: int, device: torch.device) -> torch.Tensor:

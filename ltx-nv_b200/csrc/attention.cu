@@ -29,6 +29,7 @@
 //
 // fp32 path: CUDA-core online-softmax kernel, one query per thread (accuracy mode).
 #include <algorithm>
+#include <type_traits>
 
 #include "ltx_kernels.cuh"
 
@@ -739,11 +740,71 @@ void launch_fmha_kv1(const void* q, int64_t ldq, const void* k, int64_t ldk, con
       ltx::note_launch();
 }
 
+// ---------------------------------------------------------------------------------
+// Perturbed self-attention (STG): the attention output is replaced by V
+// (ltx_nn.py:209-210, and the blend at 229-230 with a 0/1 per-sample mask), then the
+// per-(token, head) gate 2*sigmoid(logit) applies as for a real attention output
+// (231-235). One thread per 8 consecutive elements of one head.
+// ---------------------------------------------------------------------------------
+template <typename T>
+__global__ void value_gate_kernel(const T* __restrict__ v, int64_t ldv, const T* __restrict__ gate, int64_t ld_gate,
+                                  T* __restrict__ o, int64_t ldo, int64_t rows, int heads, int d) {
+  const int per_row = heads * d / 8;
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * per_row) return;
+  const int64_t r = i / per_row;
+  const int c = int(i - r * per_row) * 8;
+  float x[8];
+  ld8<T>(v + r * ldv + c, x);
+  if (gate != nullptr) {
+    const float lg = ld_elem<T>(gate + r * ld_gate + c / d);
+    float g;
+    if constexpr (std::is_same<T, float>::value) {
+      g = 2.f / (1.f + expf(-lg));
+    } else {
+      const float sg = round_bf16(1.f / (1.f + expf(-lg)));
+      g = round_bf16(2.f * sg);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[k] *= g;
+  }
+  st8<T>(o + r * ldo + c, x);
+}
+
 }  // namespace detail
 }  // namespace ltx
 
 using namespace ltx;
 using namespace ltx::detail;
+
+extern "C" int ltx_value_gate(const void* v, int64_t ldv, const void* gate_logits, int64_t ld_gate, void* o,
+                              int64_t ldo, int64_t rows, int heads, int head_dim, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(dtype == LTX_F32 || dtype == LTX_BF16, "dtype must be F32 or BF16");
+  LTX_REQUIRE(v && o, "v and o must be non-NULL");
+  LTX_REQUIRE(rows > 0 && heads > 0 && head_dim > 0 && head_dim % 8 == 0, "bad shape (head_dim % 8 == 0)");
+  const int64_t inner = int64_t(heads) * head_dim;
+  LTX_REQUIRE(ldv >= inner && ldo >= inner && ldv % 8 == 0 && ldo % 8 == 0,
+              "ldv / ldo must be multiples of 8 and >= heads*head_dim");
+  if (gate_logits) LTX_REQUIRE(ld_gate >= heads, "ld_gate must be >= heads");
+  check_vec_ptr(v, "v");
+  check_vec_ptr(o, "o");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n = rows * (inner / 8);
+  const unsigned blocks = unsigned((n + 255) / 256);
+  if (dtype == LTX_F32)
+    value_gate_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(v), ldv,
+                                                    static_cast<const float*>(gate_logits), ld_gate,
+                                                    static_cast<float*>(o), ldo, rows, heads, head_dim),
+        ltx::note_launch();
+  else
+    value_gate_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(v), ldv, static_cast<const __nv_bfloat16*>(gate_logits), ld_gate,
+        static_cast<__nv_bfloat16*>(o), ldo, rows, heads, head_dim),
+        ltx::note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
 
 extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                              void* o, int64_t ldo, int B, int64_t Tq, int64_t Tk, int heads, int head_dim,

@@ -610,6 +610,15 @@ void launch_guide_rescale(const void* cond, const void* uncond, const void* ptb,
       ltx::note_launch();
 }
 
+// X0 from a velocity (ltx_dit.py:591-593): out = round(latent - v * timesteps[row]).
+template <typename T>
+__global__ void x0_kernel(const T* __restrict__ latent, const T* __restrict__ vel, const float* __restrict__ ts,
+                          int64_t rows, int C, T* __restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * C) return;
+  st_elem<T>(out + i, __fsub_rn(ld_elem<T>(latent + i), __fmul_rn(ld_elem<T>(vel + i), ts[i / C])));
+}
+
 // velocity = round((sample - denoised) / sigma); out = round(sample + velocity * dt).
 template <typename T>
 __global__ void euler_kernel(const T* __restrict__ s, const T* __restrict__ d, int64_t n, float sigma, float dt,
@@ -1002,6 +1011,25 @@ extern "C" int ltx_guide_rescale_noalloc(const void* cond, const void* uncond, c
   else
     launch_guide_rescale<__nv_bfloat16>(cond, uncond, ptb, mod, n, cfg_scale - 1.f, stg_scale,
                                         modality_scale - 1.f, rescale_scale, out, ws, s);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_x0(const void* latent, const void* velocity, const float* timesteps, int64_t rows, int C,
+                      void* out, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(latent && velocity && timesteps && out, "NULL argument");
+  LTX_REQUIRE(rows > 0 && C > 0, "rows and C must be positive");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = unsigned((rows * C + 255) / 256);
+  if (dtype == LTX_F32)
+    x0_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(latent), static_cast<const float*>(velocity),
+                                            timesteps, rows, C, static_cast<float*>(out)), ltx::note_launch();
+  else
+    x0_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(latent),
+                                                    static_cast<const __nv_bfloat16*>(velocity), timesteps, rows, C,
+                                                    static_cast<__nv_bfloat16*>(out)), ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

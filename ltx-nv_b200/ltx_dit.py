@@ -21,8 +21,11 @@ through _native (no cuBLAS, no cuDNN, no torch element-wise math on the path):
 Activations are (B*T, D) row-major buffers in HBM; the residual stream is updated in
 place by the GEMM epilogues.
 
-Supported guidance in this build: CFG (cond/uncond). STG and modality-isolation passes
-(partial perturbation masks) and guidance rescale raise NotImplementedError.
+Guidance: cfg_denoise_step is the fused CFG-only step (B=2, X0 + CFG + Euler in the
+proj_out epilogue). guided_denoise_step / run_dit run the reference's full guidance: one
+B=4 forward over [cond, uncond, STG-perturbed, modality-isolated] (perturbed
+self-attention outputs V, ltx_value_gate; isolated samples skip the A<->V residual
+update), X0, and the blend with the two-pass std rescale (ltx_guide_rescale).
 """
 
 from __future__ import annotations
@@ -345,8 +348,10 @@ class LTXModel(torch.nn.Module):
                        context, s_len, pe, cross_pe, cross_ss, cross_gate, m.enabled, context_src=m.context)
 
     # ------------------------------------------------------------------ block pieces
-    def _self_and_text(self, blk: Block, st: _Stream, h: torch.Tensor):
-        """Self-attention + text cross-attention of one stream (ltx_dit.py:259-282)."""
+    def _self_and_text(self, blk: Block, st: _Stream, h: torch.Tensor, keep_self: list | None = None):
+        """Self-attention + text cross-attention of one stream (ltx_dit.py:259-282).
+        keep_self: per-sample self-attention keep flags of this block (STG: 0 = the
+        attention output is V, ltx_nn.py:209-210, 229-230)."""
         cfg = self.cfg
         a = st.name == "audio"
         attn1 = blk.audio_attn1 if a else blk.attn1
@@ -358,12 +363,24 @@ class LTXModel(torch.nn.Module):
         # self-attention
         nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_RMS, eps, st.mod(table, st.tmod, 0, 1))
         qkv = attn1.project_qkv(h, st.T, st.pe)
+        perturbed = [b for b, k in enumerate(keep_self) if k == 0] if keep_self is not None else []
+        v_cols = qkv[:, 2 * inner:3 * inner]
+        g_cols = qkv[:, 3 * inner:3 * inner + attn1.heads] if gated else None
         if self._sp is not None and not a:
             # sequence-parallel: this rank holds st.T of the video tokens (ltx_parallel)
+            if perturbed:
+                raise NotImplementedError("STG perturbation under sequence parallelism")
             o = self._sp.self_attention(attn1, qkv, st)
+        elif len(perturbed) == st.B:
+            # every sample perturbed: no attention at all (ltx_nn.py:209-210)
+            o = torch.empty(rows, inner, device=h.device, dtype=h.dtype)
+            nat.value_gate(v_cols, g_cols, o, attn1.heads, attn1.dim_head)
         else:
-            o = attn1.attend(qkv[:, :inner], qkv[:, inner:2 * inner], qkv[:, 2 * inner:3 * inner],
-                             qkv[:, 3 * inner:3 * inner + attn1.heads] if gated else None, st.B, st.T, st.T)
+            o = attn1.attend(qkv[:, :inner], qkv[:, inner:2 * inner], v_cols, g_cols, st.B, st.T, st.T)
+            for b in perturbed:
+                r0, r1 = b * st.T, (b + 1) * st.T
+                nat.value_gate(v_cols[r0:r1], g_cols[r0:r1] if gated else None, o[r0:r1], attn1.heads,
+                               attn1.dim_head)
         nat.linear(o, attn1.to_out.weight, st.x,
                    nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn1.to_out.bias, residual=st.x,
                                 gate=st.mod(table, st.tmod, None, 2), rows_per_batch=st.T))
@@ -410,8 +427,11 @@ class LTXModel(torch.nn.Module):
                    nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=ff.proj_out.bias, residual=st.x,
                                 gate=st.mod(table, st.tmod, None, 5), rows_per_batch=st.T))
 
-    def _av_cross(self, blk: Block, vs: _Stream, as_: _Stream, run_a2v: bool, run_v2a: bool):
-        """Audio<->video cross-attention (ltx_dit.py:284-307); both read the pre-AV states."""
+    def _av_cross(self, blk: Block, vs: _Stream, as_: _Stream, run_a2v: bool, run_v2a: bool,
+                  keep_a2v: list | None = None, keep_v2a: list | None = None):
+        """Audio<->video cross-attention (ltx_dit.py:284-307); both read the pre-AV states.
+        keep_*: per-sample keep flags (modality isolation: 0 = the sample's update is
+        skipped, which is what the reference's multiply by a 0 mask leaves)."""
         cfg = self.cfg
         eps = cfg.norm_eps
         tv, ta = blk.scale_shift_table_a2v_ca_video, blk.scale_shift_table_a2v_ca_audio
@@ -425,7 +445,7 @@ class LTXModel(torch.nn.Module):
 
         def gate_of(st, table):
             d = table.shape[-1]
-            return nat.modulation(table, st.cross_gate, shift=None, scale=(4 * d, 0), mod_ld_batch=d)
+            return lambda b0: nat.modulation(table, st.cross_gate[b0:], shift=None, scale=(4 * d, 0), mod_ld_batch=d)
 
         a2v_v = normed(vs, tv, 0) if run_a2v else None
         a2v_a = normed(as_, ta, 0) if run_a2v else None
@@ -433,13 +453,15 @@ class LTXModel(torch.nn.Module):
         v2a_v = normed(vs, tv, 2) if run_v2a else None
         if run_a2v:
             self._cross_attend(blk.audio_to_video_attn, a2v_v, vs, a2v_a, as_, vs.cross_pe, as_.cross_pe,
-                               gate_of(vs, tv), vs)
+                               gate_of(vs, tv), vs, keep_a2v)
         if run_v2a:
             self._cross_attend(blk.video_to_audio_attn, v2a_a, as_, v2a_v, vs, as_.cross_pe, vs.cross_pe,
-                               gate_of(as_, ta), as_)
+                               gate_of(as_, ta), as_, keep_v2a)
 
-    def _cross_attend(self, attn: Attention, q_in, q_st: _Stream, kv_in, kv_st: _Stream, q_pe, k_pe, gate,
-                      out_st: _Stream):
+    def _cross_attend(self, attn: Attention, q_in, q_st: _Stream, kv_in, kv_st: _Stream, q_pe, k_pe, gate_at,
+                      out_st: _Stream, keep: list | None = None):
+        """gate_at(b0): the gate modulation seen from sample b0 on. The residual update
+        runs over the runs of kept samples only."""
         inner = attn.heads * attn.dim_head
         gated = self.cfg.gated_attention
         wq, bq = attn.packed_q()
@@ -452,23 +474,36 @@ class LTXModel(torch.nn.Module):
         attn._norm_rope(kv[:, :inner], kv_st.T, attn.k_norm.weight, k_pe)
         o = attn.attend(qg[:, :inner], kv[:, :inner], kv[:, inner:2 * inner], qg[:, inner:] if gated else None,
                         q_st.B, q_st.T, kv_st.T)
-        nat.linear(o, attn.to_out.weight, out_st.x,
-                   nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn.to_out.bias, residual=out_st.x, gate=gate,
-                                rows_per_batch=out_st.T))
+        runs, b = [], 0
+        kept = keep if keep is not None else [1.0] * out_st.B
+        while b < out_st.B:
+            if kept[b] == 0:
+                b += 1
+                continue
+            b0 = b
+            while b < out_st.B and kept[b] != 0:
+                b += 1
+            runs.append((b0, b))
+        t = out_st.T
+        for b0, b1 in runs:
+            x = out_st.x[b0 * t:b1 * t]
+            nat.linear(o[b0 * t:b1 * t], attn.to_out.weight, x,
+                       nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn.to_out.bias, residual=x, gate=gate_at(b0),
+                                    rows_per_batch=t))
 
     # ------------------------------------------------------------------ forward
     def _keep_masks(self, perturbations, batch: int):
-        """Host copy of the (4, L, B) keep-mask (ltx_dit.py:381-411); None = all ones."""
+        """Host copy of the (4, L, B) keep-mask (ltx_dit.py:381-411) as nested lists; None =
+        all ones. Entries are 0 (perturbed / skipped) or 1, as build_perturbation_config
+        makes them."""
         if perturbations is None:
             return None
         keep = perturbations.detach().to("cpu", torch.float32)
-        if bool((keep[0:2] != 1).any()):
-            raise NotImplementedError("self-attention perturbation (STG) is not supported yet")
-        rows = keep[2:4]
-        mixed = (rows != 0).any(dim=-1) & (rows != 1).any(dim=-1)
-        if bool(mixed.any()):
-            raise NotImplementedError("partial A2V/V2A perturbation masks (modality guidance) are not supported yet")
-        return keep
+        if bool(((keep != 0) & (keep != 1)).any()):
+            raise NotImplementedError("perturbation keep-masks other than 0 / 1")
+        if keep.shape[-1] != batch:
+            raise ValueError(f"perturbation batch {keep.shape[-1]} != model batch {batch}")
+        return keep.tolist()
 
     def run_blocks(self, va: _Stream | None, aa: _Stream | None, perturbations=None):
         keep = self._keep_masks(perturbations, (va or aa).B)
@@ -479,15 +514,17 @@ class LTXModel(torch.nn.Module):
             run_a = aa is not None and aa.enabled and aa.x.numel() > 0
             run_a2v = run_v and aa is not None and aa.x.numel() > 0
             run_v2a = run_a and va is not None and va.x.numel() > 0
+            k_a2v = k_v2a = None
             if keep is not None:
-                run_a2v = run_a2v and bool((keep[2, i] != 0).any())
-                run_v2a = run_v2a and bool((keep[3, i] != 0).any())
+                k_a2v, k_v2a = keep[2][i], keep[3][i]
+                run_a2v = run_a2v and any(k != 0 for k in k_a2v)
+                run_v2a = run_v2a and any(k != 0 for k in k_v2a)
             if run_v:
-                self._self_and_text(blk, va, hv)
+                self._self_and_text(blk, va, hv, keep[0][i] if keep is not None else None)
             if run_a:
-                self._self_and_text(blk, aa, ha)
+                self._self_and_text(blk, aa, ha, keep[1][i] if keep is not None else None)
             if run_a2v or run_v2a:
-                self._av_cross(blk, va, aa, run_a2v, run_v2a)
+                self._av_cross(blk, va, aa, run_a2v, run_v2a, k_a2v, k_v2a)
             if run_v:
                 self._ffn(blk, va, hv)
             if run_a:
@@ -784,32 +821,66 @@ def euler_step(sample: torch.Tensor, denoised: torch.Tensor, sigmas: torch.Tenso
     return out
 
 
+@torch.inference_mode()
 def guided_denoise_step(model: LTXModel, video_state: LatentState, audio_state: LatentState | None, contexts: dict,
                         sigma: torch.Tensor, step_idx: int, v_params: GuiderParams, a_params: GuiderParams | None,
                         cfg: DiTConfig):
-    raise NotImplementedError("the 4-pass (cond/uncond/STG/modality) guidance batch is not supported yet; "
-                              "run_dit with CFG-only GuiderParams uses cfg_denoise_step")
+    """One transformer call with the B=4 guidance passes [cond, uncond, ptb (STG), mod
+    (A<->V isolated)] -> blended x0 per modality (ltx_dit.py:565-599): the perturbation
+    keep-mask of build_perturbation_config, X0 per pass, guide() with rescale."""
+    passes = ["cond", "uncond", "ptb", "mod"]
+    n = len(passes)
+    sigma = sigma.reshape(()).to(torch.float32)
+    dev = video_state.latent.device
+    sigma_b = sigma.to(dev).expand(n)
+    dtype = model.proj_out.weight.dtype
+    v_ctx = torch.cat([contexts["v_pos"], contexts["v_neg"], contexts["v_pos"], contexts["v_pos"]], dim=0)
+    v_lat = video_state.latent.repeat(n, 1, 1)
+    video = Modality(latent=v_lat, sigma=sigma_b,
+                     timesteps=video_state.denoise_mask.repeat(n, 1, 1) * sigma_b.view(n, 1, 1),
+                     positions=video_state.positions.repeat(n, 1, 1, 1), context=v_ctx,
+                     keyframes_mask=video_state.keyframes_mask.repeat(n, 1, 1)
+                     if video_state.keyframes_mask is not None else None)
+    audio = None
+    if audio_state is not None:
+        a_ctx = torch.cat([contexts["a_pos"], contexts["a_neg"], contexts["a_pos"], contexts["a_pos"]], dim=0)
+        a_lat = audio_state.latent.repeat(n, 1, 1)
+        audio = Modality(latent=a_lat, sigma=sigma_b,
+                         timesteps=audio_state.denoise_mask.repeat(n, 1, 1) * sigma_b.view(n, 1, 1),
+                         positions=audio_state.positions.repeat(n, 1, 1, 1), context=a_ctx)
+    a_blocks = list(a_params.stg_blocks) if a_params is not None else []
+    keep = build_perturbation_config(cfg.num_layers, passes, list(v_params.stg_blocks), a_blocks, dev, dtype)
+    vx, ax = model(video, audio, keep)
+    def x0(lat, vel, ts):
+        out = torch.empty_like(vel)
+        nat.x0(lat.to(vel.dtype).contiguous(), vel.contiguous(), ts.to(torch.float32).reshape(-1).contiguous(), out)
+        return out
+
+    vs_ = x0(v_lat, vx, video.timesteps).chunk(n)
+    if audio is not None:
+        as_ = x0(audio.latent, ax, audio.timesteps).chunk(n)
+    else:
+        as_ = (None,) * n
+    r = dict(zip(passes, zip(vs_, as_)))
+    denoised_video = guide(*[r[p][0] for p in passes], v_params)
+    denoised_audio = guide(*[r[p][1] for p in passes], a_params) if audio is not None else None
+    return denoised_video, denoised_audio, r
 
 
 @torch.inference_mode()
 def run_dit(model: LTXModel, cfg: DiTConfig, contexts: dict, video_state: LatentState,
             audio_state: LatentState | None, sigmas: torch.Tensor, v_params: GuiderParams,
             a_params: GuiderParams | None, on_step=None) -> tuple[torch.Tensor, torch.Tensor | None]:
-    """Denoising loop (ltx_dit.py:609-621). Video-only CFG guidance in this build."""
-    if audio_state is not None or not v_params.cfg_only:
-        raise NotImplementedError("this build runs video-only CFG guidance (audio / STG / modality / rescale: next)")
-    latent = video_state.latent
-    if latent.shape[0] != 1:
-        raise ValueError("run_dit denoises one latent (batch 1); CFG makes the model batch 2")
+    """Denoising loop (ltx_dit.py:609-621): guided_denoise_step (the 4-pass guidance
+    batch) and an Euler update per modality at every step. Without an audio state the
+    audio stream is left out of the batch."""
     for idx in range(len(sigmas) - 1):
         t0 = time.perf_counter()
-        vel, den, nxt = cfg_denoise_step(model, latent, video_state.positions[:1], contexts["v_pos"],
-                                         contexts["v_neg"], sigmas, idx, v_params.cfg_scale,
-                                         keyframes_mask=video_state.keyframes_mask[:1]
-                                         if video_state.keyframes_mask is not None else None)
-        latent = nxt
-        video_state = replace(video_state, latent=latent)
+        dv, da, passes = guided_denoise_step(model, video_state, audio_state, contexts, sigmas[idx], idx, v_params,
+                                             a_params, cfg)
+        video_state = replace(video_state, latent=euler_step(video_state.latent, dv, sigmas, idx))
+        if audio_state is not None:
+            audio_state = replace(audio_state, latent=euler_step(audio_state.latent, da, sigmas, idx))
         if on_step:
-            on_step(idx, time.perf_counter() - t0, den, None, {"cond": (vel[0:1], None), "uncond": (vel[1:2], None)},
-                    video_state, audio_state)
-    return video_state.latent, None
+            on_step(idx, time.perf_counter() - t0, dv, da, passes, video_state, audio_state)
+    return video_state.latent, audio_state.latent if audio_state is not None else None

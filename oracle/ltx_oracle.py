@@ -110,20 +110,27 @@ def adaln_single(w, name, t, dtype):
     return linear(w, name + ".linear", F.silu(emb)), emb
 
 
-def attention(w, name, x, heads, dim_head, eps, context=None, pe=None, k_pe=None, gated=True):
-    """ltx_nn.py:194-236 without perturbation masks."""
+def attention(w, name, x, heads, dim_head, eps, context=None, pe=None, k_pe=None, gated=True,
+              perturbation_mask=None, all_perturbed=False):
+    """ltx_nn.py:194-236. STG: all_perturbed -> out = V (:209-210); a per-sample
+    perturbation_mask (B, 1, 1) blends out * mask + V * (1 - mask) (:229-230)."""
     context = x if context is None else context
     b = x.shape[0]
     v = linear(w, name + ".to_v", context)
-    q = rms_norm(linear(w, name + ".to_q", x), eps, w[name + ".q_norm.weight"])
-    k = rms_norm(linear(w, name + ".to_k", context), eps, w[name + ".k_norm.weight"])
-    if pe is not None:
-        q = apply_rope(q, pe)
-        k = apply_rope(k, pe if k_pe is None else k_pe)
-    q = q.view(b, -1, heads, dim_head).transpose(1, 2)
-    k = k.view(b, -1, heads, dim_head).transpose(1, 2)
-    v4 = v.view(b, -1, heads, dim_head).transpose(1, 2)
-    out = sdpa(q, k, v4).transpose(1, 2).reshape(b, -1, heads * dim_head)
+    if all_perturbed:
+        out = v
+    else:
+        q = rms_norm(linear(w, name + ".to_q", x), eps, w[name + ".q_norm.weight"])
+        k = rms_norm(linear(w, name + ".to_k", context), eps, w[name + ".k_norm.weight"])
+        if pe is not None:
+            q = apply_rope(q, pe)
+            k = apply_rope(k, pe if k_pe is None else k_pe)
+        q = q.view(b, -1, heads, dim_head).transpose(1, 2)
+        k = k.view(b, -1, heads, dim_head).transpose(1, 2)
+        v4 = v.view(b, -1, heads, dim_head).transpose(1, 2)
+        out = sdpa(q, k, v4).transpose(1, 2).reshape(b, -1, heads * dim_head)
+        if perturbation_mask is not None:
+            out = out * perturbation_mask + v * (1 - perturbation_mask)
     if gated and (name + ".to_gate_logits.weight") in w:
         g = linear(w, name + ".to_gate_logits", x)
         t = out.shape[1]
@@ -237,6 +244,16 @@ def text_cross(w, cfg, name, sst_name, psst_name, x_normed, args: StreamArgs, he
     return attention(w, name, x_normed, heads, d, cfg.norm_eps, context=args.context, gated=cfg.gated_attention)
 
 
+def _self_ptb(keep_row):
+    """apply_block_perturbations (ltx_dit.py:381-394) for one self-attention row:
+    (perturbation_mask or None, all_perturbed)."""
+    if keep_row is None:
+        return None, False
+    all_p = bool((keep_row == 0).all())
+    any_p = bool((keep_row == 0).any())
+    return (keep_row.reshape(-1, 1, 1) if any_p and not all_p else None), all_p
+
+
 def block(w, cfg, i, va: StreamArgs | None, aa: StreamArgs | None, keep=None):
     """ltx_dit.py:250-317. keep: (4, B) keep-mask rows of this block, or None (all ones)."""
     p = f"blocks.{i}."
@@ -251,15 +268,17 @@ def block(w, cfg, i, va: StreamArgs | None, aa: StreamArgs | None, keep=None):
     run_v2a = run_a and vx is not None and vx.numel() > 0
     if run_v:
         sh, sc, g = ada(w[p + "scale_shift_table"], vx.shape[0], va.mod, slice(0, 3))
+        pm, allp = _self_ptb(keep[0] if keep is not None else None)
         out = attention(w, p + "attn1", rms_norm(vx, eps) * (1 + sc) + sh, vh, vd, eps, pe=va.pe,
-                        gated=cfg.gated_attention)
+                        gated=cfg.gated_attention, perturbation_mask=pm, all_perturbed=allp)
         vx = vx + out * g
         vx = vx + text_cross(w, cfg, p + "attn2", p + "scale_shift_table", p + "prompt_scale_shift_table",
                              rms_norm(vx, eps), va, vh, vd)
     if run_a:
         sh, sc, g = ada(w[p + "audio_scale_shift_table"], ax.shape[0], aa.mod, slice(0, 3))
+        pm, allp = _self_ptb(keep[1] if keep is not None else None)
         out = attention(w, p + "audio_attn1", rms_norm(ax, eps) * (1 + sc) + sh, ah, ad, eps, pe=aa.pe,
-                        gated=cfg.gated_attention)
+                        gated=cfg.gated_attention, perturbation_mask=pm, all_perturbed=allp)
         ax = ax + out * g
         ax = ax + text_cross(w, cfg, p + "audio_attn2", p + "audio_scale_shift_table",
                              p + "audio_prompt_scale_shift_table", rms_norm(ax, eps), aa, ah, ad)
@@ -404,6 +423,54 @@ def cfg_denoise_step(w, cfg, latent, positions, context_pos, context_neg, sigmas
     den = guide_cfg(x0[0:1], x0[1:2], cfg_scale)
     nxt = euler_step(latent, den, sigmas, idx)
     return vx, den, nxt
+
+
+def build_perturbation_config(num_blocks, passes, v_stg_blocks, a_stg_blocks, dtype):
+    """ltx_dit.py:397-411: (4, L, B) keep-mask; 0 skip-video-self, 1 skip-audio-self,
+    2 skip-A2V, 3 skip-V2A."""
+    keep = torch.ones(4, num_blocks, len(passes), dtype=dtype)
+    for i, name in enumerate(passes):
+        if name == "ptb":
+            for blk in v_stg_blocks:
+                keep[0, blk, i] = 0
+            for blk in a_stg_blocks:
+                keep[1, blk, i] = 0
+        elif name == "mod":
+            keep[2, :, i] = 0
+            keep[3, :, i] = 0
+    return keep
+
+
+@torch.inference_mode()
+def guided_denoise_step(w, cfg, video_state, audio_state, contexts, sigma, v_params, a_params):
+    """ltx_dit.py:565-599: one B=4 forward over [cond, uncond, ptb, mod], X0 per modality
+    and the guidance blend (with rescale). State objects carry latent, denoise_mask,
+    positions and (video) keyframes_mask; params are (cfg, stg, rescale, modality,
+    stg_blocks). Returns (denoised video, denoised audio, {pass: (x0_v, x0_a)})."""
+    passes = ["cond", "uncond", "ptb", "mod"]
+    n = len(passes)
+    v_ctx = torch.cat([contexts["v_pos"], contexts["v_neg"], contexts["v_pos"], contexts["v_pos"]], dim=0)
+    a_ctx = torch.cat([contexts["a_pos"], contexts["a_neg"], contexts["a_pos"], contexts["a_pos"]], dim=0)
+    sigma_b = sigma.expand(n)
+    v_lat = video_state["latent"].repeat(n, 1, 1)
+    a_lat = audio_state["latent"].repeat(n, 1, 1)
+    kf = video_state.get("keyframes_mask")
+    video = Modality(latent=v_lat, sigma=sigma_b,
+                     timesteps=video_state["denoise_mask"].repeat(n, 1, 1) * sigma_b.view(n, 1, 1),
+                     positions=video_state["positions"].repeat(n, 1, 1, 1), context=v_ctx,
+                     keyframes_mask=kf.repeat(n, 1, 1) if kf is not None else None)
+    audio = Modality(latent=a_lat, sigma=sigma_b,
+                     timesteps=audio_state["denoise_mask"].repeat(n, 1, 1) * sigma_b.view(n, 1, 1),
+                     positions=audio_state["positions"].repeat(n, 1, 1, 1), context=a_ctx)
+    keep = build_perturbation_config(cfg.num_layers, passes, list(v_params[4]), list(a_params[4]),
+                                     video_state["latent"].dtype)
+    vx, ax = forward(w, cfg, video, audio, keep)
+    x0_v = (v_lat.float() - vx.float() * video.timesteps.float()).to(vx.dtype)
+    x0_a = (a_lat.float() - ax.float() * audio.timesteps.float()).to(ax.dtype)
+    r = dict(zip(passes, zip(x0_v.chunk(n), x0_a.chunk(n))))
+    gv = guide(*[r[p][0] for p in passes], *v_params[:4])
+    ga = guide(*[r[p][1] for p in passes], *a_params[:4])
+    return gv, ga, r
 
 
 # ----------------------------------------------------------------------------------------

@@ -19,6 +19,8 @@ Fixtures written:
                       steps (X0 + guide + Euler).
   sched.pt            ltx2_scheduler_sigmas(30), video/audio positions.
   guide.pt            guide() with and without the std rescale on seeded x0 predictions.
+  guided_tiny_av_<dtype>.pt  two steps of guided_denoise_step (cond / uncond / STG /
+                      modality passes, rescale) + Euler on the tiny AV model.
 
 Weights are N(0, 0.02) from numpy's PCG64 (platform independent) in the reference's
 named_parameters() order, q/k RMSNorm gains offset by +1 (oracle.synthetic_state_dict).
@@ -211,16 +213,63 @@ def make_guide(ld):
     torch.save(rec, OUT / "guide.pt")
 
 
+GUIDED_V = (3.0, 1.0, 0.7, 3.0, (1,))  # cfg, stg, rescale, modality, stg_blocks (run_all.py:43-44 values)
+GUIDED_A = (7.0, 1.0, 0.7, 3.0, (1,))
+GUIDED_SIGMAS = [1.0, 0.7, 0.4]
+
+
+@torch.inference_mode()
+def make_guided(ld, dtype):
+    """Two steps of the reference's full guidance (guided_denoise_step: cond / uncond / STG /
+    modality-isolated passes in one B=4 call, std rescale, Euler) on the tiny AV model,
+    with a conditioned first frame (denoise mask 0, keyframes mask 1)."""
+    cfg = ld.DiTConfig(**CASES["tiny_av"])
+    model, shapes = build_reference_model(ld, cfg, dtype)
+    f, h, w = FRAMES
+    t = f * h * w
+    dmask = torch.ones(1, t, 1)
+    dmask[:, : h * w] = 0.0
+    kf = 1.0 - dmask
+    vs = ld.LatentState(latent=rng_normal((1, t, cfg.video_in), 300).to(dtype), denoise_mask=dmask,
+                        positions=ld.video_positions(1, f, h, w, 24.0, "cpu"),
+                        clean_latent=torch.zeros(1, t, cfg.video_in, dtype=dtype), keyframes_mask=kf)
+    aus = ld.LatentState(latent=rng_normal((1, AUDIO_T, cfg.audio_in), 301).to(dtype),
+                         denoise_mask=torch.ones(1, AUDIO_T, 1), positions=ld.audio_positions(1, AUDIO_T, "cpu"),
+                         clean_latent=torch.zeros(1, AUDIO_T, cfg.audio_in, dtype=dtype))
+    contexts = {"v_pos": rng_normal((1, TEXT_S, cfg.video_cross_dim), 302).to(dtype),
+                "v_neg": rng_normal((1, TEXT_S, cfg.video_cross_dim), 303).to(dtype),
+                "a_pos": rng_normal((1, TEXT_S, cfg.audio_cross_dim), 304).to(dtype),
+                "a_neg": rng_normal((1, TEXT_S, cfg.audio_cross_dim), 305).to(dtype)}
+    sigmas = torch.tensor(GUIDED_SIGMAS, dtype=torch.float32)
+    vp, ap = ld.GuiderParams(*GUIDED_V), ld.GuiderParams(*GUIDED_A)
+    rec = {"config": dataclasses.asdict(cfg), "param_shapes": shapes, "weight_seed": WEIGHT_SEED,
+           "dtype": str(dtype).replace("torch.", ""), "v_params": GUIDED_V, "a_params": GUIDED_A,
+           "sigmas": sigmas, "contexts": contexts,
+           "video_state": dataclasses.asdict(vs), "audio_state": dataclasses.asdict(aus), "steps": []}
+    for idx in range(len(GUIDED_SIGMAS) - 1):
+        dv, da, passes = ld.guided_denoise_step(model, vs, aus, contexts, sigmas[idx], idx, vp, ap, cfg)
+        vs = dataclasses.replace(vs, latent=ld.euler_step(vs.latent, dv, sigmas, idx))
+        aus = dataclasses.replace(aus, latent=ld.euler_step(aus.latent, da, sigmas, idx))
+        rec["steps"].append({"denoised_video": dv, "denoised_audio": da, "passes": passes,
+                             "video_latent": vs.latent, "audio_latent": aus.latent})
+    return rec
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["guide"], default=None, help="regenerate one fixture only")
+    ap.add_argument("--only", choices=["guide", "guided"], default=None, help="regenerate one fixture only")
     args = ap.parse_args()
     ref_root = Path(args.reference)
     ld = _import_reference(ref_root)
     patch_context_view(ld)
-    make_guide(ld)
-    if args.only == "guide":
+    if args.only in (None, "guide"):
+        make_guide(ld)
+    if args.only in (None, "guided"):
+        for dtype in (torch.float32, torch.bfloat16):
+            rec = make_guided(ld, dtype)
+            torch.save(rec, OUT / f"guided_tiny_av_{rec['dtype']}.pt")
+    if args.only is not None:
         return
     make_philox(ref_root)
     make_sched(ld)

@@ -31,3 +31,10 @@ def modality(d: dict | None) -> ltx_oracle.Modality | None:
     if d is None:
         return None
     return ltx_oracle.Modality(**d)
+
+
+GUIDED_CASES = ["guided_tiny_av_float32", "guided_tiny_av_bfloat16"]
+
+
+def load_guided(case: str) -> dict:
+    return torch.load(GOLDEN / f"{case}.pt", weights_only=False)

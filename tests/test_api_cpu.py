@@ -79,8 +79,18 @@ def test_schedule_positions_and_perturbations_match_oracle():
     assert keep[0, 2, 2] == 0 and keep[1, 1, 2] == 0 and keep[2:, :, 3].eq(0).all() and keep[:, :, :2].eq(1).all()
 
 
-def test_unsupported_guidance_is_rejected_loudly():
-    p = ltx_dit.GuiderParams(cfg_scale=3.0, stg_scale=1.0, rescale_scale=0.7, modality_scale=3.0, stg_blocks=(28,))
-    assert not p.cfg_only
+def test_perturbation_config_and_mask_checks():
+    """The guidance batch's keep-mask matches the oracle's restatement of
+    build_perturbation_config, and masks other than 0 / 1 are rejected loudly."""
+    from oracle import ltx_oracle
+
+    passes = ["cond", "uncond", "ptb", "mod"]
+    keep = ltx_dit.build_perturbation_config(6, passes, [5], [2, 5], torch.device("cpu"), torch.bfloat16)
+    assert torch.equal(keep, ltx_oracle.build_perturbation_config(6, passes, [5], [2, 5], torch.bfloat16))
+    with torch.device("meta"):
+        model = ltx_dit.LTXModel(ltx_dit.DiTConfig.video_only(num_layers=6, heads=2, head_dim=64, cross_dim=128))
+    assert model._keep_masks(keep, 4)[0][5] == [1.0, 1.0, 0.0, 1.0]
     with pytest.raises(NotImplementedError):
-        ltx_dit.run_dit(None, None, {}, None, object(), torch.zeros(2), p, p)
+        model._keep_masks(keep * 0.5, 4)
+    with pytest.raises(ValueError):
+        model._keep_masks(keep, 2)

@@ -391,6 +391,34 @@ def test_attention_fp32(b, tq, tk, h, d):
     assert rel_l2(o, ref) < 1e-5
 
 
+# ------------------------------------------------------------------- STG value pass-through, X0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_value_gate_and_x0(dtype):
+    torch.manual_seed(14)
+    rows, h, d = 300, 4, 64
+    qkv = torch.randn(rows, 3 * h * d + 8, device=DEV).to(dtype)
+    v, g = qkv[:, 2 * h * d:3 * h * d], qkv[:, 3 * h * d:3 * h * d + h]
+    o = torch.empty(rows, h * d, device=DEV, dtype=dtype)
+    nat.value_gate(v, g, o, h, d)
+    # reference op order: 2.0 * sigmoid(logit) in the activation dtype, then v * gate
+    gate = (2.0 * torch.sigmoid(g)).to(dtype)
+    ref = (v.view(rows, h, d) * gate.unsqueeze(-1)).reshape(rows, h * d)
+    if dtype == torch.bfloat16:
+        assert torch.equal(o, ref)
+    else:
+        assert rel_l2(o, ref) < 1e-6
+    nat.value_gate(v, None, o, h, d)
+    assert torch.equal(o, v)
+    lat = torch.randn(rows, 128, device=DEV).to(dtype)
+    vel = torch.randn(rows, 128, device=DEV).to(dtype)
+    ts = torch.rand(rows, device=DEV)
+    x = torch.empty_like(lat)
+    nat.x0(lat, vel, ts, x)
+    assert torch.equal(x, (lat.float() - vel.float() * ts[:, None]).to(dtype))
+
+
 # ------------------------------------------------------------------- guidance
 
 

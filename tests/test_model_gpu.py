@@ -2,6 +2,8 @@
 kernels) against the reference's golden outputs and the CPU oracle on the same seeded
 inputs. Tolerances (relative L2): 1e-4 in FP32 mode, 1e-2 in BF16."""
 
+import dataclasses
+
 import pytest
 import torch
 
@@ -74,6 +76,52 @@ def test_cfg_steps_match_reference_golden(case, fused):
         assert rel_l2(vel, r["velocity"]) < tol
         assert rel_l2(den, r["denoised"]) < tol
         assert rel_l2(nxt, r["latent_out"]) < tol
+
+
+def _state(d, dtype):
+    t = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in d.items()}
+    t["latent"] = t["latent"].to(dtype)
+    return ltx_dit.LatentState(**t)
+
+
+@pytest.mark.parametrize("case", gc.GUIDED_CASES)
+def test_guided_steps_match_reference_golden(case):
+    """Full guidance (cond / uncond / STG-perturbed / modality-isolated passes in one B=4
+    forward, std rescale) on the tiny AV model with a conditioned first frame: every
+    pass's x0, the blended x0 and the Euler-updated latents of two steps against the
+    reference; then run_dit over the same schedule."""
+    rec = gc.load_guided(case)
+    dtype = getattr(torch, rec["dtype"])
+    tol = TOL[rec["dtype"]]
+    model, cfg = _model(rec, dtype)
+    vp, ap = ltx_dit.GuiderParams(*rec["v_params"]), ltx_dit.GuiderParams(*rec["a_params"])
+    ctx = {k: v.to(DEV, dtype) for k, v in rec["contexts"].items()}
+    sig = rec["sigmas"].to(DEV)
+    vs0, as0 = _state(rec["video_state"], dtype), _state(rec["audio_state"], dtype)
+    vs, aus = vs0, as0
+    for idx, ref in enumerate(rec["steps"]):
+        dv, da, passes = ltx_dit.guided_denoise_step(model, vs, aus, ctx, sig[idx], idx, vp, ap, cfg)
+        torch.cuda.synchronize()
+        assert nat.device_error_flags() == 0
+        for name in ("cond", "uncond", "ptb", "mod"):
+            assert rel_l2(passes[name][0], ref["passes"][name][0]) < tol, (idx, name, "video")
+            assert rel_l2(passes[name][1], ref["passes"][name][1]) < tol, (idx, name, "audio")
+        # the blend weights pass differences by up to 1 + (cfg-1) + stg + (mod-1) (= 10 for
+        # the audio parameters), so the blended x0 gets that factor on top of the per-pass
+        # tolerance in BF16; the guidance arithmetic itself is checked exactly below
+        blend_tol = tol if rec["dtype"] == "float32" else 3 * tol
+        assert rel_l2(dv, ref["denoised_video"]) < blend_tol
+        assert rel_l2(da, ref["denoised_audio"]) < blend_tol
+        for got, par, k in ((dv, vp, 0), (da, ap, 1)):
+            mine = ltx_oracle.guide(*[passes[p][k].cpu() for p in ("cond", "uncond", "ptb", "mod")],
+                                    par.cfg_scale, par.stg_scale, par.rescale_scale, par.modality_scale)
+            assert rel_l2(got, mine) < (1e-6 if rec["dtype"] == "float32" else 4e-3)
+        vs = dataclasses.replace(vs, latent=ltx_dit.euler_step(vs.latent, dv, sig, idx))
+        aus = dataclasses.replace(aus, latent=ltx_dit.euler_step(aus.latent, da, sig, idx))
+        assert rel_l2(vs.latent, ref["video_latent"]) < tol
+        assert rel_l2(aus.latent, ref["audio_latent"]) < tol
+    lv, la = ltx_dit.run_dit(model, cfg, ctx, vs0, as0, sig, vp, ap)
+    assert torch.equal(lv, vs.latent) and torch.equal(la, aus.latent)
 
 
 def _config1(num_layers=8):

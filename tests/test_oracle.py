@@ -93,3 +93,25 @@ def test_oracle_guide_matches_reference():
     for case in rec["cases"].values():
         for (cfg, stg, rs, mod), out in zip(rec["params"], case["outputs"]):
             assert torch.equal(ltx_oracle.guide(*case["inputs"], cfg, stg, rs, mod), out)
+
+
+@pytest.mark.parametrize("case", gc.GUIDED_CASES)
+def test_oracle_guided_steps_match_reference(case):
+    """Two steps of the full guidance batch (cond / uncond / STG / modality, rescale) on the
+    tiny AV model against the reference's guided_denoise_step + euler_step."""
+    rec = gc.load_guided(case)
+    cfg = gc.cfg_of(rec)
+    w = gc.weights_of(rec)
+    vs, aus = dict(rec["video_state"]), dict(rec["audio_state"])
+    for idx, ref in enumerate(rec["steps"]):
+        dv, da, passes = ltx_oracle.guided_denoise_step(w, cfg, vs, aus, rec["contexts"], rec["sigmas"][idx],
+                                                        rec["v_params"], rec["a_params"])
+        for name in ("cond", "uncond", "ptb", "mod"):
+            assert torch.equal(passes[name][0], ref["passes"][name][0]), name
+            assert torch.equal(passes[name][1], ref["passes"][name][1]), name
+        assert torch.equal(dv, ref["denoised_video"])
+        assert torch.equal(da, ref["denoised_audio"])
+        vs["latent"] = ltx_oracle.euler_step(vs["latent"], dv, rec["sigmas"], idx)
+        aus["latent"] = ltx_oracle.euler_step(aus["latent"], da, rec["sigmas"], idx)
+        assert torch.equal(vs["latent"], ref["video_latent"])
+        assert torch.equal(aus["latent"], ref["audio_latent"])
