@@ -19,6 +19,8 @@ Fixtures written:
                       steps (X0 + guide + Euler).
   sched.pt            ltx2_scheduler_sigmas(30), video/audio positions.
   guide.pt            guide() with and without the std rescale on seeded x0 predictions.
+  ckpt_keys.json      dev-checkpoint key -> parameter name as the reference's
+                      load_transformer maps it (tiny AV model), with parameter shapes.
   guided_tiny_av_<dtype>.pt  two steps of guided_denoise_step (cond / uncond / STG /
                       modality passes, rescale) + Euler on the tiny AV model.
 
@@ -255,10 +257,54 @@ def make_guided(ld, dtype):
     return rec
 
 
+def make_ckpt_keys(ld):
+    """The reference's load_transformer (ltx_dit.py:414-432) on a tiny checkpoint written
+    in the dev-checkpoint key format: records, per checkpoint key, the parameter name the
+    reference loads it into (None = dropped) and the parameter shapes."""
+    import json
+    import tempfile
+
+    import common as ref_common
+    from safetensors.torch import save_file
+
+    cfg = ld.DiTConfig(**CASES["tiny_av"])
+    _, shapes = build_reference_model(ld, cfg, torch.float32)
+
+    def to_ckpt(n):
+        k = n.replace("blocks.", "transformer_blocks.", 1) if n.startswith("blocks.") else n
+        k = k.replace("to_out.", "to_out.0.")
+        k = k.replace("audio_ff.proj_in.", "audio_ff.net.0.proj.").replace("audio_ff.proj_out.", "audio_ff.net.2.")
+        k = k.replace(".ff.proj_in.", ".ff.net.0.proj.").replace(".ff.proj_out.", ".ff.net.2.")
+        return "model.diffusion_model." + k
+
+    keys = [to_ckpt(n) for n, _ in shapes] + ["vae.decoder.conv_in.weight", "text_embedding_projection.weight"]
+    tensors = {k: torch.zeros(2, 2) for k in keys}
+    for (n, shp), k in zip(shapes, keys):
+        tensors[k] = torch.zeros(shp)
+    captured = {}
+
+    def cpu_load(path, rename=None, **kw):
+        captured["rename"] = rename
+        return ref_common.load_state_dict(path, device="cpu", dtype=torch.float32, rename=rename)
+
+    saved = ld.load_state_dict, ld.DEVICE
+    ld.load_state_dict, ld.DEVICE = cpu_load, "cpu"
+    try:
+        with tempfile.TemporaryDirectory() as d:
+            path = f"{d}/tiny.safetensors"
+            save_file(tensors, path)
+            ld.load_transformer(path, cfg)  # raises on any missing parameter
+    finally:
+        ld.load_state_dict, ld.DEVICE = saved
+    rec = {"config": "tiny_av", "shapes": [[n, list(shp)] for n, shp in shapes],
+           "keys": {k: captured["rename"](k) for k in keys}}
+    (OUT / "ckpt_keys.json").write_text(json.dumps(rec, indent=0))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["guide", "guided"], default=None, help="regenerate one fixture only")
+    ap.add_argument("--only", choices=["guide", "guided", "ckpt"], default=None, help="regenerate one fixture only")
     args = ap.parse_args()
     ref_root = Path(args.reference)
     ld = _import_reference(ref_root)
@@ -269,6 +315,8 @@ def main():
         for dtype in (torch.float32, torch.bfloat16):
             rec = make_guided(ld, dtype)
             torch.save(rec, OUT / f"guided_tiny_av_{rec['dtype']}.pt")
+    if args.only in (None, "ckpt"):
+        make_ckpt_keys(ld)
     if args.only is not None:
         return
     make_philox(ref_root)

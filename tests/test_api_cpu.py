@@ -94,3 +94,29 @@ def test_perturbation_config_and_mask_checks():
         model._keep_masks(keep * 0.5, 4)
     with pytest.raises(ValueError):
         model._keep_masks(keep, 2)
+
+
+def test_load_transformer_maps_checkpoint_keys_like_the_reference(tmp_path):
+    """A dev-format checkpoint of the tiny AV model (keys recorded from the reference's
+    load_transformer, tests/golden/ckpt_keys.json) loads into the same parameters."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from oracle import ltx_oracle
+
+    rec = json.loads((gc.GOLDEN / "ckpt_keys.json").read_text())
+    shapes = [(n, tuple(s)) for n, s in rec["shapes"]]
+    sd = ltx_oracle.synthetic_state_dict(shapes, 7, dtype=torch.float32)
+    tensors = {}
+    for key, name in rec["keys"].items():
+        tensors[key] = sd[name].contiguous() if name is not None else torch.ones(3)
+    path = tmp_path / "tiny.safetensors"
+    save_file(tensors, str(path))
+    case = gc.load("tiny_av_float32")
+    cfg = ltx_dit.DiTConfig(**{k: (tuple(v) if isinstance(v, list) else v) for k, v in case["config"].items()})
+    model = ltx_dit.load_transformer(str(path), cfg, device=torch.device("cpu"), dtype=torch.float32)
+    got = dict(model.named_parameters())
+    assert set(got) == set(sd)
+    for name, t in sd.items():
+        assert torch.equal(got[name], t), name
