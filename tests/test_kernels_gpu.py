@@ -378,6 +378,29 @@ def test_attention_bf16_tcgen05(b, tq, tk, h, d):
     assert rel_l2(o, _attn_ref(q, k, v, b, tq, tk, h, d)) < 1e-2
 
 
+def test_attention_bf16_config5_sequence():
+    """BASELINE config 5 length (T = 33x22x38 = 27588, not a multiple of the 128-key tile)
+    for two heads, against a float32 reference computed in query chunks."""
+    torch.manual_seed(15)
+    t, h, d = 27588, 2, 64
+    qkv = torch.randn(t, 3 * h * d + 8, device=DEV, dtype=torch.bfloat16)
+    q, k, v = qkv[:, :h * d], qkv[:, h * d:2 * h * d], qkv[:, 2 * h * d:3 * h * d]
+    gate = qkv[:, 3 * h * d:3 * h * d + h]
+    o = torch.empty(t, h * d, device=DEV, dtype=torch.bfloat16)
+    nat.attention(q, k, v, o, 1, t, t, h, d, d ** -0.5, gate)
+    torch.cuda.synchronize()
+    assert nat.device_error_flags() == 0
+    ref = torch.empty(t, h * d, device=DEV)
+    kh = k.float().view(t, h, d).transpose(0, 1)
+    vh = v.float().view(t, h, d).transpose(0, 1)
+    for r0 in range(0, t, 4096):
+        qh = q[r0:r0 + 4096].float().view(-1, h, d).transpose(0, 1)
+        p = torch.softmax(qh @ kh.transpose(1, 2) * d ** -0.5, dim=-1)
+        out = (p @ vh).transpose(0, 1) * (2 * torch.sigmoid(gate[r0:r0 + 4096].float()))[..., None]
+        ref[r0:r0 + 4096] = out.reshape(-1, h * d)
+    assert rel_l2(o, ref) < 1e-2
+
+
 @pytest.mark.parametrize("b,tq,tk,h,d", [(2, 480, 480, 32, 64), (2, 100, 8, 4, 16 * 2), (1, 70, 90, 2, 128)])
 def test_attention_fp32(b, tq, tk, h, d):
     torch.manual_seed(10)

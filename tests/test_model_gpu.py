@@ -184,6 +184,33 @@ def test_bf16_two_blocks_at_benchmark_width_matches_oracle(t_shape):
     assert rel_l2(nxt, rnxt) < 1e-2, rel_l2(nxt, rnxt)
 
 
+def test_bf16_config4_width_av_two_blocks_matches_oracle():
+    """BASELINE config 4 geometry with 2 of its 48 blocks: video D=4096 (32x128 heads, FFN
+    16384, head_dim 128 attention), audio D=2048 (32x64), A<->V attention every block,
+    text contexts 3840 (video) and 2048 (audio) wide, cross-adaLN off, BF16, CFG batch 2.
+    Token counts are cut (192 video, 25 audio, 64 text) so the CPU oracle stays fast."""
+    cfg = ltx_dit.DiTConfig(num_layers=2, video_cross_dim=3840, cross_attention_adaln=False)
+    model, sd = _synthetic(cfg, torch.bfloat16, seed=4)
+    wb = {k: v.to(torch.bfloat16) for k, v in sd.items()}
+    g = torch.Generator().manual_seed(9)
+    f, h, w = 2, 8, 12
+    tv, ta, s = f * h * w, 25, 64
+    sig = torch.full((2,), 0.5)
+    vid = dict(latent=torch.randn(2, tv, 128, generator=g).to(torch.bfloat16), sigma=sig,
+               timesteps=torch.full((2, tv, 1), 0.5), positions=ltx_oracle.video_positions(2, f, h, w, 24.0),
+               context=torch.randn(2, s, 3840, generator=g).to(torch.bfloat16))
+    aud = dict(latent=torch.randn(2, ta, 128, generator=g).to(torch.bfloat16), sigma=sig,
+               timesteps=torch.full((2, ta, 1), 0.5), positions=ltx_oracle.audio_positions(2, ta),
+               context=torch.randn(2, s, 2048, generator=g).to(torch.bfloat16))
+    vx, ax = model(ltx_dit.Modality(**{k: v.to(DEV) for k, v in vid.items()}),
+                   ltx_dit.Modality(**{k: v.to(DEV) for k, v in aud.items()}), None)
+    torch.cuda.synchronize()
+    assert nat.device_error_flags() == 0
+    rvx, rax = ltx_oracle.forward(wb, cfg, ltx_oracle.Modality(**vid), ltx_oracle.Modality(**aud))
+    assert rel_l2(vx, rvx) < 1e-2, rel_l2(vx, rvx)
+    assert rel_l2(ax, rax) < 1e-2, rel_l2(ax, rax)
+
+
 def test_create_noised_states_bit_exact_vs_torch():
     vs, as_ = ltx_dit.create_noised_states(1, 65, 512, 768, 24.0, 10, DEV, torch.bfloat16)
     g = torch.Generator(device=DEV).manual_seed(10)
