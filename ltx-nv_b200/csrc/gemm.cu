@@ -146,25 +146,37 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait(&tempty[acc], (u & 1) ^ 1, abort_flag)) goto done;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
-          const int s = it % Cfg::STAGES;
-          if (!mbar_wait(&full[s], uint32_t(it / Cfg::STAGES) & 1, abort_flag)) goto done;
+        for (int kb = 0; kb < k_blocks; kb += 2) {
+          // two k-blocks per round: both waits first, then 8 MMAs, each stage released
+          // right after its own MMAs
+          const int nb = (kb + 1 < k_blocks) ? 2 : 1;
+          const int s0 = it % Cfg::STAGES;
+          const int s1 = (it + 1) % Cfg::STAGES;
+          if (!mbar_wait(&full[s0], uint32_t(it / Cfg::STAGES) & 1, abort_flag)) goto done;
+          if (nb == 2 && !mbar_wait(&full[s1], uint32_t((it + 1) / Cfg::STAGES) & 1, abort_flag)) goto done;
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + s * Cfg::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
-            if constexpr (PAIR)
-              umma_ss_pair(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            else
-              umma_ss(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          for (int j = 0; j < 2; ++j) {
+            if (j < nb) {
+              const int s = j ? s1 : s0;
+              const uint32_t a_addr = smem_u32(smem + s * Cfg::STAGE_BYTES);
+              const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+              for (int k = 0; k < kBK / 16; ++k) {
+                const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+                const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
+                if constexpr (PAIR)
+                  umma_ss_pair(d_tmem, ad, bd, idesc, (kb + j > 0 || k > 0) ? 1u : 0u);
+                else
+                  umma_ss(d_tmem, ad, bd, idesc, (kb + j > 0 || k > 0) ? 1u : 0u);
+              }
+              if constexpr (PAIR)
+                umma_commit_pair(&empty[s], 3);
+              else
+                umma_commit(&empty[s]);
+            }
           }
-          if constexpr (PAIR)
-            umma_commit_pair(&empty[s], 3);
-          else
-            umma_commit(&empty[s]);
+          it += nb;
         }
         if constexpr (PAIR)
           umma_commit_pair(&tfull[acc], 3);
