@@ -413,6 +413,8 @@ PROBES = {
     "attn_out": "attention out-projection tcgen05 GEMM + gate*out+residual epilogue, M=12288, N=2048, K=2048",
     "norm": "RMSNorm + adaLN modulate, [2*6144, 2048] bf16",
     "qknorm": "q RMSNorm (with weight) + split RoPE in place on the packed QKV buffer, [2*6144, 2048] bf16",
+    "connector": "text connector (Embeddings1DConnector): 8 blocks, 32x128 heads, 128 registers, B=2 prompts x "
+                 "1024 tokens, bf16",
 }
 
 
@@ -460,6 +462,23 @@ def run_probe(args, dev: torch.device) -> dict:
         mm = nat.modulation(table, mod, shift=(0, 0), scale=(d, d), mod_ld_batch=6 * d)
         fn = lambda: nat.norm_modulate(x, y, t, nat.LTX_NORM_RMS, 1e-6, mm)  # noqa: E731
         flops, nbytes = None, 2 * (x.numel() + y.numel())
+    elif args.probe == "connector":
+        import ltx_te
+
+        conn = ltx_te.Embeddings1DConnector(heads=32, dim_head=128, num_layers=8, max_pos=[4096], registers=128,
+                                            gated=False, ff_bias=True)
+        for prm in conn.parameters():
+            prm.data = rnd(*prm.shape, scale=0.02)
+        conn = conn.to(dev).eval()
+        s_len, dd = 1024, 4096
+        hid = rnd(2, s_len, dd)
+        amask = torch.zeros(2, 1, 1, s_len, device=dev, dtype=torch.bfloat16)
+        amask[:, :, :, 300:] = -10000.0  # padded prompt tail -> registers
+        fn = lambda: conn(hid, amask)  # noqa: E731
+        m_rows = 2 * s_len
+        flops = 8 * (2.0 * m_rows * dd * 3 * dd + 4.0 * 2 * s_len * s_len * dd + 2.0 * m_rows * dd * dd
+                     + 2.0 * m_rows * dd * 4 * dd * 2)
+        nbytes = 8 * 2 * (4 * dd * dd + 8 * dd * dd)  # weights streamed once per call
     elif args.probe == "qknorm":
         qkv = rnd(m, 3 * d + c["heads"])
         wq = (1 + rnd(d, scale=0.02).float()).to(torch.bfloat16)

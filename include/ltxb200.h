@@ -221,6 +221,12 @@ int ltx_guide_rescale(const void* cond, const void* uncond, const void* ptb, con
 int ltx_guide_rescale_noalloc(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
                               float cfg_scale, float stg_scale, float modality_scale, float rescale_scale, void* out,
                               int dtype, void* stream);
+/* Text-connector register fill (ltx_te.py:218-223): out row r = x row r where the
+ * additive mask of token r is >= 0, else registers row ((r % rows_per_batch) %
+ * num_registers). x / out (rows, D) row-major, mask (rows) and registers
+ * (num_registers, D) in the same dtype. */
+int ltx_register_fill(const void* x, int64_t ldx, const void* additive_mask, const void* registers, int num_registers,
+                      int64_t rows, int64_t rows_per_batch, int D, void* out, int64_t ldo, int dtype, void* stream);
 /* X0 of a velocity prediction (ltx_dit.py:591-593, X0Model): out = round(latent - v *
  * timesteps[row]) with fp32 math; latent, velocity and out are (rows, C), timesteps fp32 (rows). */
 int ltx_x0(const void* latent, const void* velocity, const float* timesteps, int64_t rows, int C, void* out,

@@ -104,6 +104,8 @@ _SIGNATURES = {
     "ltx_value_gate": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int, c_vp]),
     "ltx_x0": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, c_vp, ctypes.c_int, c_vp]),
+    "ltx_register_fill": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, ctypes.c_int, c_i64, c_i64, ctypes.c_int, c_vp,
+                                         c_i64, ctypes.c_int, c_vp]),
     "ltx_guide_rescale_workspace_bytes": (ctypes.c_size_t, [c_i64]),
     "ltx_guide_rescale_noalloc": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float,
                                                  ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
@@ -402,6 +404,15 @@ def x0(latent: torch.Tensor, velocity: torch.Tensor, timesteps: torch.Tensor, ou
     if timesteps.dtype != torch.float32 or not timesteps.is_contiguous() or timesteps.numel() != rows:
         raise ValueError("timesteps must be a contiguous float32 tensor with one entry per row")
     _call("ltx_x0", _ptr(latent), _ptr(velocity), _ptr(timesteps), rows, c, _ptr(out), _dt(latent), _stream(latent))
+
+
+def register_fill(x: torch.Tensor, additive_mask: torch.Tensor, registers: torch.Tensor, rows_per_batch: int,
+                  out: torch.Tensor) -> None:
+    """out = x where the per-row additive mask is >= 0, else registers[(row % S) % R]."""
+    if not additive_mask.is_contiguous() or additive_mask.numel() != x.shape[0]:
+        raise ValueError("additive_mask must be contiguous with one entry per row")
+    _call("ltx_register_fill", _ptr(x), _ld(x), _ptr(additive_mask), _ptr(registers.contiguous()),
+          registers.shape[0], x.shape[0], rows_per_batch, x.shape[1], _ptr(out), _ld(out), _dt(x), _stream(x))
 
 
 def guide_rescale_workspace(n: int, device: torch.device) -> torch.Tensor:

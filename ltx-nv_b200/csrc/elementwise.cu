@@ -610,6 +610,25 @@ void launch_guide_rescale(const void* cond, const void* uncond, const void* ptb,
       ltx::note_launch();
 }
 
+// Learnable-register fill of the text connector (ltx_te.py:218-223): a token whose
+// additive mask is negative (padding) is replaced by register row (token % R); the
+// reference's blend binary*h + (1-binary)*regs with binary in {0, 1} is this selection.
+template <typename T>
+__global__ void register_fill_kernel(const T* __restrict__ x, int64_t ldx, const T* __restrict__ mask,
+                                     const T* __restrict__ regs, int R, int64_t rows, int64_t S, int D,
+                                     T* __restrict__ out, int64_t ldo) {
+  const int per_row = D / 8;
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * per_row) return;
+  const int64_t r = i / per_row;
+  const int c = int(i - r * per_row) * 8;
+  const bool keep = ld_elem<T>(mask + r) >= 0.f;
+  const T* src = keep ? x + r * ldx + c : regs + int64_t((r % S) % R) * D + c;
+  float v[8];
+  ld8<T>(src, v);
+  st8<T>(out + r * ldo + c, v);
+}
+
 // X0 from a velocity (ltx_dit.py:591-593): out = round(latent - v * timesteps[row]).
 template <typename T>
 __global__ void x0_kernel(const T* __restrict__ latent, const T* __restrict__ vel, const float* __restrict__ ts,
@@ -1011,6 +1030,36 @@ extern "C" int ltx_guide_rescale_noalloc(const void* cond, const void* uncond, c
   else
     launch_guide_rescale<__nv_bfloat16>(cond, uncond, ptb, mod, n, cfg_scale - 1.f, stg_scale,
                                         modality_scale - 1.f, rescale_scale, out, ws, s);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_register_fill(const void* x, int64_t ldx, const void* additive_mask, const void* registers,
+                                 int num_registers, int64_t rows, int64_t rows_per_batch, int D, void* out,
+                                 int64_t ldo, int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_CHECK_DTYPE(dtype);
+  LTX_REQUIRE(x && additive_mask && registers && out, "NULL argument");
+  LTX_REQUIRE(rows > 0 && rows_per_batch > 0 && num_registers > 0 && D > 0 && D % 8 == 0,
+              "bad shape (D must be a positive multiple of 8)");
+  LTX_REQUIRE(ldx % 8 == 0 && ldo % 8 == 0 && ldx >= D && ldo >= D, "ldx / ldo must be multiples of 8 and >= D");
+  check_vec_ptr(x, "x");
+  check_vec_ptr(registers, "registers");
+  check_vec_ptr(out, "out");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = unsigned((rows * (D / 8) + 255) / 256);
+  if (dtype == LTX_F32)
+    register_fill_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), ldx,
+                                                       static_cast<const float*>(additive_mask),
+                                                       static_cast<const float*>(registers), num_registers, rows,
+                                                       rows_per_batch, D, static_cast<float*>(out), ldo),
+        ltx::note_launch();
+  else
+    register_fill_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(additive_mask),
+        static_cast<const __nv_bfloat16*>(registers), num_registers, rows, rows_per_batch, D,
+        static_cast<__nv_bfloat16*>(out), ldo),
+        ltx::note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

@@ -40,9 +40,9 @@ def rms_norm(x, eps=1e-6, weight=None):
     return F.rms_norm(x, (x.shape[-1],), weight=weight, eps=eps)
 
 
-def sdpa(q, k, v):
-    """ltx_nn.py:22-26 (no mask in these configurations). (B, H, T, d)."""
-    return F.scaled_dot_product_attention(q, k, v, dropout_p=0.0, is_causal=False)
+def sdpa(q, k, v, mask=None):
+    """ltx_nn.py:22-26. (B, H, T, d); mask an additive (B, 1, 1, T) mask or None."""
+    return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, dropout_p=0.0, is_causal=False)
 
 
 @functools.lru_cache(maxsize=16)
@@ -111,7 +111,7 @@ def adaln_single(w, name, t, dtype):
 
 
 def attention(w, name, x, heads, dim_head, eps, context=None, pe=None, k_pe=None, gated=True,
-              perturbation_mask=None, all_perturbed=False):
+              perturbation_mask=None, all_perturbed=False, mask=None):
     """ltx_nn.py:194-236. STG: all_perturbed -> out = V (:209-210); a per-sample
     perturbation_mask (B, 1, 1) blends out * mask + V * (1 - mask) (:229-230)."""
     context = x if context is None else context
@@ -128,7 +128,7 @@ def attention(w, name, x, heads, dim_head, eps, context=None, pe=None, k_pe=None
         q = q.view(b, -1, heads, dim_head).transpose(1, 2)
         k = k.view(b, -1, heads, dim_head).transpose(1, 2)
         v4 = v.view(b, -1, heads, dim_head).transpose(1, 2)
-        out = sdpa(q, k, v4).transpose(1, 2).reshape(b, -1, heads * dim_head)
+        out = sdpa(q, k, v4, mask).transpose(1, 2).reshape(b, -1, heads * dim_head)
         if perturbation_mask is not None:
             out = out * perturbation_mask + v * (1 - perturbation_mask)
     if gated and (name + ".to_gate_logits.weight") in w:
@@ -471,6 +471,35 @@ def guided_denoise_step(w, cfg, video_state, audio_state, contexts, sigma, v_par
     gv = guide(*[r[p][0] for p in passes], *v_params[:4])
     ga = guide(*[r[p][1] for p in passes], *a_params[:4])
     return gv, ga, r
+
+
+# ----------------------------------------------------------------------------------------
+# text connector (ltx_te.py:187-229)
+# ----------------------------------------------------------------------------------------
+
+
+@torch.inference_mode()
+def connector_forward(w, prefix, heads, dim_head, num_layers, max_pos, registers, gated, hidden, additive_mask):
+    """Embeddings1DConnector.forward (ltx_te.py:212-229): learnable-register fill of
+    padded tokens, 1D RoPE over token indices (no mid-point grid), `num_layers` blocks of
+    x + attn1(rms(x)) and x + ff(rms(x)), final RMS norm. Returns (out, mask)."""
+    b, s, _ = hidden.shape
+    inner = heads * dim_head
+    if registers:
+        regs = w[prefix + "learnable_registers"].repeat(s // registers, 1).to(hidden.dtype)
+        regs = regs.unsqueeze(0).expand(b, -1, -1)
+        binary = (additive_mask[:, 0, 0, :] >= 0).to(hidden.dtype).unsqueeze(-1)
+        hidden = binary * hidden + (1 - binary) * regs
+        additive_mask = torch.zeros_like(additive_mask)
+    grid = torch.arange(s, dtype=torch.float32)[None, None, :].expand(b, -1, -1)
+    pe = rope_tables(torch.stack([grid, grid], dim=-1), inner, hidden.dtype, 10000.0, list(max_pos), heads, True)
+    x = hidden
+    for i in range(num_layers):
+        p = f"{prefix}blocks.{i}."
+        x = x + attention(w, p + "attn1", rms_norm(x), heads, dim_head, 1e-6, pe=pe, gated=gated,
+                          mask=additive_mask)
+        x = x + feed_forward(w, p + "ff", rms_norm(x))
+    return rms_norm(x), additive_mask
 
 
 # ----------------------------------------------------------------------------------------

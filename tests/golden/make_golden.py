@@ -19,6 +19,7 @@ Fixtures written:
                       steps (X0 + guide + Euler).
   sched.pt            ltx2_scheduler_sigmas(30), video/audio positions.
   guide.pt            guide() with and without the std rescale on seeded x0 predictions.
+  connector_<dtype>.pt  the text connector (Embeddings1DConnector) on seeded inputs.
   ckpt_keys.json      dev-checkpoint key -> parameter name as the reference's
                       load_transformer maps it (tiny AV model), with parameter shapes.
   guided_tiny_av_<dtype>.pt  two steps of guided_denoise_step (cond / uncond / STG /
@@ -301,10 +302,35 @@ def make_ckpt_keys(ld):
     (OUT / "ckpt_keys.json").write_text(json.dumps(rec, indent=0))
 
 
+CONNECTOR = dict(heads=4, dim_head=64, num_layers=2, max_pos=[4096], registers=8, gated=True, ff_bias=True)
+
+
+@torch.inference_mode()
+def make_connector(ref_root: Path, dtype):
+    """The reference's Embeddings1DConnector (ltx_te.py:187-229) on seeded inputs: sample 0
+    has its last 12 of 32 tokens padded (negative additive mask), sample 1 none."""
+    sys.path.insert(0, str(ref_root / "standalone"))
+    import ltx_te
+
+    conn = ltx_te.Embeddings1DConnector(**CONNECTOR)
+    shapes = [(n, tuple(p.shape)) for n, p in conn.named_parameters()]
+    conn.load_state_dict(ltx_oracle.synthetic_state_dict(shapes, WEIGHT_SEED + 5, dtype=torch.float32))
+    conn = conn.to(dtype).eval()
+    inner = CONNECTOR["heads"] * CONNECTOR["dim_head"]
+    hidden = rng_normal((2, 32, inner), 400).to(dtype)
+    mask = torch.zeros(2, 1, 1, 32, dtype=dtype)
+    mask[0, :, :, 20:] = -10000.0
+    out, out_mask = conn(hidden, mask)
+    return {"config": CONNECTOR, "param_shapes": shapes, "weight_seed": WEIGHT_SEED + 5,
+            "dtype": str(dtype).replace("torch.", ""), "hidden": hidden, "mask": mask, "out": out,
+            "out_mask": out_mask}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["guide", "guided", "ckpt"], default=None, help="regenerate one fixture only")
+    ap.add_argument("--only", choices=["guide", "guided", "ckpt", "connector"], default=None,
+                    help="regenerate one fixture only")
     args = ap.parse_args()
     ref_root = Path(args.reference)
     ld = _import_reference(ref_root)
@@ -317,6 +343,10 @@ def main():
             torch.save(rec, OUT / f"guided_tiny_av_{rec['dtype']}.pt")
     if args.only in (None, "ckpt"):
         make_ckpt_keys(ld)
+    if args.only in (None, "connector"):
+        for dtype in (torch.float32, torch.bfloat16):
+            rec = make_connector(ref_root, dtype)
+            torch.save(rec, OUT / f"connector_{rec['dtype']}.pt")
     if args.only is not None:
         return
     make_philox(ref_root)

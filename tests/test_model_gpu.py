@@ -211,6 +211,24 @@ def test_bf16_config4_width_av_two_blocks_matches_oracle():
     assert rel_l2(ax, rax) < 1e-2, rel_l2(ax, rax)
 
 
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_text_connector_matches_reference_golden(dtype):
+    """The text connector on the native kernels against the reference's
+    Embeddings1DConnector outputs (padded tokens replaced by learnable registers)."""
+    import ltx_te
+
+    rec = torch.load(gc.GOLDEN / f"connector_{dtype}.pt", weights_only=False)
+    dt = getattr(torch, dtype)
+    conn = ltx_te.Embeddings1DConnector(**rec["config"])
+    conn.load_state_dict(ltx_oracle.synthetic_state_dict(rec["param_shapes"], rec["weight_seed"], dtype=torch.float32))
+    conn = conn.to(DEV, dt).eval()
+    out, mask = conn(rec["hidden"].to(DEV), rec["mask"].to(DEV))
+    torch.cuda.synchronize()
+    assert nat.device_error_flags() == 0
+    assert rel_l2(out, rec["out"]) < TOL[dtype], rel_l2(out, rec["out"])
+    assert torch.equal(mask.cpu(), rec["out_mask"])
+
+
 def test_create_noised_states_bit_exact_vs_torch():
     vs, as_ = ltx_dit.create_noised_states(1, 65, 512, 768, 24.0, 10, DEV, torch.bfloat16)
     g = torch.Generator(device=DEV).manual_seed(10)

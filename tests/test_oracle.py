@@ -115,3 +115,15 @@ def test_oracle_guided_steps_match_reference(case):
         aus["latent"] = ltx_oracle.euler_step(aus["latent"], da, rec["sigmas"], idx)
         assert torch.equal(vs["latent"], ref["video_latent"])
         assert torch.equal(aus["latent"], ref["audio_latent"])
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_oracle_text_connector_matches_reference(dtype):
+    """Embeddings1DConnector (ltx_te.py:187-229): register fill, 1D RoPE, blocks, final norm."""
+    rec = torch.load(gc.GOLDEN / f"connector_{dtype}.pt", weights_only=False)
+    c = rec["config"]
+    w = ltx_oracle.synthetic_state_dict(rec["param_shapes"], rec["weight_seed"], dtype=getattr(torch, dtype))
+    out, mask = ltx_oracle.connector_forward(w, "", c["heads"], c["dim_head"], c["num_layers"], c["max_pos"],
+                                             c["registers"], c["gated"], rec["hidden"], rec["mask"])
+    assert torch.equal(out, rec["out"])
+    assert torch.equal(mask, rec["out_mask"])
