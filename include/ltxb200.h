@@ -108,6 +108,13 @@ int ltx_qk_norm_rope(void* x, int64_t ldx, int64_t rows, int64_t rows_per_batch,
                      const void* weight, float eps, const void* cos_tab, const void* sin_tab, int64_t ld_rope,
                      int64_t rope_ld_batch, int dtype, void* stream);
 
+/* Self-attention q and k in one pass (ltx_nn.py:186-187, 214-218): the q block at column 0
+ * and the k block at column k_offset of the same rows are each RMS-normalised over the
+ * inner dim with their own weight and rotated with the same RoPE tables (read once per
+ * row). Same arithmetic as two ltx_qk_norm_rope calls. */
+int ltx_qk_norm_rope_pair(void* x, int64_t ldx, int64_t k_offset, int64_t rows, int64_t rows_per_batch, int heads,
+                          int head_dim, const void* q_weight, const void* k_weight, float eps, const void* cos_tab,
+                          const void* sin_tab, int64_t ld_rope, int64_t rope_ld_batch, int dtype, void* stream);
 /* RoPE tables from token positions (precompute_freqs_cis, ltx_nn.py:63-96): `bounds`
  * (n_axes, T, 2) fp32 [start, end) positions of one sample (the reference's
  * positions[b]), `freqs` (F) fp32 frequency grid (computed in float64 by the caller,

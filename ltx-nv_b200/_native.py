@@ -81,6 +81,8 @@ _SIGNATURES = {
                                          ctypes.c_float, ctypes.POINTER(Modulation), ctypes.c_int, c_vp]),
     "ltx_qk_norm_rope": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i64, ctypes.c_int, ctypes.c_int, c_vp, ctypes.c_float,
                                         c_vp, c_vp, c_i64, c_i64, ctypes.c_int, c_vp]),
+    "ltx_qk_norm_rope_pair": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, ctypes.c_int, ctypes.c_int, c_vp, c_vp,
+                                             ctypes.c_float, c_vp, c_vp, c_i64, c_i64, ctypes.c_int, c_vp]),
     "ltx_rope_tables": (ctypes.c_int, [c_vp, ctypes.c_int, c_i64, c_vp, ctypes.c_int, c_vp, ctypes.c_int, c_vp, c_vp,
                                        ctypes.c_int, c_vp]),
     "ltx_gelu_tanh": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_int, c_vp]),
@@ -292,6 +294,16 @@ def qk_norm_rope(x: torch.Tensor, rows_per_batch: int, heads: int, head_dim: int
     ld_rope = _ld(cos) if cos is not None else 0
     _call("ltx_qk_norm_rope", _ptr(x), _ld(x), rows, rows_per_batch, heads, head_dim, _ptr(weight), eps, _ptr(cos),
           _ptr(sin), ld_rope, rope_ld_batch, _dt(x), _stream(x))
+
+
+def qk_norm_rope_pair(x: torch.Tensor, k_offset: int, rows_per_batch: int, heads: int, head_dim: int,
+                      q_weight: torch.Tensor, k_weight: torch.Tensor, eps: float, cos: torch.Tensor | None,
+                      sin: torch.Tensor | None, rope_ld_batch: int = 0) -> None:
+    """q (columns [0, H*d)) and k (columns [k_offset, k_offset + H*d)) of x normalised and
+    rotated in one launch; x is a row-major view whose row stride covers both blocks."""
+    ld_rope = _ld(cos) if cos is not None else 0
+    _call("ltx_qk_norm_rope_pair", _ptr(x), _ld(x), k_offset, x.shape[0], rows_per_batch, heads, head_dim,
+          _ptr(q_weight), _ptr(k_weight), eps, _ptr(cos), _ptr(sin), ld_rope, rope_ld_batch, _dt(x), _stream(x))
 
 
 def rope_tables(bounds: torch.Tensor, freqs: torch.Tensor, max_pos: torch.Tensor, dim: int, cos_out: torch.Tensor,

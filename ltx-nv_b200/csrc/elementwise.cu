@@ -260,27 +260,39 @@ __global__ void __launch_bounds__(256, 2) qk_rows_bf16_kernel(__nv_bfloat16* __r
                                                            const __nv_bfloat16* __restrict__ w, float eps,
                                                            const __nv_bfloat16* __restrict__ cos_t,
                                                            const __nv_bfloat16* __restrict__ sin_t, int64_t ld_rope,
-                                                           int64_t rope_ld_batch) {
+                                                           int64_t rope_ld_batch,
+                                                           const __nv_bfloat16* __restrict__ w2 = nullptr,
+                                                           int64_t off2 = 0) {
+  // w2 != nullptr: a second column block at off2 (self-attention k) is normalised with
+  // w2 and rotated with the same RoPE entries, which are loaded once per row.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r0 = int64_t(blockIdx.x) * rows_per_cta;
   const int64_t r1 = min(r0 + rows_per_cta, rows);
   const int per_head = d >> 4;
   const float inv_D = 1.f / float(32 * NI * 16);
+  const int n_parts = w2 != nullptr ? 2 : 1;
   for (int64_t r = r0 + warp; r < r1; r += 8) {
-    __nv_bfloat16* xr = x + r * ldx;
     const int64_t b = r / rows_per_batch, t = r - b * rows_per_batch;
     const int64_t ro = b * rope_ld_batch + t * ld_rope;
     uint4 ra[NI], rb[NI], rc[NI], rs[NI];
+    if (cos_t != nullptr) {
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const int u = i * 32 + lane;
+        const int h = u / per_head, j0 = (u - h * per_head) * 8;
+        rc[i] = *reinterpret_cast<const uint4*>(cos_t + ro + h * (d >> 1) + j0);
+        rs[i] = *reinterpret_cast<const uint4*>(sin_t + ro + h * (d >> 1) + j0);
+      }
+    }
+    for (int part = 0; part < n_parts; ++part) {
+    __nv_bfloat16* xr = x + r * ldx + (part ? off2 : 0);
+    const __nv_bfloat16* wp = part ? w2 : w;
 #pragma unroll
     for (int i = 0; i < NI; ++i) {
       const int u = i * 32 + lane;
       const int h = u / per_head, j0 = (u - h * per_head) * 8;
       ra[i] = *reinterpret_cast<const uint4*>(xr + h * d + j0);
       rb[i] = *reinterpret_cast<const uint4*>(xr + h * d + j0 + (d >> 1));
-      if (cos_t != nullptr) {
-        rc[i] = *reinterpret_cast<const uint4*>(cos_t + ro + h * (d >> 1) + j0);
-        rs[i] = *reinterpret_cast<const uint4*>(sin_t + ro + h * (d >> 1) + j0);
-      }
     }
     float s = 0.f;
 #pragma unroll
@@ -309,14 +321,14 @@ __global__ void __launch_bounds__(256, 2) qk_rows_bf16_kernel(__nv_bfloat16* __r
         unpack_bf16x2(pa[k], a[2 * k], a[2 * k + 1]);
         unpack_bf16x2(pb[k], bb[2 * k], bb[2 * k + 1]);
       }
-      if (w != nullptr) {
-        float w1[8], w2[8];
-        ld8<__nv_bfloat16>(w + c1, w1);
-        ld8<__nv_bfloat16>(w + c1 + (d >> 1), w2);
+      if (wp != nullptr) {
+        float wa[8], wb[8];
+        ld8<__nv_bfloat16>(wp + c1, wa);
+        ld8<__nv_bfloat16>(wp + c1 + (d >> 1), wb);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          a[k] = a[k] * rstd * w1[k];
-          bb[k] = bb[k] * rstd * w2[k];
+          a[k] = a[k] * rstd * wa[k];
+          bb[k] = bb[k] * rstd * wb[k];
           round_bf16_pair(a[k], bb[k]);
         }
       }
@@ -345,6 +357,7 @@ __global__ void __launch_bounds__(256, 2) qk_rows_bf16_kernel(__nv_bfloat16* __r
         st8<__nv_bfloat16>(xr + c1, a);
         st8<__nv_bfloat16>(xr + c1 + (d >> 1), bb);
       }
+    }
     }
   }
 }
@@ -779,6 +792,62 @@ extern "C" int ltx_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ld
     launch_norm_modulate<float>(x, ldx, y, ldy, rows, rows_per_batch, D, norm_kind, eps, mod, s);
   else
     launch_norm_modulate<__nv_bfloat16>(x, ldx, y, ldy, rows, rows_per_batch, D, norm_kind, eps, mod, s);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_qk_norm_rope(void* x, int64_t ldx, int64_t rows, int64_t rows_per_batch, int heads, int head_dim,
+                                const void* weight, float eps, const void* cos_tab, const void* sin_tab,
+                                int64_t ld_rope, int64_t rope_ld_batch, int dtype, void* stream);
+
+extern "C" int ltx_qk_norm_rope_pair(void* x, int64_t ldx, int64_t k_offset, int64_t rows, int64_t rows_per_batch,
+                                     int heads, int head_dim, const void* q_weight, const void* k_weight, float eps,
+                                     const void* cos_tab, const void* sin_tab, int64_t ld_rope, int64_t rope_ld_batch,
+                                     int dtype, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(x != nullptr && q_weight != nullptr && k_weight != nullptr, "x and both weights must be non-NULL");
+  LTX_REQUIRE(k_offset % 8 == 0 && k_offset >= int64_t(heads) * head_dim, "k_offset must be a multiple of 8 past q");
+  LTX_REQUIRE(ldx >= k_offset + int64_t(heads) * head_dim, "ldx too small for the k block");
+  const int nthr = heads * (head_dim / 16);
+  const bool fast = dtype == LTX_BF16 && head_dim % 16 == 0 && (nthr % 32) == 0 && nthr / 32 <= 4 && ldx % 8 == 0 &&
+                    rows > 0 && rows_per_batch > 0 && (cos_tab == nullptr) == (sin_tab == nullptr) &&
+                    (cos_tab == nullptr || (ld_rope % 8 == 0 && rope_ld_batch % 8 == 0));
+  if (!fast) {
+    // generic: the two blocks one after the other
+    char* xb = static_cast<char*>(x);
+    const size_t es = dtype == LTX_F32 ? 4 : 2;
+    int st = ltx_qk_norm_rope(x, ldx, rows, rows_per_batch, heads, head_dim, q_weight, eps, cos_tab, sin_tab, ld_rope,
+                              rope_ld_batch, dtype, stream);
+    if (st != LTX_OK) return st;
+    return ltx_qk_norm_rope(xb + k_offset * es, ldx, rows, rows_per_batch, heads, head_dim, k_weight, eps, cos_tab,
+                            sin_tab, ld_rope, rope_ld_batch, dtype, stream);
+  }
+  check_vec_ptr(x, "x");
+  check_vec_ptr(q_weight, "q_weight");
+  check_vec_ptr(k_weight, "k_weight");
+  check_vec_ptr(cos_tab, "cos");
+  check_vec_ptr(sin_tab, "sin");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int ni = nthr / 32;
+  const int64_t target = int64_t(num_sms()) * 2;
+  const int per = int(std::max<int64_t>(8, (rows + target - 1) / target));
+  const unsigned grid = unsigned((rows + per - 1) / per);
+  auto xb = static_cast<__nv_bfloat16*>(x);
+  auto wq = static_cast<const __nv_bfloat16*>(q_weight);
+  auto wk = static_cast<const __nv_bfloat16*>(k_weight);
+  auto cb = static_cast<const __nv_bfloat16*>(cos_tab);
+  auto sb = static_cast<const __nv_bfloat16*>(sin_tab);
+#define LTX_QK_PAIR(NIV)                                                                                           \
+  qk_rows_bf16_kernel<NIV><<<grid, 256, 0, s>>>(xb, ldx, rows, rows_per_batch, per, head_dim, wq, eps, cb, sb, ld_rope, \
+                                                rope_ld_batch, wk, k_offset),                                          \
+      ltx::note_launch()
+  switch (ni) {
+    case 1: LTX_QK_PAIR(1); break;
+    case 2: LTX_QK_PAIR(2); break;
+    case 3: LTX_QK_PAIR(3); break;
+    default: LTX_QK_PAIR(4); break;
+  }
+#undef LTX_QK_PAIR
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

@@ -304,8 +304,21 @@ class Attention(torch.nn.Module):
         w, b = self.packed_self()
         qkv = torch.empty(x2.shape[0], w.shape[0], device=x2.device, dtype=x2.dtype)
         nat.linear(x2, w, qkv, nat.epilogue(bias=b))
+        if k_pe is None:
+            # q and k share the tables: one pass over both blocks
+            if pe is None:
+                nat.qk_norm_rope_pair(qkv, inner, rows_per_batch, self.heads, self.dim_head, self.q_norm.weight,
+                                      self.k_norm.weight, self.norm_eps, None, None)
+            else:
+                rh = pe.heads
+                nat.qk_norm_rope_pair(qkv, inner, rows_per_batch, rh, inner // rh, self.q_norm.weight,
+                                      self.k_norm.weight, self.norm_eps,
+                                      pe.cos.view(-1, inner // 2) if pe.cos.dim() == 3 else pe.cos,
+                                      pe.sin.view(-1, inner // 2) if pe.sin.dim() == 3 else pe.sin,
+                                      rope_ld_batch=pe.ld_batch)
+            return qkv
         self._norm_rope(qkv[:, :inner], rows_per_batch, self.q_norm.weight, pe)
-        self._norm_rope(qkv[:, inner:2 * inner], rows_per_batch, self.k_norm.weight, k_pe if k_pe is not None else pe)
+        self._norm_rope(qkv[:, inner:2 * inner], rows_per_batch, self.k_norm.weight, k_pe)
         return qkv
 
     def _norm_rope(self, view: torch.Tensor, rows_per_batch: int, weight: torch.Tensor, pe: RopeTables | None):

@@ -146,6 +146,25 @@ def test_norm_modulate_per_token_and_plain():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("heads,hd", [(32, 64), (4, 16)])
+def test_qk_norm_rope_pair_equals_two_passes(dtype, heads, hd):
+    torch.manual_seed(16)
+    rows, t = 2 * 300, 300
+    d = heads * hd
+    x = torch.randn(rows, 3 * d + 8, device=DEV).to(dtype)
+    wq = (1 + 0.02 * torch.randn(d, device=DEV)).to(dtype)
+    wk = (1 + 0.02 * torch.randn(d, device=DEV)).to(dtype)
+    cos = torch.randn(t, d // 2, device=DEV).to(dtype)
+    sin = torch.randn(t, d // 2, device=DEV).to(dtype)
+    a, b = x.clone(), x.clone()
+    nat.qk_norm_rope_pair(a, d, t, heads, hd, wq, wk, 1e-6, cos, sin, 0)
+    nat.qk_norm_rope(b[:, :d], t, heads, hd, wq, 1e-6, cos, sin, 0)
+    nat.qk_norm_rope(b[:, d:2 * d], t, heads, hd, wk, 1e-6, cos, sin, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("heads,hd", [(32, 64), (32, 128), (4, 16), (2, 32)])
 def test_qk_norm_rope_vs_oracle(dtype, heads, hd):
     torch.manual_seed(2)
