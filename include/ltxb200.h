@@ -264,6 +264,43 @@ int ltx_sp_pack(const void* src, int64_t ld_src, int64_t rows, int parts, int n_
 int ltx_sp_unpack(const void* src, int64_t rows, int parts, int w, void* dst, int64_t ld_dst, int dtype,
                   void* stream);
 
+/* ---------------------------------------------------------------------------------- */
+/* Video VAE decoder (ConvVideoDecoder, ltx_vae.py:167-222). Activations are           */
+/* channels-last (B, F, H, W, C) bf16; the reference's tensors are (B, C, F, H, W).    */
+/* ---------------------------------------------------------------------------------- */
+/* CausalConv3d (ltx_vae.py:31-57) with stride 1: ksize 3 -> 3x3x3 taps, zero padding of
+ * one voxel in H and W, frames padded by repeating the edge frames (causal = 0: one
+ * copy at each end; causal = 1: two copies of the first frame in front); ksize 1 -> the
+ * 1x1x1 Conv3d shortcut (ltx_vae.py:100). weight (cout, taps, cin) bf16, i.e. the
+ * reference's (cout, cin, kt, kh, kw) permuted to tap-major K; bias (cout).
+ * out = round(conv + bias), then + residual (same layout as out, may equal out) when
+ * residual is not NULL. cin a multiple of 64, cout of 8; out must not alias x. */
+int ltx_conv3d(const void* x, int B, int F, int H, int W, int cin, const void* weight, const void* bias, int cout,
+               int ksize, int causal, const void* residual, void* out, void* stream);
+/* PixelNorm (ltx_vae.py:20-28) over the C channels of each of `rows` voxels, followed by
+ * SiLU when silu != 0 (ResnetBlock3D.nonlin, ltx_vae.py:111-115; the decoder's final
+ * norm + SiLU, :209-210). x may equal y. */
+int ltx_pixel_norm(const void* x, void* y, int64_t rows, int C, float eps, int silu, void* stream);
+/* GroupNorm(1, C, eps) with affine weight / bias (ResnetBlock3D.norm3, ltx_vae.py:99):
+ * per sample, mean and variance over its n_per_sample = F*H*W*C values. Two passes;
+ * workspace of ltx_group_norm1_workspace_bytes(B) bytes (caller-owned, no init). */
+int64_t ltx_group_norm1_workspace_bytes(int B);
+int ltx_group_norm1(const void* x, int B, int64_t n_per_sample, int C, const void* weight, const void* bias, float eps,
+                    void* workspace, int64_t ws_bytes, void* y, void* stream);
+/* DepthToSpaceUpsample's rearrange (ltx_vae.py:135-143): x (B, F, H, W, c*p1*p2*p3) ->
+ * y (B, F*p1 - drop_first, H*p2, W*p3, c); drop_first = 1 drops the first frame (the
+ * reference does so when p1 == 2). c a multiple of 8. */
+int ltx_depth_to_space(const void* x, int B, int F, int H, int W, int c, int p1, int p2, int p3, int drop_first,
+                       void* y, void* stream);
+/* PerChannelStatistics.un_normalize (ltx_vae.py:83-87) of the (B, C, F, H, W) latent into
+ * the channels-last layout: y = round(round(x * bf16(std)) + bf16(mean)); std / mean fp32. */
+int ltx_vae_latent_in(const void* latent, int B, int C, int F, int H, int W, const float* std_of_means,
+                      const float* mean_of_means, void* y, void* stream);
+/* Output unpatchify (ltx_vae.py:212-216) of x (B, F, H, W, c*p*p): mode 0 -> the
+ * reference's (B, c, F, H*p, W*p) bf16 tensor; mode 1 -> decode_video's (F, H*p, W*p, c)
+ * float frames of sample 0, (v + 1) / 2 clamped to [0, 1] (ltx_vae.py:218-222). */
+int ltx_vae_unpatchify(const void* x, int B, int F, int H, int W, int c, int p, int mode, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -108,6 +108,15 @@ _SIGNATURES = {
     "ltx_x0": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, c_vp, ctypes.c_int, c_vp]),
     "ltx_register_fill": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, ctypes.c_int, c_i64, c_i64, ctypes.c_int, c_vp,
                                          c_i64, ctypes.c_int, c_vp]),
+    "ltx_conv3d": (ctypes.c_int, [c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_vp,
+                                  c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_vp, c_vp, c_vp]),
+    "ltx_pixel_norm": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_int, c_vp]),
+    "ltx_group_norm1_workspace_bytes": (c_i64, [ctypes.c_int]),
+    "ltx_group_norm1": (ctypes.c_int, [c_vp, ctypes.c_int, c_i64, ctypes.c_int, c_vp, c_vp, ctypes.c_float, c_vp, c_i64,
+                                       c_vp, c_vp]),
+    "ltx_depth_to_space": (ctypes.c_int, [c_vp] + [ctypes.c_int] * 9 + [c_vp, c_vp]),
+    "ltx_vae_latent_in": (ctypes.c_int, [c_vp] + [ctypes.c_int] * 5 + [c_vp, c_vp, c_vp, c_vp]),
+    "ltx_vae_unpatchify": (ctypes.c_int, [c_vp] + [ctypes.c_int] * 7 + [c_vp, c_vp]),
     "ltx_guide_rescale_workspace_bytes": (ctypes.c_size_t, [c_i64]),
     "ltx_guide_rescale_noalloc": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float,
                                                  ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
@@ -425,6 +434,67 @@ def register_fill(x: torch.Tensor, additive_mask: torch.Tensor, registers: torch
         raise ValueError("additive_mask must be contiguous with one entry per row")
     _call("ltx_register_fill", _ptr(x), _ld(x), _ptr(additive_mask), _ptr(registers.contiguous()),
           registers.shape[0], x.shape[0], rows_per_batch, x.shape[1], _ptr(out), _ld(out), _dt(x), _stream(x))
+
+
+# ---------------------------------------------------------------------------------------
+# Video VAE decoder (channels-last (B, F, H, W, C) bf16 activations)
+# ---------------------------------------------------------------------------------------
+def _cl5(t: torch.Tensor) -> tuple[int, int, int, int, int]:
+    if t.dim() != 5 or not t.is_contiguous() or t.dtype != torch.bfloat16:
+        raise ValueError(f"expected a contiguous (B, F, H, W, C) bf16 tensor, got {tuple(t.shape)} {t.dtype}")
+    return tuple(t.shape)
+
+
+def conv3d(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, out: torch.Tensor, ksize: int,
+           causal: bool = False, residual: torch.Tensor | None = None) -> None:
+    """out (B, F, H, W, cout) = conv(x) + bias (+ residual); weight (cout, taps, cin)."""
+    b, f, h, w, cin = _cl5(x)
+    cout = _cl5(out)[4]
+    if weight.shape != (cout, ksize ** 3, cin) or not weight.is_contiguous():
+        raise ValueError(f"weight must be contiguous ({cout}, {ksize ** 3}, {cin}), got {tuple(weight.shape)}")
+    if residual is not None and residual.shape != out.shape:
+        raise ValueError("residual must have the output's shape")
+    _call("ltx_conv3d", _ptr(x), b, f, h, w, cin, _ptr(weight), _ptr(bias), cout, ksize, int(causal),
+          _ptr(residual), _ptr(out), _stream(x), label=f"conv3d k{ksize} {cin}->{cout} {b}x{f}x{h}x{w}"
+          if _profile is not None else None)
+
+
+def pixel_norm(x: torch.Tensor, y: torch.Tensor, eps: float = 1e-8, silu: bool = False) -> None:
+    c = x.shape[-1]
+    _call("ltx_pixel_norm", _ptr(x), _ptr(y), x.numel() // c, c, eps, int(silu), _stream(x),
+          label=f"pixel_norm C={c}" if _profile is not None else None)
+
+
+def group_norm1(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float, y: torch.Tensor,
+                workspace: torch.Tensor) -> None:
+    b, c = x.shape[0], x.shape[-1]
+    _call("ltx_group_norm1", _ptr(x), b, x.numel() // b, c, _ptr(weight), _ptr(bias), eps, _ptr(workspace),
+          workspace.numel() * workspace.element_size(), _ptr(y), _stream(x))
+
+
+def group_norm1_workspace(batch: int, device: torch.device) -> torch.Tensor:
+    nbytes = int(load_library().ltx_group_norm1_workspace_bytes(batch))
+    return torch.empty(nbytes // 8, dtype=torch.float64, device=device)
+
+
+def depth_to_space(x: torch.Tensor, stride: tuple[int, int, int], drop_first: bool, y: torch.Tensor) -> None:
+    b, f, h, w, cin = _cl5(x)
+    p1, p2, p3 = stride
+    c = cin // (p1 * p2 * p3)
+    if y.shape != (b, f * p1 - int(drop_first), h * p2, w * p3, c):
+        raise ValueError(f"output shape {tuple(y.shape)} does not match the rearrange")
+    _call("ltx_depth_to_space", _ptr(x), b, f, h, w, c, p1, p2, p3, int(drop_first), _ptr(y), _stream(x))
+
+
+def vae_latent_in(latent: torch.Tensor, std: torch.Tensor, mean: torch.Tensor, y: torch.Tensor) -> None:
+    b, c, f, h, w = latent.shape
+    _call("ltx_vae_latent_in", _ptr(latent.contiguous()), b, c, f, h, w, _ptr(std.float().contiguous()),
+          _ptr(mean.float().contiguous()), _ptr(y), _stream(latent))
+
+
+def vae_unpatchify(x: torch.Tensor, p: int, out: torch.Tensor, frames: bool = False) -> None:
+    b, f, h, w, cin = _cl5(x)
+    _call("ltx_vae_unpatchify", _ptr(x), b, f, h, w, cin // (p * p), p, int(frames), _ptr(out), _stream(x))
 
 
 def guide_rescale_workspace(n: int, device: torch.device) -> torch.Tensor:

@@ -6,3 +6,4 @@
 #include "gemm.cu"
 #include "attention.cu"
 #include "parallel.cu"
+#include "vae.cu"

@@ -1,0 +1,569 @@
+// Video VAE decoder kernels (lipaul/ltx-nv standalone/ltx_vae.py:20-222): the 3x3x3 /
+// 1x1x1 convolution as an implicit GEMM on the tcgen05 tensor cores, and the
+// channels-last element-wise stages around it (PixelNorm + SiLU, GroupNorm(1),
+// depth-to-space, latent un-normalisation, output unpatchify).
+//
+// Activations are channels-last (B, F, H, W, C) bf16 so that the C input channels of a
+// voxel are one contiguous row: the convolution's K dimension is (tap, channel) and an
+// A-operand row of 64 channels is one 128-byte line.
+#include <algorithm>
+
+#include "ltx_kernels.cuh"
+
+namespace ltx {
+namespace detail {
+
+LTX_DEVICE void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+LTX_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+LTX_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy
+// (tcgen05.mma operand reads).
+LTX_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+struct ConvShape {
+  int F, H, W;  // spatial size of input and output (stride 1, 'same' padding)
+  int cin, cout;
+  int taps;     // 27 (3x3x3) or 1 (1x1x1)
+  int t_off;    // input frame of tap dt: clamp(f + dt + t_off, 0, F - 1)
+  int m_vox;    // B * F * H * W output voxels
+};
+
+template <int BN>
+struct ConvCfg {
+  static constexpr int A_BYTES = 128 * 64 * 2;  // 128 voxels x 64 channels
+  static constexpr int B_BYTES = BN * 64 * 2;   // BN output channels x 64 channels
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+};
+// cp.async groups a producer thread keeps in flight before it signals a stage.
+constexpr int kConvLag = 2;
+
+// Implicit-GEMM convolution, one CTA per SM, persistent over (128-voxel, BN-channel)
+// output tiles. M = output voxels in (b, f, h, w) order, N = output channels, K = (tap,
+// input channel) in 64-channel blocks.
+//   warps 0-3  gather A: thread r copies voxel r's 64 input channels of the current tap
+//              (16-byte cp.async into the 128-byte-swizzled K-major layout, zero-filled
+//              outside the frame, frame index clamped in time), then signals the stage
+//   warp 4     TMA of the weight block [BN x 64] (weights (Cout, taps * Cin) row-major)
+//   warp 5     TMEM allocation and the single-thread tcgen05.mma issue (M=128, N=BN)
+//   warps 6-9  epilogue: one TMEM lane quadrant each, + bias (+ residual), bf16 stores
+// The TMEM accumulator is double-buffered so the epilogue of one tile overlaps the
+// MMAs of the next.
+template <int BN>
+__global__ void __launch_bounds__(320, 1)
+    conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __nv_bfloat16* __restrict__ x,
+                     const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* residual,
+                     __nv_bfloat16* out, ConvShape cs) {
+  using Cfg = ConvCfg<BN>;
+  constexpr int S = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int cchunks = cs.cin / 64;
+  const int k_blocks = cs.taps * cchunks;
+  const int n_tiles = (cs.cout + BN - 1) / BN;
+  const int num_tiles = ((cs.m_vox + 127) / 128) * n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 128 + 1);  // the 128 gathering threads + the weight TMA
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < 4) {
+    const int r = threadIdx.x;
+    const uint32_t a_row = smem_u32(smem) + uint32_t(r) * 128u;
+    const int sw = r & 7;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int v = (tile / n_tiles) * 128 + r;
+      const bool live = v < cs.m_vox;
+      const int w = v % cs.W;
+      int t = v / cs.W;
+      const int h = t % cs.H;
+      t /= cs.H;
+      const int f = t % cs.F;
+      const int b = t / cs.F;
+      for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        const int s = it % S;
+        if (!mbar_wait(&empty[s], (uint32_t(it / S) & 1u) ^ 1u, abort_flag)) goto drain;
+        const int tap = kb / cchunks, cc = kb - tap * cchunks;
+        int fi = f, hi = h, wi = w;
+        if (cs.taps == 27) {
+          fi = min(max(f + tap / 9 + cs.t_off, 0), cs.F - 1);
+          hi = h + (tap / 3) % 3 - 1;
+          wi = w + tap % 3 - 1;
+        }
+        const bool in = live && hi >= 0 && hi < cs.H && wi >= 0 && wi < cs.W;
+        const __nv_bfloat16* src =
+            in ? x + (((int64_t(b) * cs.F + fi) * cs.H + hi) * cs.W + wi) * cs.cin + cc * 64 : x;
+        const uint32_t dst = a_row + uint32_t(s * Cfg::STAGE_BYTES);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cp_async16(dst + uint32_t((j ^ sw) << 4), src + (in ? j * 8 : 0), in ? 16u : 0u);
+        cp_async_commit();
+        if (it >= kConvLag) {
+          cp_async_wait<kConvLag>();
+          fence_proxy_async_smem();
+          mbar_arrive(&full[(it - kConvLag) % S]);
+        }
+      }
+    }
+  drain:
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    for (int j = std::max(it - kConvLag, 0); j < it; ++j) mbar_arrive(&full[j % S]);
+  } else if (warp == 4) {
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&empty[s], (uint32_t(it / S) & 1u) ^ 1u, abort_flag)) goto done;
+          mbar_arrive_expect_tx(&full[s], Cfg::B_BYTES);
+          tma_load_2d(smem + s * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmW, &full[s], kb * 64, n0);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, BN, 0);
+      int it = 0, local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t u = uint32_t(local >> 1);
+        if (!mbar_wait(&tempty[acc], (u & 1u) ^ 1u, abort_flag)) goto done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], uint32_t(it / S) & 1u, abort_flag)) goto done;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * Cfg::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_ss(d_tmem, umma_desc_sw128(a_addr + k * 32, 16, 1024), umma_desc_sw128(b_addr + k * 32, 16, 1024),
+                    idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t u = uint32_t(local >> 1);
+      const int64_t m = int64_t(tile / n_tiles) * 128 + row;
+      const int n0 = (tile % n_tiles) * BN;
+      if (!mbar_wait(&tfull[acc], u & 1u, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN && n0 + c0 < cs.cout; c0 += 32) {
+        uint32_t rr[32];
+        tmem_ld32(tbase + uint32_t(c0), rr);
+        tmem_wait_ld();
+        if (m < cs.m_vox) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int col = n0 + c0 + g * 8;
+            if (col < cs.cout) {
+              float v[8], bb[8];
+              ld8<__nv_bfloat16>(bias + col, bb);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = round_bf16(__uint_as_float(rr[g * 8 + e]) + bb[e]);
+              if (residual != nullptr) {
+                float rs[8];
+                ld8<__nv_bfloat16>(residual + m * cs.cout + col, rs);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] += rs[e];
+              }
+              st8<__nv_bfloat16>(out + m * cs.cout + col, v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+done:
+  __syncwarp();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int BN>
+void launch_conv(const void* x, const void* w, const void* bias, const void* residual, void* out, const ConvShape& cs,
+                 cudaStream_t s) {
+  using Cfg = ConvCfg<BN>;
+  const uint64_t k = uint64_t(cs.taps) * uint64_t(cs.cin);
+  const CUtensorMap tw = make_tmap_bf16_2d(w, k, uint64_t(cs.cout), k, 64, BN);
+  auto kern = conv3d_tc_kernel<BN>;
+  static int attr_dev = -1;
+  int dev = 0;
+  LTX_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    attr_dev = dev;
+  }
+  const int64_t tiles = int64_t((cs.m_vox + 127) / 128) * ((cs.cout + BN - 1) / BN);
+  const int grid = int(std::min<int64_t>(tiles, num_sms()));
+  kern<<<grid, 320, Cfg::SMEM, s>>>(tw, static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(bias),
+                                     static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), cs),
+      ltx::note_launch();
+}
+
+// ---------------------------------------------------------------------------------
+// Element-wise stages (channels-last rows of C channels)
+// ---------------------------------------------------------------------------------
+
+// PixelNorm (ltx_vae.py:20-28) over the C channels of each voxel, optionally followed by
+// SiLU, with the bf16 roundings of the reference's tensor ops: x^2, mean, + eps, sqrt,
+// division and SiLU each round to bf16. One warp per voxel.
+__global__ void __launch_bounds__(256) pixel_norm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         __nv_bfloat16* __restrict__ y, int64_t rows, int C,
+                                                         float eps, int silu) {
+  const int64_t warps = int64_t(gridDim.x) * 8;
+  for (int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5); r < rows; r += warps) {
+    const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + r * C);
+    __nv_bfloat162* yr = reinterpret_cast<__nv_bfloat162*>(y + r * C);
+    const int lane = threadIdx.x & 31;
+    float ss = 0.f;
+    for (int j = lane; j < C / 2; j += 32) {
+      const float2 v = __bfloat1622float2(xr[j]);
+      ss += round_bf16(v.x * v.x) + round_bf16(v.y * v.y);
+    }
+    ss = warp_sum(ss);
+    const float mean = round_bf16(ss / float(C));
+    const float den = round_bf16(sqrtf(round_bf16(mean + eps)));
+    for (int j = lane; j < C / 2; j += 32) {
+      const float2 v = __bfloat1622float2(xr[j]);
+      float a = round_bf16(v.x / den), b = round_bf16(v.y / den);
+      if (silu) {
+        a = a / (1.f + expf(-a));
+        b = b / (1.f + expf(-b));
+      }
+      yr[j] = __floats2bfloat162_rn(a, b);
+    }
+  }
+}
+
+// GroupNorm with one group (ltx_vae.py:96, torch.nn.GroupNorm(1, C, eps=1e-6)): per sample
+// the mean and variance of all F*H*W*C values. Pass 1: per-block partial sums (fp64) of
+// value and square; pass 2: every block combines its sample's partials in block order
+// (deterministic) and writes (x - mean) * rstd * w[c] + b[c], rounded once.
+constexpr int kGnBlocks = 128;  // partial-sum blocks per sample
+
+__global__ void __launch_bounds__(256) group_norm_stats_kernel(const __nv_bfloat16* __restrict__ x, int64_t n,
+                                                               double* __restrict__ part) {
+  const int b = blockIdx.y;
+  const __nv_bfloat16* xs = x + int64_t(b) * n;
+  double s = 0.0, s2 = 0.0;
+  for (int64_t i = int64_t(blockIdx.x) * 256 + threadIdx.x; i < n; i += int64_t(kGnBlocks) * 256) {
+    const double v = double(__bfloat162float(xs[i]));
+    s += v;
+    s2 += v * v;
+  }
+  __shared__ double red[2][256];
+  red[0][threadIdx.x] = s;
+  red[1][threadIdx.x] = s2;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (threadIdx.x < o) {
+      red[0][threadIdx.x] += red[0][threadIdx.x + o];
+      red[1][threadIdx.x] += red[1][threadIdx.x + o];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    part[(int64_t(b) * kGnBlocks + blockIdx.x) * 2] = red[0][0];
+    part[(int64_t(b) * kGnBlocks + blockIdx.x) * 2 + 1] = red[1][0];
+  }
+}
+
+__global__ void __launch_bounds__(256) group_norm_apply_kernel(const __nv_bfloat16* __restrict__ x, int64_t n, int C,
+                                                               const __nv_bfloat16* __restrict__ wt,
+                                                               const __nv_bfloat16* __restrict__ bs, float eps,
+                                                               const double* __restrict__ part,
+                                                               __nv_bfloat16* __restrict__ y) {
+  const int b = blockIdx.y;
+  __shared__ float stat[2];
+  if (threadIdx.x == 0) {
+    double s = 0.0, s2 = 0.0;
+    for (int i = 0; i < kGnBlocks; ++i) {
+      s += part[(int64_t(b) * kGnBlocks + i) * 2];
+      s2 += part[(int64_t(b) * kGnBlocks + i) * 2 + 1];
+    }
+    const double mean = s / double(n);
+    const double var = std::max(s2 / double(n) - mean * mean, 0.0);
+    stat[0] = float(mean);
+    stat[1] = float(1.0 / sqrt(var + double(eps)));
+  }
+  __syncthreads();
+  const float mean = stat[0], rstd = stat[1];
+  const __nv_bfloat16* xs = x + int64_t(b) * n;
+  __nv_bfloat16* ys = y + int64_t(b) * n;
+  for (int64_t i = int64_t(blockIdx.x) * 256 + threadIdx.x; i < n; i += int64_t(gridDim.x) * 256) {
+    const int c = int(i % C);
+    const float v = (__bfloat162float(xs[i]) - mean) * rstd * __bfloat162float(wt[c]) + __bfloat162float(bs[c]);
+    ys[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// DepthToSpaceUpsample's rearrange (ltx_vae.py:135-143): input channel ((c*p1 + i)*p2 + j)*p3
+// + k of voxel (d, h, w) goes to channel c of voxel (d*p1 + i - drop, h*p2 + j, w*p3 + k);
+// with drop = 1 the first output frame is dropped. One thread per output (voxel, 8
+// channels).
+__global__ void __launch_bounds__(256) depth_to_space_kernel(const __nv_bfloat16* __restrict__ x,
+                                                             __nv_bfloat16* __restrict__ y, int B, int F, int H,
+                                                             int W, int c, int p1, int p2, int p3, int drop) {
+  const int Fo = F * p1 - drop, Ho = H * p2, Wo = W * p3;
+  const int cg = c / 8;
+  const int64_t total = int64_t(B) * Fo * Ho * Wo * cg;
+  const int cin = c * p1 * p2 * p3;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int g = int(i % cg);
+    int64_t t = i / cg;
+    const int wo = int(t % Wo);
+    t /= Wo;
+    const int ho = int(t % Ho);
+    t /= Ho;
+    const int fo = int(t % Fo);
+    const int b = int(t / Fo);
+    const int fd = fo + drop;
+    const int d = fd / p1, ii = fd - d * p1, h = ho / p2, jj = ho - h * p2, w = wo / p3, kk = wo - w * p3;
+    const __nv_bfloat16* src = x + (((int64_t(b) * F + d) * H + h) * W + w) * cin + (ii * p2 + jj) * p3 + kk;
+    const int step = p1 * p2 * p3;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = __bfloat162float(src[int64_t(g * 8 + e) * step]);
+    st8<__nv_bfloat16>(y + i * 8, v);
+  }
+}
+
+// PerChannelStatistics.un_normalize (ltx_vae.py:83-87) and the NCDHW -> channels-last
+// transpose of the latent: y[b,f,h,w,c] = round(round(x[b,c,f,h,w] * std[c]) + mean[c]), std
+// and mean rounded to bf16 first (the reference's .to(x)).
+__global__ void __launch_bounds__(256) vae_latent_in_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            const float* __restrict__ stdv,
+                                                            const float* __restrict__ meanv,
+                                                            __nv_bfloat16* __restrict__ y, int B, int C,
+                                                            int64_t fhw) {
+  const int64_t total = int64_t(B) * C * fhw;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int c = int(i % C);
+    const int64_t t = i / C;  // b * fhw + voxel
+    const int64_t b = t / fhw, vox = t - b * fhw;
+    const float v = __bfloat162float(x[(b * C + c) * fhw + vox]);
+    y[i] = __float2bfloat16_rn(round_bf16(v * round_bf16(stdv[c])) + round_bf16(meanv[c]));
+  }
+}
+
+// Output unpatchify (ltx_vae.py:212-216): channel ((c*p + r)*p + q) of voxel (f, h, w), q
+// fastest, goes to pixel (h*p + q, w*p + r) of channel c. mode 0 writes the reference's
+// (B, c, F, H*p, W*p) bf16 tensor; mode 1 writes decode_video's float (F, H*p, W*p, c)
+// frames of sample 0 in [0, 1] ((v + 1) / 2, clamped).
+__global__ void __launch_bounds__(256) vae_unpatchify_kernel(const __nv_bfloat16* __restrict__ x, void* out, int B,
+                                                             int F, int H, int W, int c, int p, int mode) {
+  const int Ho = H * p, Wo = W * p;
+  const int64_t total = (mode == 0 ? int64_t(B) : 1) * c * F * Ho * Wo;
+  const int cin = c * p * p;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int b, ch, f, ho, wo;
+    int64_t t = i;
+    if (mode == 0) {  // (B, c, F, Ho, Wo)
+      wo = int(t % Wo);
+      t /= Wo;
+      ho = int(t % Ho);
+      t /= Ho;
+      f = int(t % F);
+      t /= F;
+      ch = int(t % c);
+      b = int(t / c);
+    } else {  // (F, Ho, Wo, c) of sample 0
+      ch = int(t % c);
+      t /= c;
+      wo = int(t % Wo);
+      t /= Wo;
+      ho = int(t % Ho);
+      f = int(t / Ho);
+      b = 0;
+    }
+    const int h = ho / p, q = ho - h * p, w = wo / p, r = wo - w * p;
+    const float v = __bfloat162float(x[(((int64_t(b) * F + f) * H + h) * W + w) * cin + (ch * p + r) * p + q]);
+    if (mode == 0)
+      static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    else
+      static_cast<float*>(out)[i] = fminf(fmaxf((v + 1.f) * 0.5f, 0.f), 1.f);
+  }
+}
+
+int ew_grid(int64_t work, int per_block = 256) {
+  const int64_t cap = int64_t(num_sms()) * 16;
+  return int(std::max<int64_t>(1, std::min<int64_t>((work + per_block - 1) / per_block, cap)));
+}
+
+}  // namespace detail
+}  // namespace ltx
+
+using namespace ltx;
+using namespace ltx::detail;
+
+static void check16(const void* p, const char* what) {
+  if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+    throw ApiError{LTX_ERR_INVALID, std::string(what) + " must be 16-byte aligned"};
+}
+
+extern "C" int ltx_conv3d(const void* x, int B, int F, int H, int W, int cin, const void* weight, const void* bias,
+                          int cout, int ksize, int causal, const void* residual, void* out, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(x && weight && bias && out, "x, weight, bias and out must be non-NULL");
+  LTX_REQUIRE(ksize == 1 || ksize == 3, "ksize must be 1 or 3");
+  LTX_REQUIRE(B > 0 && F > 0 && H > 0 && W > 0, "sizes must be positive");
+  LTX_REQUIRE(cin > 0 && cin % 64 == 0, "cin must be a positive multiple of 64");
+  LTX_REQUIRE(cout > 0 && cout % 8 == 0, "cout must be a positive multiple of 8");
+  const int64_t m = int64_t(B) * F * H * W;
+  LTX_REQUIRE(m < (int64_t(1) << 31) && m * std::max(cin, cout) < (int64_t(1) << 46), "tensor too large");
+  LTX_REQUIRE(x != out && (residual == nullptr || residual != x), "out and residual must not alias x");
+  check16(x, "x");
+  check16(weight, "weight");
+  check16(bias, "bias");
+  check16(out, "out");
+  if (residual) check16(residual, "residual");
+  ConvShape cs;
+  cs.F = F;
+  cs.H = H;
+  cs.W = W;
+  cs.cin = cin;
+  cs.cout = cout;
+  cs.taps = ksize == 3 ? 27 : 1;
+  cs.t_off = causal ? -2 : -1;
+  cs.m_vox = int(m);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cout <= 64)
+    launch_conv<64>(x, weight, bias, residual, out, cs, s);
+  else if (cout <= 128)
+    launch_conv<128>(x, weight, bias, residual, out, cs, s);
+  else
+    launch_conv<256>(x, weight, bias, residual, out, cs, s);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_pixel_norm(const void* x, void* y, int64_t rows, int C, float eps, int silu, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(x && y, "x and y must be non-NULL");
+  LTX_REQUIRE(rows > 0 && C > 0 && C % 2 == 0, "rows must be positive and C even");
+  pixel_norm_kernel<<<ew_grid(rows, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), rows, C, eps, silu ? 1 : 0),
+      note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int64_t ltx_group_norm1_workspace_bytes(int B) { return B > 0 ? int64_t(B) * kGnBlocks * 2 * 8 : -1; }
+
+extern "C" int ltx_group_norm1(const void* x, int B, int64_t n_per_sample, int C, const void* weight,
+                               const void* bias, float eps, void* workspace, int64_t ws_bytes, void* y,
+                               void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(x && weight && bias && workspace && y, "NULL argument");
+  LTX_REQUIRE(B > 0 && C > 0 && n_per_sample > 0 && n_per_sample % C == 0, "bad sizes");
+  LTX_REQUIRE(ws_bytes >= ltx_group_norm1_workspace_bytes(B), "workspace smaller than ltx_group_norm1_workspace_bytes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto part = static_cast<double*>(workspace);
+  group_norm_stats_kernel<<<dim3(kGnBlocks, B), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), n_per_sample,
+                                                             part),
+      note_launch();
+  const int gx = std::max(1, std::min(ew_grid(n_per_sample), 1024));
+  group_norm_apply_kernel<<<dim3(gx, B), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(x), n_per_sample, C, static_cast<const __nv_bfloat16*>(weight),
+      static_cast<const __nv_bfloat16*>(bias), eps, part, static_cast<__nv_bfloat16*>(y)),
+      note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_depth_to_space(const void* x, int B, int F, int H, int W, int c, int p1, int p2, int p3,
+                                  int drop_first, void* y, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(x && y && x != y, "x and y must be non-NULL and distinct");
+  LTX_REQUIRE(B > 0 && F > 0 && H > 0 && W > 0 && c > 0 && c % 8 == 0, "bad sizes (c must be a multiple of 8)");
+  LTX_REQUIRE(p1 >= 1 && p2 >= 1 && p3 >= 1 && p1 <= 4 && p2 <= 4 && p3 <= 4, "strides must be 1..4");
+  LTX_REQUIRE(drop_first == 0 || (drop_first == 1 && F * p1 > 1), "drop_first must be 0 or 1");
+  check16(y, "y");
+  const int64_t work = int64_t(B) * (int64_t(F) * p1 - drop_first) * H * p2 * W * p3 * (c / 8);
+  depth_to_space_kernel<<<ew_grid(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), B, F, H, W, c, p1, p2, p3, drop_first),
+      note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_vae_latent_in(const void* latent, int B, int C, int F, int H, int W, const float* std_of_means,
+                                 const float* mean_of_means, void* y, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(latent && std_of_means && mean_of_means && y, "NULL argument");
+  LTX_REQUIRE(B > 0 && C > 0 && F > 0 && H > 0 && W > 0, "bad sizes");
+  const int64_t fhw = int64_t(F) * H * W;
+  vae_latent_in_kernel<<<ew_grid(int64_t(B) * C * fhw), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(latent), std_of_means, mean_of_means, static_cast<__nv_bfloat16*>(y), B, C,
+      fhw),
+      note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_vae_unpatchify(const void* x, int B, int F, int H, int W, int c, int p, int mode, void* out,
+                                  void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(x && out, "NULL argument");
+  LTX_REQUIRE(B > 0 && F > 0 && H > 0 && W > 0 && c > 0 && p > 0, "bad sizes");
+  LTX_REQUIRE(mode == 0 || mode == 1, "mode must be 0 (bf16 NCDHW) or 1 (float frames of sample 0)");
+  const int64_t work = (mode == 0 ? int64_t(B) : 1) * c * F * int64_t(H) * p * W * p;
+  vae_unpatchify_kernel<<<ew_grid(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), out, B, F, H, W, c, p, mode),
+      note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}

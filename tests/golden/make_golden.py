@@ -44,7 +44,7 @@ ROOT = Path(__file__).resolve().parents[2]
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-from oracle import ltx_oracle  # noqa: E402
+from oracle import ltx_oracle, vae_oracle  # noqa: E402
 
 
 def _import_reference(ref_root: Path):
@@ -326,10 +326,38 @@ def make_connector(ref_root: Path, dtype):
             "out_mask": out_mask}
 
 
+# Every decoder block kind (res_x, res_x_y with the GroupNorm + 1x1 shortcut,
+# compress_time / compress_space / compress_all) at channel counts the tcgen05
+# convolution takes (input channels a multiple of 64).
+VAE_CFG = {"decoder_blocks": [["res_x", {"num_layers": 1}], ["compress_all", {"multiplier": 2}],
+                              ["res_x_y", {"multiplier": 2}], ["compress_time", {"multiplier": 1}],
+                              ["compress_space", {"multiplier": 1}], ["res_x", {"num_layers": 1}]],
+           "decoder_base_channels": 64, "patch_size": 4, "spatial_padding_mode": "zeros", "latent_channels": 128,
+           "out_channels": 3}
+
+
+@torch.inference_mode()
+def make_vae(ref_root: Path, dtype):
+    """The reference's ConvVideoDecoder (ltx_vae.py:161-216) on a seeded (2, 128, 3, 4, 6)
+    latent -> (2, 3, 9, 64, 96)."""
+    sys.path.insert(0, str(ref_root / "standalone"))
+    import ltx_vae
+
+    dec = ltx_vae.ConvVideoDecoder(VAE_CFG)
+    shapes = [(n, tuple(p.shape)) for n, p in dec.named_parameters()]
+    sd = vae_oracle.synthetic_decoder_state_dict(shapes, WEIGHT_SEED + 7, VAE_CFG["latent_channels"])
+    dec.load_state_dict(sd)
+    dec = dec.to(dtype).eval()
+    latent = rng_normal((2, 128, 3, 4, 6), 500).to(dtype)
+    out = dec(latent)
+    return {"config": VAE_CFG, "param_shapes": shapes, "weight_seed": WEIGHT_SEED + 7,
+            "dtype": str(dtype).replace("torch.", ""), "latent": latent, "out": out}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["guide", "guided", "ckpt", "connector"], default=None,
+    ap.add_argument("--only", choices=["guide", "guided", "ckpt", "connector", "vae"], default=None,
                     help="regenerate one fixture only")
     args = ap.parse_args()
     ref_root = Path(args.reference)
@@ -347,6 +375,10 @@ def main():
         for dtype in (torch.float32, torch.bfloat16):
             rec = make_connector(ref_root, dtype)
             torch.save(rec, OUT / f"connector_{rec['dtype']}.pt")
+    if args.only in (None, "vae"):
+        for dtype in (torch.float32, torch.bfloat16):
+            rec = make_vae(ref_root, dtype)
+            torch.save(rec, OUT / f"vae_tiny_{rec['dtype']}.pt")
     if args.only is not None:
         return
     make_philox(ref_root)

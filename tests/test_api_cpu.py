@@ -46,6 +46,19 @@ def test_library_status_codes_without_a_gpu():
     assert lib.ltx_philox_offset_increment(1572864, 1184) == philox_oracle.offset_increment(1572864, 1184)
 
 
+def test_vae_decoder_parameter_layout_matches_reference():
+    """ConvVideoDecoder has the reference's parameter names, shapes and order (and its
+    per-channel statistics buffers), so reference state dicts load unchanged."""
+    import ltx_vae
+
+    rec = torch.load(gc.GOLDEN / "vae_tiny_bfloat16.pt", weights_only=False)
+    with torch.device("meta"):
+        dec = ltx_vae.ConvVideoDecoder(rec["config"])
+    assert [(n, tuple(p.shape)) for n, p in dec.named_parameters()] == [(n, tuple(s)) for n, s in rec["param_shapes"]]
+    assert {n for n, _ in dec.named_buffers()} == {"per_channel_statistics.std-of-means",
+                                                    "per_channel_statistics.mean-of-means"}
+
+
 def test_native_wrappers_refuse_cpu_tensors():
     with pytest.raises(ValueError):
         nat.gelu_tanh(torch.zeros(8), torch.zeros(8))

@@ -127,3 +127,17 @@ def test_oracle_text_connector_matches_reference(dtype):
                                              c["registers"], c["gated"], rec["hidden"], rec["mask"])
     assert torch.equal(out, rec["out"])
     assert torch.equal(mask, rec["out_mask"])
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_oracle_vae_decoder_matches_reference(dtype):
+    """ConvVideoDecoder.forward (ltx_vae.py:161-216) with every block kind, against the
+    reference's own output on the same seeded weights and latent."""
+    from oracle import vae_oracle
+
+    rec = torch.load(gc.GOLDEN / f"vae_tiny_{dtype}.pt", weights_only=False)
+    sd = vae_oracle.synthetic_decoder_state_dict(rec["param_shapes"], rec["weight_seed"],
+                                                 rec["config"]["latent_channels"])
+    sd = {k: v.to(getattr(torch, dtype)) for k, v in sd.items()}
+    out = vae_oracle.decode(sd, rec["config"], rec["latent"])
+    assert torch.equal(out, rec["out"])
