@@ -415,7 +415,48 @@ PROBES = {
     "qknorm": "q RMSNorm (with weight) + split RoPE in place on the packed QKV buffer, [2*6144, 2048] bf16",
     "connector": "text connector (Embeddings1DConnector): 8 blocks, 32x128 heads, 128 registers, B=2 prompts x "
                  "1024 tokens, bf16",
+    "vae": "video VAE decoder (ConvVideoDecoder), latent (1, 128, 9, 16, 24) -> 65 frames of 512x768, assumed "
+           "block layout base 128, [res_x 5, compress_all 2] x 3 + res_x 5 (random weights), bf16",
+    "conv3d": "one 3x3x3 decoder convolution at the last stage: 128 -> 128 channels over 65x128x192 voxels",
 }
+
+# Assumed production layout of the video decoder (the real one is read from the
+# checkpoint's metadata, absent here): 8x temporal and 8x spatial upsampling by three
+# compress_all stages, patch 4, so a (9, 16, 24) latent decodes to 65 frames of 512x768.
+VAE_PROBE_CFG = {"decoder_blocks": [["res_x", {"num_layers": 5}], ["compress_all", {"multiplier": 2}],
+                                    ["res_x", {"num_layers": 5}], ["compress_all", {"multiplier": 2}],
+                                    ["res_x", {"num_layers": 5}], ["compress_all", {"multiplier": 2}],
+                                    ["res_x", {"num_layers": 5}]],
+                 "decoder_base_channels": 128, "patch_size": 4, "spatial_padding_mode": "zeros",
+                 "latent_channels": 128, "out_channels": 3}
+
+
+def vae_conv_flops(dec, latent_shape) -> float:
+    """2 * voxels * taps * cin * cout summed over the decoder's convolutions."""
+    import ltx_vae
+
+    _, _, f, h, w = latent_shape
+    total = 0.0
+
+    def conv(c, vox):
+        k = c.kernel_size[0] * c.kernel_size[1] * c.kernel_size[2]
+        return 2.0 * vox * k * c.in_channels * c.out_channels
+
+    vox = f * h * w
+    total += conv(dec.conv_in.conv, vox)
+    for blk in dec.up_blocks:
+        res = blk.res_blocks if isinstance(blk, ltx_vae.UNetMidBlock3D) else (
+            [blk] if isinstance(blk, ltx_vae.ResnetBlock3D) else [])
+        for rb in res:
+            total += conv(rb.conv1.conv, vox) + conv(rb.conv2.conv, vox)
+            if isinstance(rb.conv_shortcut, torch.nn.Conv3d):
+                total += conv(rb.conv_shortcut, vox)
+        if isinstance(blk, ltx_vae.DepthToSpaceUpsample):
+            total += conv(blk.conv.conv, vox)
+            p1, p2, p3 = blk.stride
+            f, h, w = f * p1 - (1 if p1 == 2 else 0), h * p2, w * p3
+            vox = f * h * w
+    return total + conv(dec.conv_out.conv, vox)
 
 
 def run_probe(args, dev: torch.device) -> dict:
@@ -479,6 +520,34 @@ def run_probe(args, dev: torch.device) -> dict:
         flops = 8 * (2.0 * m_rows * dd * 3 * dd + 4.0 * 2 * s_len * s_len * dd + 2.0 * m_rows * dd * dd
                      + 2.0 * m_rows * dd * 4 * dd * 2)
         nbytes = 8 * 2 * (4 * dd * dd + 8 * dd * dd)  # weights streamed once per call
+    elif args.probe == "vae":
+        import ltx_vae
+
+        with torch.device("meta"):
+            dec = ltx_vae.ConvVideoDecoder(VAE_PROBE_CFG)
+        sd = {}
+        for name, prm in list(dec.named_parameters()) + list(dec.named_buffers()):
+            if name.endswith("std-of-means"):
+                sd[name] = torch.ones(prm.shape, device=dev)
+            elif name.endswith("mean-of-means"):
+                sd[name] = torch.zeros(prm.shape, device=dev)
+            else:
+                fan = prm[0].numel() if prm.dim() > 1 else 1
+                sd[name] = torch.randn(prm.shape, generator=g, device=dev) * (fan ** -0.5 if prm.dim() > 1 else 0.02)
+        dec.load_state_dict(sd, assign=True)
+        dec = dec.eval()
+        latent = rnd(1, 128, 9, 16, 24)
+        fn = lambda: dec(latent)  # noqa: E731
+        flops = vae_conv_flops(dec, latent.shape)
+        nbytes = 2 * 3 * 65 * 512 * 768
+    elif args.probe == "conv3d":
+        f_, h_, w_, cc = 65, 128, 192, 128
+        x = rnd(1, f_, h_, w_, cc)
+        wt, bias = rnd(cc, 27, cc, scale=(27 * cc) ** -0.5), rnd(cc)
+        out = torch.empty_like(x)
+        fn = lambda: nat.conv3d(x, wt, bias, out, 3)  # noqa: E731
+        flops = 2.0 * f_ * h_ * w_ * 27 * cc * cc
+        nbytes = 2 * (x.numel() + out.numel() + wt.numel())
     elif args.probe == "qknorm":
         qkv = rnd(m, 3 * d + c["heads"])
         wq = (1 + rnd(d, scale=0.02).float()).to(torch.bfloat16)
