@@ -52,6 +52,31 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, u
   return m;
 }
 
+CUtensorMap make_tmap_bf16_4d(const void* ptr, const uint64_t (&dims)[4], const uint64_t (&strides)[3],
+                              const uint32_t (&box)[4]) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+    throw ApiError{LTX_ERR_INVALID, "TMA operand must be 16-byte aligned"};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 16 != 0) throw ApiError{LTX_ERR_INVALID, "TMA strides must be multiples of 16 bytes"};
+  if (box[0] * 2 > 128 || box[0] == 0)
+    throw ApiError{LTX_ERR_INVALID, "TMA box out of range"};
+  for (int i = 1; i < 4; ++i)
+    if (box[i] == 0 || box[i] > 256) throw ApiError{LTX_ERR_INVALID, "TMA box out of range"};
+  auto fn = encode_fn();
+  if (fn == nullptr) throw ApiError{LTX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable"};
+  CUtensorMap m;
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t st[3] = {strides[0], strides[1], strides[2]};
+  cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), d, st, bx, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw ApiError{LTX_ERR_CUDA, "cuTensorMapEncodeTiled (4-D) failed with code " + std::to_string(int(r))};
+  return m;
+}
+
 static std::atomic<uint64_t> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 

@@ -202,6 +202,16 @@ LTX_DEVICE void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int x, i
       : "memory");
 }
 
+// 4-D tiled load (box x fastest); coordinates other than x may be negative or past the
+// end (zero fill); x times the element size must be a multiple of 16 bytes.
+LTX_DEVICE void tma_load_4d(void* dst, const void* tmap, uint64_t* bar, int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 // ---------------------------------------------------------------------------------
 // tcgen05: TMEM allocation, UMMA issue, commit, TMEM loads / stores
 // ---------------------------------------------------------------------------------

@@ -22,6 +22,10 @@ struct ApiError {
 // inner = elements per row (contiguous), outer = rows, ld = elements between rows,
 // box = (box_inner x box_outer) elements; box_inner * 2 must be <= 128.
 // Throws ApiError on invalid input.
+// Encode a 4-D, 128-byte-swizzled bf16 tensor map: dims[0] contiguous, strides in bytes
+// for dims 1..3, box[0] * 2 <= 128 bytes. Throws ApiError on invalid input.
+CUtensorMap make_tmap_bf16_4d(const void* ptr, const uint64_t (&dims)[4], const uint64_t (&strides)[3],
+                              const uint32_t (&box)[4]);
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
                               uint32_t box_outer);
 

@@ -13,24 +13,14 @@
 namespace ltx {
 namespace detail {
 
-LTX_DEVICE void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-LTX_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-LTX_DEVICE void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-// Make this thread's generic-proxy shared-memory writes visible to the async proxy
-// (tcgen05.mma operand reads).
-LTX_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
 struct ConvShape {
   int F, H, W;  // spatial size of input and output (stride 1, 'same' padding)
   int cin, cout;
   int taps;     // 27 (3x3x3) or 1 (1x1x1)
   int t_off;    // input frame of tap dt: clamp(f + dt + t_off, 0, F - 1)
-  int m_vox;    // B * F * H * W output voxels
+  int bf;       // B * F frames
+  int hb, wb;   // spatial block of one M tile: hb rows x wb columns of one frame, hb * wb = 128
+  int th, tw;   // blocks per frame: ceil(H / hb) x ceil(W / wb)
 };
 
 template <int BN>
@@ -43,25 +33,24 @@ struct ConvCfg {
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
 };
-// cp.async groups a producer thread keeps in flight before it signals a stage.
-constexpr int kConvLag = 2;
 
-// Implicit-GEMM convolution, one CTA per SM, persistent over (128-voxel, BN-channel)
-// output tiles. M = output voxels in (b, f, h, w) order, N = output channels, K = (tap,
-// input channel) in 64-channel blocks.
-//   warps 0-3  gather A: thread r copies voxel r's 64 input channels of the current tap
-//              (16-byte cp.async into the 128-byte-swizzled K-major layout, zero-filled
-//              outside the frame, frame index clamped in time), then signals the stage
-//   warp 4     TMA of the weight block [BN x 64] (weights (Cout, taps * Cin) row-major)
-//   warp 5     TMEM allocation and the single-thread tcgen05.mma issue (M=128, N=BN)
-//   warps 6-9  epilogue: one TMEM lane quadrant each, + bias (+ residual), bf16 stores
+// Implicit-GEMM convolution, one CTA per SM, persistent over output tiles of 128 voxels
+// (an hb x wb block of one frame) by BN output channels. K = (tap, 64-channel block).
+// The A operand of a k-block is the input block shifted by the tap, (64 channels, wb,
+// hb, 1 frame), loaded by one 4-D TMA from the channels-last activation: the hardware
+// zero-fills rows and columns outside the frame, and the frame coordinate is clamped
+// (edge-frame padding). The box lands as 128 rows of 128 bytes in the 128B-swizzled
+// K-major layout the MMA reads.
+//   warp 0     TMA of the input block and of the weight block [BN x 64]
+//   warp 1     TMEM allocation and the single-thread tcgen05.mma issue (M=128, N=BN)
+//   warps 2-5  epilogue: one TMEM lane quadrant each, + bias (+ residual), bf16 stores
 // The TMEM accumulator is double-buffered so the epilogue of one tile overlaps the
 // MMAs of the next.
 template <int BN>
-__global__ void __launch_bounds__(320, 1)
-    conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __nv_bfloat16* __restrict__ x,
-                     const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* residual,
-                     __nv_bfloat16* out, ConvShape cs) {
+__global__ void __launch_bounds__(192, 1)
+    conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* residual, __nv_bfloat16* out,
+                     ConvShape cs) {
   using Cfg = ConvCfg<BN>;
   constexpr int S = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -77,11 +66,12 @@ __global__ void __launch_bounds__(320, 1)
   const int cchunks = cs.cin / 64;
   const int k_blocks = cs.taps * cchunks;
   const int n_tiles = (cs.cout + BN - 1) / BN;
-  const int num_tiles = ((cs.m_vox + 127) / 128) * n_tiles;
+  const int per_frame = cs.th * cs.tw;
+  const int num_tiles = cs.bf * per_frame * n_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 128 + 1);  // the 128 gathering threads + the weight TMA
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -90,9 +80,10 @@ __global__ void __launch_bounds__(320, 1)
     }
     *abort_flag = 0;
     fence_mbar_init();
+    tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
   }
-  if (warp == 5) {
+  if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tmem_relinquish();
   }
@@ -101,62 +92,32 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp < 4) {
-    const int r = threadIdx.x;
-    const uint32_t a_row = smem_u32(smem) + uint32_t(r) * 128u;
-    const int sw = r & 7;
-    int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int v = (tile / n_tiles) * 128 + r;
-      const bool live = v < cs.m_vox;
-      const int w = v % cs.W;
-      int t = v / cs.W;
-      const int h = t % cs.H;
-      t /= cs.H;
-      const int f = t % cs.F;
-      const int b = t / cs.F;
-      for (int kb = 0; kb < k_blocks; ++kb, ++it) {
-        const int s = it % S;
-        if (!mbar_wait(&empty[s], (uint32_t(it / S) & 1u) ^ 1u, abort_flag)) goto drain;
-        const int tap = kb / cchunks, cc = kb - tap * cchunks;
-        int fi = f, hi = h, wi = w;
-        if (cs.taps == 27) {
-          fi = min(max(f + tap / 9 + cs.t_off, 0), cs.F - 1);
-          hi = h + (tap / 3) % 3 - 1;
-          wi = w + tap % 3 - 1;
-        }
-        const bool in = live && hi >= 0 && hi < cs.H && wi >= 0 && wi < cs.W;
-        const __nv_bfloat16* src =
-            in ? x + (((int64_t(b) * cs.F + fi) * cs.H + hi) * cs.W + wi) * cs.cin + cc * 64 : x;
-        const uint32_t dst = a_row + uint32_t(s * Cfg::STAGE_BYTES);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) cp_async16(dst + uint32_t((j ^ sw) << 4), src + (in ? j * 8 : 0), in ? 16u : 0u);
-        cp_async_commit();
-        if (it >= kConvLag) {
-          cp_async_wait<kConvLag>();
-          fence_proxy_async_smem();
-          mbar_arrive(&full[(it - kConvLag) % S]);
-        }
-      }
-    }
-  drain:
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    for (int j = std::max(it - kConvLag, 0); j < it; ++j) mbar_arrive(&full[j % S]);
-  } else if (warp == 4) {
+  if (warp == 0) {
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int n0 = (tile % n_tiles) * BN;
+        const int mt = tile / n_tiles, n0 = (tile - mt * n_tiles) * BN;
+        const int bf = mt / per_frame, rem = mt - bf * per_frame;
+        const int h0 = (rem / cs.tw) * cs.hb, w0 = (rem % cs.tw) * cs.wb;
+        const int f = bf % cs.F, fbase = bf - f;
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
           const int s = it % S;
           if (!mbar_wait(&empty[s], (uint32_t(it / S) & 1u) ^ 1u, abort_flag)) goto done;
-          mbar_arrive_expect_tx(&full[s], Cfg::B_BYTES);
-          tma_load_2d(smem + s * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmW, &full[s], kb * 64, n0);
+          const int tap = kb / cchunks, cc = kb - tap * cchunks;
+          int fi = f, dh = 0, dw = 0;
+          if (cs.taps == 27) {
+            fi = min(max(f + tap / 9 + cs.t_off, 0), cs.F - 1);
+            dh = (tap / 3) % 3 - 1;
+            dw = tap % 3 - 1;
+          }
+          uint8_t* sa = smem + s * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          tma_load_4d(sa, &tmX, &full[s], cc * 64, w0 + dw, h0 + dh, fbase + fi);
+          tma_load_2d(sa + Cfg::A_BYTES, &tmW, &full[s], kb * 64, n0);
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16(128, BN, 0);
       int it = 0, local = 0;
@@ -184,12 +145,16 @@ __global__ void __launch_bounds__(320, 1)
   } else {
     const int q = warp & 3;
     const int row = q * 32 + lane;
+    const int rh = row / cs.wb, rw = row - rh * cs.wb;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t u = uint32_t(local >> 1);
-      const int64_t m = int64_t(tile / n_tiles) * 128 + row;
-      const int n0 = (tile % n_tiles) * BN;
+      const int mt = tile / n_tiles, n0 = (tile - mt * n_tiles) * BN;
+      const int bf = mt / per_frame, rem = mt - bf * per_frame;
+      const int hh = (rem / cs.tw) * cs.hb + rh, ww = (rem % cs.tw) * cs.wb + rw;
+      const bool live = hh < cs.H && ww < cs.W;
+      const int64_t m = (int64_t(bf) * cs.H + hh) * cs.W + ww;
       if (!mbar_wait(&tfull[acc], u & 1u, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
@@ -198,7 +163,7 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t rr[32];
         tmem_ld32(tbase + uint32_t(c0), rr);
         tmem_wait_ld();
-        if (m < cs.m_vox) {
+        if (live) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             const int col = n0 + c0 + g * 8;
@@ -226,18 +191,39 @@ __global__ void __launch_bounds__(320, 1)
 done:
   __syncwarp();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
+// Spatial block of a 128-voxel M tile for an H x W frame: the (hb, wb) with hb * wb = 128
+// whose blocks cover the frame with the fewest padded voxels (ties: the wider block).
+void conv_block_shape(int H, int W, int& hb, int& wb) {
+  int64_t best = -1;
+  for (int w = 128; w >= 1; w >>= 1) {
+    const int h = 128 / w;
+    const int64_t cover = int64_t((H + h - 1) / h) * h * (int64_t((W + w - 1) / w) * w);
+    if (best < 0 || cover < best) {
+      best = cover;
+      hb = h;
+      wb = w;
+    }
+  }
+}
+
 template <int BN>
-void launch_conv(const void* x, const void* w, const void* bias, const void* residual, void* out, const ConvShape& cs,
-                 cudaStream_t s) {
+void launch_conv(const void* x, int B, const void* w, const void* bias, const void* residual, void* out,
+                 ConvShape cs, cudaStream_t s) {
   using Cfg = ConvCfg<BN>;
   const uint64_t k = uint64_t(cs.taps) * uint64_t(cs.cin);
   const CUtensorMap tw = make_tmap_bf16_2d(w, k, uint64_t(cs.cout), k, 64, BN);
+  const uint64_t c2 = uint64_t(cs.cin) * 2;
+  const uint64_t dims[4] = {uint64_t(cs.cin), uint64_t(cs.W), uint64_t(cs.H), uint64_t(B) * cs.F};
+  // byte strides of W, H and frame
+  const uint64_t strides[3] = {c2, c2 * cs.W, c2 * cs.W * cs.H};
+  const uint32_t box[4] = {64, uint32_t(cs.wb), uint32_t(cs.hb), 1};
+  const CUtensorMap tx = make_tmap_bf16_4d(x, dims, strides, box);
   auto kern = conv3d_tc_kernel<BN>;
   static int attr_dev = -1;
   int dev = 0;
@@ -246,9 +232,9 @@ void launch_conv(const void* x, const void* w, const void* bias, const void* res
     LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     attr_dev = dev;
   }
-  const int64_t tiles = int64_t((cs.m_vox + 127) / 128) * ((cs.cout + BN - 1) / BN);
+  const int64_t tiles = int64_t(cs.bf) * cs.th * cs.tw * ((cs.cout + BN - 1) / BN);
   const int grid = int(std::min<int64_t>(tiles, num_sms()));
-  kern<<<grid, 320, Cfg::SMEM, s>>>(tw, static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(bias),
+  kern<<<grid, 192, Cfg::SMEM, s>>>(tx, tw, static_cast<const __nv_bfloat16*>(bias),
                                      static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), cs),
       ltx::note_launch();
 }
@@ -478,14 +464,18 @@ extern "C" int ltx_conv3d(const void* x, int B, int F, int H, int W, int cin, co
   cs.cout = cout;
   cs.taps = ksize == 3 ? 27 : 1;
   cs.t_off = causal ? -2 : -1;
-  cs.m_vox = int(m);
+  cs.bf = B * F;
+  conv_block_shape(H, W, cs.hb, cs.wb);
+  cs.th = (H + cs.hb - 1) / cs.hb;
+  cs.tw = (W + cs.wb - 1) / cs.wb;
+  LTX_REQUIRE(int64_t(cs.bf) * cs.th * cs.tw * ((cout + 255) / 64) < (int64_t(1) << 31), "tensor too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cout <= 64)
-    launch_conv<64>(x, weight, bias, residual, out, cs, s);
+    launch_conv<64>(x, B, weight, bias, residual, out, cs, s);
   else if (cout <= 128)
-    launch_conv<128>(x, weight, bias, residual, out, cs, s);
+    launch_conv<128>(x, B, weight, bias, residual, out, cs, s);
   else
-    launch_conv<256>(x, weight, bias, residual, out, cs, s);
+    launch_conv<256>(x, B, weight, bias, residual, out, cs, s);
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
