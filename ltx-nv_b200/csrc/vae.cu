@@ -19,39 +19,42 @@ struct ConvShape {
   int taps;     // 27 (3x3x3) or 1 (1x1x1)
   int t_off;    // input frame of tap dt: clamp(f + dt + t_off, 0, F - 1)
   int bf;       // B * F frames
-  int hb, wb;   // spatial block of one M tile: hb rows x wb columns of one frame, hb * wb = 128
+  int hb, wb;   // spatial block of one M tile: hb rows x wb columns of one frame, hb * wb = 128 * MH
   int th, tw;   // blocks per frame: ceil(H / hb) x ceil(W / wb)
 };
 
-template <int BN>
+// MH = 128-row halves of an M tile: 2 for BN <= 128 (256 voxels share each weight block,
+// two M=128 accumulators), 1 for BN = 256 (TMEM holds 2 x 256 columns).
+template <int BN, int MH>
 struct ConvCfg {
-  static constexpr int A_BYTES = 128 * 64 * 2;  // 128 voxels x 64 channels
-  static constexpr int B_BYTES = BN * 64 * 2;   // BN output channels x 64 channels
+  static constexpr int A_BYTES = MH * 128 * 64 * 2;  // 128 * MH voxels x 64 channels
+  static constexpr int B_BYTES = BN * 64 * 2;        // BN output channels x 64 channels
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * MH * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
 };
 
-// Implicit-GEMM convolution, one CTA per SM, persistent over output tiles of 128 voxels
-// (an hb x wb block of one frame) by BN output channels. K = (tap, 64-channel block).
+// Implicit-GEMM convolution, one CTA per SM, persistent over output tiles of 128 * MH
+// voxels (an hb x wb block of one frame) by BN output channels. K = (tap, 64-channel
+// block).
 // The A operand of a k-block is the input block shifted by the tap, (64 channels, wb,
 // hb, 1 frame), loaded by one 4-D TMA from the channels-last activation: the hardware
 // zero-fills rows and columns outside the frame, and the frame coordinate is clamped
 // (edge-frame padding). The box lands as 128 rows of 128 bytes in the 128B-swizzled
 // K-major layout the MMA reads.
 //   warp 0     TMA of the input block and of the weight block [BN x 64]
-//   warp 1     TMEM allocation and the single-thread tcgen05.mma issue (M=128, N=BN)
+//   warp 1     TMEM allocation and the single-thread tcgen05.mma issue (MH x M=128, N=BN)
 //   warps 2-5  epilogue: one TMEM lane quadrant each, + bias (+ residual), bf16 stores
 // The TMEM accumulator is double-buffered so the epilogue of one tile overlaps the
 // MMAs of the next.
-template <int BN>
+template <int BN, int MH>
 __global__ void __launch_bounds__(192, 1)
     conv3d_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* residual, __nv_bfloat16* out,
                      ConvShape cs) {
-  using Cfg = ConvCfg<BN>;
+  using Cfg = ConvCfg<BN, MH>;
   constexpr int S = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -126,7 +129,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t u = uint32_t(local >> 1);
         if (!mbar_wait(&tempty[acc], (u & 1u) ^ 1u, abort_flag)) goto done;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * MH * BN);
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
           const int s = it % S;
           if (!mbar_wait(&full[s], uint32_t(it / S) & 1u, abort_flag)) goto done;
@@ -134,9 +137,11 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t a_addr = smem_u32(smem + s * Cfg::STAGE_BYTES);
           const uint32_t b_addr = a_addr + Cfg::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_ss(d_tmem, umma_desc_sw128(a_addr + k * 32, 16, 1024), umma_desc_sw128(b_addr + k * 32, 16, 1024),
-                    idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          for (int h = 0; h < MH; ++h)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              umma_ss(d_tmem + uint32_t(h * BN), umma_desc_sw128(a_addr + h * 16384 + k * 32, 16, 1024),
+                      umma_desc_sw128(b_addr + k * 32, 16, 1024), idesc, (kb > 0 || k > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
         }
         umma_commit(&tfull[acc]);
@@ -144,20 +149,22 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const int rh = row / cs.wb, rw = row - rh * cs.wb;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t u = uint32_t(local >> 1);
       const int mt = tile / n_tiles, n0 = (tile - mt * n_tiles) * BN;
       const int bf = mt / per_frame, rem = mt - bf * per_frame;
+      if (!mbar_wait(&tfull[acc], u & 1u, abort_flag)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int h = 0; h < MH; ++h) {
+      const int row = h * 128 + q * 32 + lane;
+      const int rh = row / cs.wb, rw = row - rh * cs.wb;
       const int hh = (rem / cs.tw) * cs.hb + rh, ww = (rem % cs.tw) * cs.wb + rw;
       const bool live = hh < cs.H && ww < cs.W;
       const int64_t m = (int64_t(bf) * cs.H + hh) * cs.W + ww;
-      if (!mbar_wait(&tfull[acc], u & 1u, abort_flag)) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + uint32_t(acc * BN) + (uint32_t(q * 32) << 16);
+      const uint32_t tbase = tmem_base + uint32_t((acc * MH + h) * BN) + (uint32_t(q * 32) << 16);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN && n0 + c0 < cs.cout; c0 += 32) {
         uint32_t rr[32];
@@ -183,6 +190,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -197,12 +205,13 @@ done:
   }
 }
 
-// Spatial block of a 128-voxel M tile for an H x W frame: the (hb, wb) with hb * wb = 128
-// whose blocks cover the frame with the fewest padded voxels (ties: the wider block).
-void conv_block_shape(int H, int W, int& hb, int& wb) {
+// Spatial block of an M tile of `rows` voxels for an H x W frame: the (hb, wb) with
+// hb * wb = rows whose blocks cover the frame with the fewest padded voxels (ties: the
+// wider block).
+void conv_block_shape(int H, int W, int rows, int& hb, int& wb) {
   int64_t best = -1;
-  for (int w = 128; w >= 1; w >>= 1) {
-    const int h = 128 / w;
+  for (int w = rows; w >= 1; w >>= 1) {
+    const int h = rows / w;
     const int64_t cover = int64_t((H + h - 1) / h) * h * (int64_t((W + w - 1) / w) * w);
     if (best < 0 || cover < best) {
       best = cover;
@@ -212,10 +221,15 @@ void conv_block_shape(int H, int W, int& hb, int& wb) {
   }
 }
 
-template <int BN>
+template <int BN, int MH>
 void launch_conv(const void* x, int B, const void* w, const void* bias, const void* residual, void* out,
                  ConvShape cs, cudaStream_t s) {
-  using Cfg = ConvCfg<BN>;
+  using Cfg = ConvCfg<BN, MH>;
+  conv_block_shape(cs.H, cs.W, 128 * MH, cs.hb, cs.wb);
+  cs.th = (cs.H + cs.hb - 1) / cs.hb;
+  cs.tw = (cs.W + cs.wb - 1) / cs.wb;
+  if (int64_t(cs.bf) * cs.th * cs.tw * ((cs.cout + BN - 1) / BN) >= (int64_t(1) << 31))
+    throw ApiError{LTX_ERR_INVALID, "tensor too large"};
   const uint64_t k = uint64_t(cs.taps) * uint64_t(cs.cin);
   const CUtensorMap tw = make_tmap_bf16_2d(w, k, uint64_t(cs.cout), k, 64, BN);
   const uint64_t c2 = uint64_t(cs.cin) * 2;
@@ -224,7 +238,7 @@ void launch_conv(const void* x, int B, const void* w, const void* bias, const vo
   const uint64_t strides[3] = {c2, c2 * cs.W, c2 * cs.W * cs.H};
   const uint32_t box[4] = {64, uint32_t(cs.wb), uint32_t(cs.hb), 1};
   const CUtensorMap tx = make_tmap_bf16_4d(x, dims, strides, box);
-  auto kern = conv3d_tc_kernel<BN>;
+  auto kern = conv3d_tc_kernel<BN, MH>;
   static int attr_dev = -1;
   int dev = 0;
   LTX_CUDA(cudaGetDevice(&dev));
@@ -465,17 +479,13 @@ extern "C" int ltx_conv3d(const void* x, int B, int F, int H, int W, int cin, co
   cs.taps = ksize == 3 ? 27 : 1;
   cs.t_off = causal ? -2 : -1;
   cs.bf = B * F;
-  conv_block_shape(H, W, cs.hb, cs.wb);
-  cs.th = (H + cs.hb - 1) / cs.hb;
-  cs.tw = (W + cs.wb - 1) / cs.wb;
-  LTX_REQUIRE(int64_t(cs.bf) * cs.th * cs.tw * ((cout + 255) / 64) < (int64_t(1) << 31), "tensor too large");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cout <= 64)
-    launch_conv<64>(x, B, weight, bias, residual, out, cs, s);
+    launch_conv<64, 2>(x, B, weight, bias, residual, out, cs, s);
   else if (cout <= 128)
-    launch_conv<128>(x, B, weight, bias, residual, out, cs, s);
+    launch_conv<128, 2>(x, B, weight, bias, residual, out, cs, s);
   else
-    launch_conv<256>(x, B, weight, bias, residual, out, cs, s);
+    launch_conv<256, 1>(x, B, weight, bias, residual, out, cs, s);
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
