@@ -259,10 +259,63 @@ void launch_conv(const void* x, int B, const void* w, const void* bias, const vo
 
 // PixelNorm (ltx_vae.py:20-28) over the C channels of each voxel, optionally followed by
 // SiLU, with the bf16 roundings of the reference's tensor ops: x^2, mean, + eps, sqrt,
-// division and SiLU each round to bf16. One warp per voxel.
+// division and SiLU each round to bf16. G lanes share a voxel and each holds V 16-byte
+// chunks (8 channels) of it in registers: C = 8 * G * V, one read and one write per
+// element.
+template <int G, int V>
 __global__ void __launch_bounds__(256) pixel_norm_kernel(const __nv_bfloat16* __restrict__ x,
-                                                         __nv_bfloat16* __restrict__ y, int64_t rows, int C,
-                                                         float eps, int silu) {
+                                                         __nv_bfloat16* __restrict__ y, int64_t rows, float eps,
+                                                         int silu) {
+  constexpr int C = 8 * G * V;
+  constexpr int PER_WARP = 32 / G;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / G, li = lane % G;
+  const int64_t step = int64_t(gridDim.x) * 8 * PER_WARP;
+  for (int64_t r0 = (int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5)) * PER_WARP; r0 < rows; r0 += step) {
+    const int64_t r = r0 + sub;
+    const bool live = r < rows;
+    uint4 u[V];
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      u[v] = live ? *reinterpret_cast<const uint4*>(x + r * C + (v * G + li) * 8) : make_uint4(0, 0, 0, 0);
+      float a[8];
+      unpack_bf16x2(u[v].x, a[0], a[1]);
+      unpack_bf16x2(u[v].y, a[2], a[3]);
+      unpack_bf16x2(u[v].z, a[4], a[5]);
+      unpack_bf16x2(u[v].w, a[6], a[7]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += round_bf16(a[e] * a[e]);
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float mean = round_bf16(ss / float(C));
+    const float den = round_bf16(sqrtf(round_bf16(mean + eps)));
+    // x / den as x * (1 / den): within one fp32 ulp of the division, before the bf16
+    // rounding; SiLU with the fast exponential and divide intrinsics
+    const float rden = 1.f / den;
+    if (!live) continue;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      float a[8];
+      unpack_bf16x2(u[v].x, a[0], a[1]);
+      unpack_bf16x2(u[v].y, a[2], a[3]);
+      unpack_bf16x2(u[v].z, a[4], a[5]);
+      unpack_bf16x2(u[v].w, a[6], a[7]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        a[e] = round_bf16(a[e] * rden);
+        if (silu) a[e] = __fdividef(a[e], 1.f + __expf(-a[e]));
+      }
+      st8<__nv_bfloat16>(y + r * C + (v * G + li) * 8, a);
+    }
+  }
+}
+
+// Any other even C: one warp per voxel, two channels per lane step (two reads per element).
+__global__ void __launch_bounds__(256) pixel_norm_generic_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                 __nv_bfloat16* __restrict__ y, int64_t rows, int C,
+                                                                 float eps, int silu) {
   const int64_t warps = int64_t(gridDim.x) * 8;
   for (int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5); r < rows; r += warps) {
     const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + r * C);
@@ -494,9 +547,24 @@ extern "C" int ltx_pixel_norm(const void* x, void* y, int64_t rows, int C, float
   LTX_API_BEGIN
   LTX_REQUIRE(x && y, "x and y must be non-NULL");
   LTX_REQUIRE(rows > 0 && C > 0 && C % 2 == 0, "rows must be positive and C even");
-  pixel_norm_kernel<<<ew_grid(rows, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), rows, C, eps, silu ? 1 : 0),
-      note_launch();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto xp = static_cast<const __nv_bfloat16*>(x);
+  auto yp = static_cast<__nv_bfloat16*>(y);
+  const int sl = silu ? 1 : 0;
+  const bool vec = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
+  // voxels per 256-thread block: 8 warps x (32 / G)
+  if (vec && C == 64)
+    pixel_norm_kernel<8, 1><<<ew_grid(rows, 32), 256, 0, s>>>(xp, yp, rows, eps, sl), note_launch();
+  else if (vec && C == 128)
+    pixel_norm_kernel<16, 1><<<ew_grid(rows, 16), 256, 0, s>>>(xp, yp, rows, eps, sl), note_launch();
+  else if (vec && C == 256)
+    pixel_norm_kernel<32, 1><<<ew_grid(rows, 8), 256, 0, s>>>(xp, yp, rows, eps, sl), note_launch();
+  else if (vec && C == 512)
+    pixel_norm_kernel<32, 2><<<ew_grid(rows, 8), 256, 0, s>>>(xp, yp, rows, eps, sl), note_launch();
+  else if (vec && C == 1024)
+    pixel_norm_kernel<32, 4><<<ew_grid(rows, 8), 256, 0, s>>>(xp, yp, rows, eps, sl), note_launch();
+  else
+    pixel_norm_generic_kernel<<<ew_grid(rows, 8), 256, 0, s>>>(xp, yp, rows, C, eps, sl), note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

@@ -75,9 +75,12 @@ def test_conv3d_residual_in_place_and_errors():
         nat.conv3d(x, wt[:, :1], bias, acc, 3)
 
 
-def test_pixel_norm_silu_matches_oracle():
+@pytest.mark.parametrize("c", [64, 128, 256, 512, 1024, 96])
+def test_pixel_norm_silu_matches_oracle(c):
+    """Every channel count the decoder uses (and a generic one), with a voxel count that is
+    not a multiple of the voxels a warp takes."""
     torch.manual_seed(23)
-    x = (torch.randn(2, 3, 5, 6, 256, device=DEV) * 3).to(torch.bfloat16)
+    x = (torch.randn(2, 3, 5, 7, c, device=DEV) * 3).to(torch.bfloat16)
     for silu in (False, True):
         y = torch.empty_like(x)
         nat.pixel_norm(x, y, 1e-8, silu)
