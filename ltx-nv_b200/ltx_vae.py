@@ -109,6 +109,15 @@ class ResnetBlock3D(torch.nn.Module):
             self.conv_shortcut = torch.nn.Identity()
         self._packed = None
         self._gn_ws = None
+        self._gn = None
+
+    def _norm3_params(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """GroupNorm weight and bias as bf16, cached until the parameters change."""
+        w, b = self.norm3.weight, self.norm3.bias
+        key = (w.data_ptr(), w._version, b.data_ptr(), b._version)
+        if self._gn is None or self._gn[0] != key:
+            self._gn = (key, w.detach().to(torch.bfloat16).contiguous(), b.detach().to(torch.bfloat16).contiguous())
+        return self._gn[1], self._gn[2]
 
     def run(self, x: torch.Tensor, causal: bool = False) -> torch.Tensor:
         cout = self.conv1.conv.out_channels
@@ -120,8 +129,8 @@ class ResnetBlock3D(torch.nn.Module):
             g = torch.empty_like(x)
             if self._gn_ws is None or self._gn_ws.device != x.device or self._gn_ws.numel() < x.shape[0] * 256:
                 self._gn_ws = nat.group_norm1_workspace(x.shape[0], x.device)
-            nat.group_norm1(x, self.norm3.weight.detach().to(torch.bfloat16).contiguous(),
-                            self.norm3.bias.detach().to(torch.bfloat16).contiguous(), self.norm3.eps, g, self._gn_ws)
+            gw, gb = self._norm3_params()
+            nat.group_norm1(x, gw, gb, self.norm3.eps, g, self._gn_ws)
             w, b = _pack_conv(self, self.conv_shortcut, 1)
             sc = _cl_empty(x, x.shape[:-1] + (cout,))
             nat.conv3d(g, w, b, sc, 1)

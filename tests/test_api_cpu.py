@@ -59,6 +59,32 @@ def test_vae_decoder_parameter_layout_matches_reference():
                                                     "per_channel_statistics.mean-of-means"}
 
 
+def test_load_video_decoder_maps_checkpoint_keys(tmp_path):
+    """load_video_decoder reads the config from the checkpoint's metadata and takes
+    `decoder.*` (prefix removed) and `per_channel_statistics.*` keys, ignoring the rest,
+    as the reference's load_video_decoder (ltx_vae.py:225-235)."""
+    import json
+
+    from safetensors.torch import save_file
+
+    import ltx_vae
+    from oracle import vae_oracle
+
+    rec = torch.load(gc.GOLDEN / "vae_tiny_bfloat16.pt", weights_only=False)
+    sd = vae_oracle.synthetic_decoder_state_dict(rec["param_shapes"], rec["weight_seed"],
+                                                 rec["config"]["latent_channels"])
+    tensors = {(k if k.startswith("per_channel_statistics.") else "decoder." + k): v.contiguous()
+               for k, v in sd.items()}
+    tensors["encoder.conv_in.conv.weight"] = torch.zeros(4)  # other parts of the VAE file
+    path = tmp_path / "vae.safetensors"
+    save_file(tensors, str(path), metadata={"config": json.dumps({"vae": rec["config"]})})
+    dec = ltx_vae.load_video_decoder(str(path), device="cpu")
+    got = dict(dec.named_parameters()) | dict(dec.named_buffers())
+    assert set(got) == set(sd)
+    for name, t in sd.items():
+        assert torch.equal(got[name], t), name
+
+
 def test_native_wrappers_refuse_cpu_tensors():
     with pytest.raises(ValueError):
         nat.gelu_tanh(torch.zeros(8), torch.zeros(8))
