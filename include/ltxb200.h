@@ -277,6 +277,12 @@ int ltx_sp_unpack(const void* src, int64_t rows, int parts, int w, void* dst, in
  * residual is not NULL. cin a multiple of 64, cout of 8; out must not alias x. */
 int ltx_conv3d(const void* x, int B, int F, int H, int W, int cin, const void* weight, const void* bias, int cout,
                int ksize, int causal, const void* residual, void* out, void* stream);
+/* The same with norm_silu = 1: out = silu(PixelNorm_eps(round(conv + bias))) over each
+ * voxel's cout channels (ResnetBlock3D's conv1 followed by norm2 and the nonlinearity,
+ * ltx_vae.py:107-110), computed in the epilogue. Needs cout <= 256 and no residual. */
+int ltx_conv3d_norm(const void* x, int B, int F, int H, int W, int cin, const void* weight, const void* bias,
+                    int cout, int ksize, int causal, const void* residual, int norm_silu, float eps, void* out,
+                    void* stream);
 /* PixelNorm (ltx_vae.py:20-28) over the C channels of each of `rows` voxels, followed by
  * SiLU when silu != 0 (ResnetBlock3D.nonlin, ltx_vae.py:111-115; the decoder's final
  * norm + SiLU, :209-210). x may equal y. */

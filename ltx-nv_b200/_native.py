@@ -110,6 +110,9 @@ _SIGNATURES = {
                                          c_i64, ctypes.c_int, c_vp]),
     "ltx_conv3d": (ctypes.c_int, [c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_vp,
                                   c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_vp, c_vp, c_vp]),
+    "ltx_conv3d_norm": (ctypes.c_int, [c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       c_vp, c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_vp, ctypes.c_int,
+                                       ctypes.c_float, c_vp, c_vp]),
     "ltx_pixel_norm": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_int, c_vp]),
     "ltx_group_norm1_workspace_bytes": (c_i64, [ctypes.c_int]),
     "ltx_group_norm1": (ctypes.c_int, [c_vp, ctypes.c_int, c_i64, ctypes.c_int, c_vp, c_vp, ctypes.c_float, c_vp, c_i64,
@@ -446,16 +449,19 @@ def _cl5(t: torch.Tensor) -> tuple[int, int, int, int, int]:
 
 
 def conv3d(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, out: torch.Tensor, ksize: int,
-           causal: bool = False, residual: torch.Tensor | None = None) -> None:
-    """out (B, F, H, W, cout) = conv(x) + bias (+ residual); weight (cout, taps, cin)."""
+           causal: bool = False, residual: torch.Tensor | None = None, norm_silu_eps: float | None = None) -> None:
+    """out (B, F, H, W, cout) = conv(x) + bias (+ residual); weight (cout, taps, cin). With
+    norm_silu_eps, out = silu(PixelNorm(conv(x) + bias)) computed in the epilogue."""
     b, f, h, w, cin = _cl5(x)
     cout = _cl5(out)[4]
     if weight.shape != (cout, ksize ** 3, cin) or not weight.is_contiguous():
         raise ValueError(f"weight must be contiguous ({cout}, {ksize ** 3}, {cin}), got {tuple(weight.shape)}")
     if residual is not None and residual.shape != out.shape:
         raise ValueError("residual must have the output's shape")
-    _call("ltx_conv3d", _ptr(x), b, f, h, w, cin, _ptr(weight), _ptr(bias), cout, ksize, int(causal),
-          _ptr(residual), _ptr(out), _stream(x), label=f"conv3d k{ksize} {cin}->{cout} {b}x{f}x{h}x{w}"
+    fused = norm_silu_eps is not None
+    _call("ltx_conv3d_norm", _ptr(x), b, f, h, w, cin, _ptr(weight), _ptr(bias), cout, ksize, int(causal),
+          _ptr(residual), int(fused), float(norm_silu_eps) if fused else 0.0, _ptr(out), _stream(x),
+          label=f"conv3d k{ksize} {cin}->{cout} {b}x{f}x{h}x{w}{' +norm' if fused else ''}"
           if _profile is not None else None)
 
 

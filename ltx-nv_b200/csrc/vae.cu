@@ -21,6 +21,8 @@ struct ConvShape {
   int bf;       // B * F frames
   int hb, wb;   // spatial block of one M tile: hb rows x wb columns of one frame, hb * wb = 128 * MH
   int th, tw;   // blocks per frame: ceil(H / hb) x ceil(W / wb)
+  int norm_silu;  // 1: write silu(PixelNorm(conv + bias)) (all Cout channels in one tile)
+  float eps;      // PixelNorm eps
 };
 
 // MH = 128-row halves of an M tile: 2 for BN <= 128 (256 voxels share each weight block,
@@ -165,12 +167,55 @@ __global__ void __launch_bounds__(192, 1)
       const bool live = hh < cs.H && ww < cs.W;
       const int64_t m = (int64_t(bf) * cs.H + hh) * cs.W + ww;
       const uint32_t tbase = tmem_base + uint32_t((acc * MH + h) * BN) + (uint32_t(q * 32) << 16);
+      // PixelNorm of the voxel's Cout outputs (ltx_vae.py:20-28, then SiLU): a first pass
+      // over the accumulator sums round(v^2) of v = round(conv + bias), as the reference's
+      // x**2 and mean over the stored output do.
+      float rden = 0.f;
+      if (cs.norm_silu) {
+        float ss = 0.f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN && c0 < cs.cout; c0 += 32) {
+          uint32_t rr[32];
+          tmem_ld32(tbase + uint32_t(c0), rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int col = c0 + g * 8;
+            if (col < cs.cout) {
+              float bb[8];
+              ld8<__nv_bfloat16>(bias + col, bb);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float v = round_bf16(__uint_as_float(rr[g * 8 + e]) + bb[e]);
+                ss += round_bf16(v * v);
+              }
+            }
+          }
+        }
+        const float mean = round_bf16(ss / float(cs.cout));
+        rden = 1.f / round_bf16(sqrtf(round_bf16(mean + cs.eps)));
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < BN && n0 + c0 < cs.cout; c0 += 32) {
         uint32_t rr[32];
         tmem_ld32(tbase + uint32_t(c0), rr);
         tmem_wait_ld();
-        if (live) {
+        if (live && cs.norm_silu) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int col = c0 + g * 8;
+            if (col < cs.cout) {
+              float v[8], bb[8];
+              ld8<__nv_bfloat16>(bias + col, bb);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float a = round_bf16(round_bf16(__uint_as_float(rr[g * 8 + e]) + bb[e]) * rden);
+                v[e] = __fdividef(a, 1.f + __expf(-a));
+              }
+              st8<__nv_bfloat16>(out + m * cs.cout + col, v);
+            }
+          }
+        } else if (live) {
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             const int col = n0 + c0 + g * 8;
@@ -509,6 +554,12 @@ static void check16(const void* p, const char* what) {
 
 extern "C" int ltx_conv3d(const void* x, int B, int F, int H, int W, int cin, const void* weight, const void* bias,
                           int cout, int ksize, int causal, const void* residual, void* out, void* stream) {
+  return ltx_conv3d_norm(x, B, F, H, W, cin, weight, bias, cout, ksize, causal, residual, 0, 0.f, out, stream);
+}
+
+extern "C" int ltx_conv3d_norm(const void* x, int B, int F, int H, int W, int cin, const void* weight,
+                               const void* bias, int cout, int ksize, int causal, const void* residual,
+                               int norm_silu, float eps, void* out, void* stream) {
   LTX_API_BEGIN
   LTX_REQUIRE(x && weight && bias && out, "x, weight, bias and out must be non-NULL");
   LTX_REQUIRE(ksize == 1 || ksize == 3, "ksize must be 1 or 3");
@@ -532,6 +583,10 @@ extern "C" int ltx_conv3d(const void* x, int B, int F, int H, int W, int cin, co
   cs.taps = ksize == 3 ? 27 : 1;
   cs.t_off = causal ? -2 : -1;
   cs.bf = B * F;
+  cs.norm_silu = norm_silu ? 1 : 0;
+  cs.eps = eps;
+  LTX_REQUIRE(!norm_silu || (cout <= 256 && residual == nullptr),
+              "the fused PixelNorm needs cout <= 256 (one tile per voxel row) and no residual");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cout <= 64)
     launch_conv<64, 2>(x, B, weight, bias, residual, out, cs, s);

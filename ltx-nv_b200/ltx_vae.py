@@ -63,11 +63,11 @@ class CausalConv3d(torch.nn.Module):
         return _pack_conv(self, self.conv, 27)
 
     def run(self, x: torch.Tensor, causal: bool = False, residual: torch.Tensor | None = None,
-            out: torch.Tensor | None = None) -> torch.Tensor:
+            out: torch.Tensor | None = None, norm_silu_eps: float | None = None) -> torch.Tensor:
         w, b = self.packed()
         if out is None:
             out = _cl_empty(x, x.shape[:-1] + (w.shape[0],))
-        nat.conv3d(x, w, b, out, 3, causal, residual)
+        nat.conv3d(x, w, b, out, 3, causal, residual, norm_silu_eps)
         return out
 
 
@@ -123,8 +123,12 @@ class ResnetBlock3D(torch.nn.Module):
         cout = self.conv1.conv.out_channels
         h = torch.empty_like(x)
         self.norm1.run(x, h, silu=True)
-        h2 = self.conv1.run(h, causal)
-        self.norm2.run(h2, h2, silu=True)
+        if cout <= 256:
+            # norm2 + SiLU in conv1's epilogue (the tile holds all cout channels of a voxel)
+            h2 = self.conv1.run(h, causal, norm_silu_eps=self.norm2.eps)
+        else:
+            h2 = self.conv1.run(h, causal)
+            self.norm2.run(h2, h2, silu=True)
         if isinstance(self.conv_shortcut, torch.nn.Conv3d):
             g = torch.empty_like(x)
             if self._gn_ws is None or self._gn_ws.device != x.device or self._gn_ws.numel() < x.shape[0] * 256:

@@ -58,6 +58,27 @@ def test_conv3d_matches_float32(b, f, h, w, cin, cout, k, causal, res):
     assert rel_l2(out, ref) < 4e-3
 
 
+@pytest.mark.parametrize("cout", [64, 128, 256])
+def test_conv3d_fused_pixel_norm_matches_unfused(cout):
+    """conv + bias, then PixelNorm + SiLU in the epilogue == the conv followed by
+    ltx_pixel_norm (up to the channel-sum order of the mean)."""
+    torch.manual_seed(27)
+    x = torch.randn(1, 3, 6, 20, 128, device=DEV).to(torch.bfloat16)
+    wt = (torch.randn(cout, 27, 128, device=DEV) * (27 * 128) ** -0.5).to(torch.bfloat16)
+    bias = (0.1 * torch.randn(cout, device=DEV)).to(torch.bfloat16)
+    fused = torch.empty(1, 3, 6, 20, cout, device=DEV, dtype=torch.bfloat16)
+    nat.conv3d(x, wt, bias, fused, 3, norm_silu_eps=1e-8)
+    plain = torch.empty_like(fused)
+    nat.conv3d(x, wt, bias, plain, 3)
+    nat.pixel_norm(plain, plain, 1e-8, True)
+    torch.cuda.synchronize()
+    assert nat.device_error_flags() == 0
+    assert rel_l2(fused, plain) < 2e-3
+    assert (fused.float() - plain.float()).abs().max() <= 2 ** -6 * plain.float().abs().max()
+    with pytest.raises(nat.LtxError):
+        nat.conv3d(x, wt, bias, fused, 3, residual=fused, norm_silu_eps=1e-8)
+
+
 def test_conv3d_residual_in_place_and_errors():
     torch.manual_seed(22)
     x = torch.randn(1, 2, 4, 4, 64, device=DEV).to(torch.bfloat16)
