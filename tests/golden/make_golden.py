@@ -6,7 +6,7 @@ configurations and records inputs and outputs. The fixtures pin the CPU oracle
 (oracle/ltx_oracle.py, oracle/philox_oracle.c); the GPU parity tests then compare the
 sm_100a kernels with that oracle. The reference is not needed at test time.
 
-    python tests/golden/make_golden.py [--reference /path/to/lipaul/ltx-nv]
+    python tests/golden/make_golden.py --reference /path/to/lipaul/ltx-nv [--only KIND]
 
 Fixtures written:
   philox_m1.npz       the reference's own golden noise (cuda_c_standalone/artifacts/
@@ -24,6 +24,8 @@ Fixtures written:
                       load_transformer maps it (tiny AV model), with parameter shapes.
   guided_tiny_av_<dtype>.pt  two steps of guided_denoise_step (cond / uncond / STG /
                       modality passes, rescale) + Euler on the tiny AV model.
+  vae_tiny_<dtype>.pt the video VAE decoder (ConvVideoDecoder) with every block kind on
+                      a seeded (2, 128, 3, 4, 6) latent (oracle/vae_oracle.py weights).
 
 Weights are N(0, 0.02) from numpy's PCG64 (platform independent) in the reference's
 named_parameters() order, q/k RMSNorm gains offset by +1 (oracle.synthetic_state_dict).
@@ -34,6 +36,7 @@ from __future__ import annotations
 import argparse
 import dataclasses
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -356,7 +359,8 @@ def make_vae(ref_root: Path, dtype):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("LTX_NV_REFERENCE"), required="LTX_NV_REFERENCE" not in os.environ,
+                    help="checkout of lipaul/ltx-nv (default: $LTX_NV_REFERENCE)")
     ap.add_argument("--only", choices=["guide", "guided", "ckpt", "connector", "vae"], default=None,
                     help="regenerate one fixture only")
     args = ap.parse_args()
