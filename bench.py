@@ -459,6 +459,32 @@ def vae_conv_flops(dec, latent_shape) -> float:
     return total + conv(dec.conv_out.conv, vox)
 
 
+def vae_cpu_sample(decode_flops: float) -> dict:
+    """The decoder's CPU restatement (oracle/vae_oracle.py, the reference's PyTorch ops) on
+    the host cores: one output frame of the last-stage 3x3x3 convolution (128 -> 128
+    channels, 128x192 voxels, bf16), the decode time extrapolated by FLOPs."""
+    from oracle import vae_oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, 128, 1, 128, 192, generator=g).to(torch.bfloat16)
+    w = (torch.randn(128, 128, 3, 3, 3, generator=g) * (27 * 128) ** -0.5).to(torch.bfloat16)
+    b = torch.zeros(128, dtype=torch.bfloat16)
+    vae_oracle.conv3d_same(x, w, b)  # warm-up
+    times = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        vae_oracle.conv3d_same(x, w, b)
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    fl = 2.0 * 128 * 192 * 27 * 128 * 128
+    return {"value": decode_flops / (fl / sec) * 1e3, "unit": "ms per decode (extrapolated)", "cores": threads,
+            "kind": "port", "sample": f"one output frame of the last-stage 128->128 3x3x3 convolution "
+                                      f"({fl / 1e9:.1f} GFLOP) on the CPU oracle, median of 5: {sec:.3f} s, "
+                                      f"{fl / sec / 1e12:.3f} TFLOP/s, scaled to the decode's convolution FLOPs"}
+
+
 def run_probe(args, dev: torch.device) -> dict:
     """Launch one kernel of the step at its config-3 shape W + K times and time the K
     launches with CUDA events (the small, single-kernel case for ncu captures)."""
@@ -569,6 +595,8 @@ def run_probe(args, dev: torch.device) -> dict:
     peaks = load_peaks()
     res = {"probe": args.probe, "what": PROBES[args.probe], "avg_launch_ms": ms, "launches": args.steps,
            "algorithmic_bytes": nbytes, "achieved_GBps": nbytes / (ms / 1e3) / 1e9}
+    if args.probe == "vae":
+        res["cpu_baseline"] = vae_cpu_sample(flops)
     if flops:
         res.update({"flops": flops, "achieved_TFLOPs": flops / (ms / 1e3) / 1e12,
                     "frac_of_measured_burst": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"]})
