@@ -479,6 +479,51 @@ __global__ void __launch_bounds__(256) depth_to_space_kernel(const __nv_bfloat16
   }
 }
 
+// The same rearrange read per input voxel: thread (voxel, g) loads the 8 * P contiguous
+// input channels of output channels 8g..8g+7 (P = p1 * p2 * p3 subpositions, P 16-byte
+// loads), transposes them in registers and stores 8 channels to each of the P output
+// voxels (one 16-byte store each; 16-byte aligned output, c a multiple of 8).
+template <int P>
+__global__ void __launch_bounds__(256) depth_to_space_vox_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                 __nv_bfloat16* __restrict__ y, int B, int F, int H,
+                                                                 int W, int c, int p1, int p2, int p3, int drop) {
+  const int Fo = F * p1 - drop, Ho = H * p2, Wo = W * p3;
+  const int cg = c / 8;
+  const int64_t total = int64_t(B) * F * H * W * cg;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int g = int(i % cg);
+    const int64_t vox = i / cg;  // ((b * F + d) * H + h) * W + w
+    const int w = int(vox % W);
+    int64_t t = vox / W;
+    const int h = int(t % H);
+    t /= H;
+    const int d = int(t % F);
+    const int b = int(t / F);
+    // in[e * P + s] = channel (8g + e) * P + s of the voxel: P chunks of 16 bytes
+    uint32_t in[4 * P];
+    const uint4* src = reinterpret_cast<const uint4*>(x + vox * (int64_t(c) * P) + int64_t(g) * 8 * P);
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const uint4 u = src[k];
+      in[4 * k] = u.x;
+      in[4 * k + 1] = u.y;
+      in[4 * k + 2] = u.z;
+      in[4 * k + 3] = u.w;
+    }
+    const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(in);
+#pragma unroll
+    for (int sidx = 0; sidx < P; ++sidx) {
+      const int ii = sidx / (p2 * p3), jj = (sidx / p3) % p2, kk = sidx % p3;
+      const int fo = d * p1 + ii - drop;
+      if (fo < 0) continue;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __bfloat162float(hv[e * P + sidx]);
+      st8<__nv_bfloat16>(y + (((int64_t(b) * Fo + fo) * Ho + h * p2 + jj) * Wo + w * p3 + kk) * c + g * 8, v);
+    }
+  }
+}
+
 // PerChannelStatistics.un_normalize (ltx_vae.py:83-87) and the NCDHW -> channels-last
 // transpose of the latent: y[b,f,h,w,c] = round(round(x[b,c,f,h,w] * std[c]) + mean[c]), std
 // and mean rounded to bf16 first (the reference's .to(x)).
@@ -686,9 +731,24 @@ extern "C" int ltx_depth_to_space(const void* x, int B, int F, int H, int W, int
   LTX_REQUIRE(drop_first == 0 || (drop_first == 1 && F * p1 > 1), "drop_first must be 0 or 1");
   check16(y, "y");
   const int64_t work = int64_t(B) * (int64_t(F) * p1 - drop_first) * H * p2 * W * p3 * (c / 8);
-  depth_to_space_kernel<<<ew_grid(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), B, F, H, W, c, p1, p2, p3, drop_first),
-      note_launch();
+  const int P = p1 * p2 * p3;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto xp = static_cast<const __nv_bfloat16*>(x);
+  auto yp = static_cast<__nv_bfloat16*>(y);
+  const bool vec = reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  const int64_t vwork = int64_t(B) * F * H * W * (c / 8);
+  if (vec && P == 8)
+    depth_to_space_vox_kernel<8><<<ew_grid(vwork), 256, 0, s>>>(xp, yp, B, F, H, W, c, p1, p2, p3, drop_first),
+        note_launch();
+  else if (vec && P == 4)
+    depth_to_space_vox_kernel<4><<<ew_grid(vwork), 256, 0, s>>>(xp, yp, B, F, H, W, c, p1, p2, p3, drop_first),
+        note_launch();
+  else if (vec && P == 2)
+    depth_to_space_vox_kernel<2><<<ew_grid(vwork), 256, 0, s>>>(xp, yp, B, F, H, W, c, p1, p2, p3, drop_first),
+        note_launch();
+  else
+    depth_to_space_kernel<<<ew_grid(work), 256, 0, s>>>(xp, yp, B, F, H, W, c, p1, p2, p3, drop_first),
+        note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
