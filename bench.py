@@ -18,7 +18,8 @@ Prints one JSON line on rank 0.
   roofline  the dominant kernel (by time share) of an instrumented step, CUDA events
             on the launching stream, against MEASURED_PEAKS.json.
   cpu_baseline  the CPU oracle (the reference's PyTorch math restated) on this box's
-            host cores for a bounded sample (one of the 28 blocks), scaled to a step.
+            host cores: one whole 28-block CFG step (the --impl reference arm times as
+            many whole steps as fit in 90 s).
 N > 1: the same single step split over the N GPUs (strong scaling): CFG cond/uncond on
 two GPU groups x Ulysses sequence parallelism over the video tokens inside each group
 (ltx_parallel.ParallelDenoiser, NCCL all-to-all / all-gather over NVLink).
@@ -48,14 +49,31 @@ CFG3 = dict(num_layers=28, heads=32, head_dim=64, cross_dim=4096, f=16, h=16, w=
             sigma_next=0.25, cfg_scale=3.0)
 
 
-def step_flops(c=CFG3, batch=2) -> float:
-    """Algorithmic FLOPs of one CFG step (adaLN counted once per sample)."""
+def step_flops(c=CFG3, batch=2, text_kv_cached=True) -> float:
+    """Algorithmic FLOPs of one CFG step (adaLN counted once per sample). The text-context
+    K/V projection (4*S*C*D per block and sample) depends only on the constant context
+    and weights; the step caches it across denoise steps, so with text_kv_cached it is not
+    counted (0.4 % of the step at config 3)."""
     t = c["f"] * c["h"] * c["w"]
     d = c["heads"] * c["head_dim"]
     f, s, cc, h = 4 * d, c["text"], c["cross_dim"], c["heads"]
-    per_block = 8 * t * d * d + 4 * t * t * d + 4 * t * d * d + 4 * s * cc * d + 4 * t * s * d + 4 * t * d * f \
-        + 4 * t * d * h
+    per_block = 8 * t * d * d + 4 * t * t * d + 4 * t * d * d + 4 * t * s * d + 4 * t * d * f + 4 * t * d * h
+    if not text_kv_cached:
+        per_block += 4 * s * cc * d
     return float((per_block * c["num_layers"] + 4 * t * d * 128) * batch)
+
+
+def workload_config(c=CFG3) -> dict:
+    """The `config` object of both arms' JSON lines (the workload only, so the two arms'
+    objects are equal; how it ran goes in `execution`)."""
+    t = c["f"] * c["h"] * c["w"]
+    return {"workload": "BASELINE config 3: full-size video DiT CFG denoise step",
+            "model": f"LTX-2.5 video DiT {c['num_layers']} blocks, hidden {c['heads'] * c['head_dim']}, "
+                     f"{c['heads']}x{c['head_dim']} heads, FFN {4 * c['heads'] * c['head_dim']} (random-init "
+                     "N(0,0.02))",
+            "global_batch": 2, "latent_tokens": t, "seq_len": t, "text_tokens": c["text"],
+            "sigma": c["sigma"], "sigma_next": c["sigma_next"], "cfg_scale": c["cfg_scale"],
+            "l2": "inputs larger than L2 (4.2 GB weights, ~1 GB activations per step)"}
 
 
 def load_peaks() -> dict:
@@ -287,12 +305,11 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "BASELINE config 3: full-size video DiT CFG denoise step", "model": "LTX-2.5 video DiT "
-                   "28 blocks, hidden 2048, 32x64 heads, FFN 8192 (random-init N(0,0.02))", "global_batch": 2,
-                   "latent_tokens": t, "seq_len": t, "text_tokens": CFG3["text"],
-                   "parallelism": "single GPU" if world == 1 else f"cfg{layout.cfg} x sp{layout.sp} (Ulysses, NCCL)",
-                   "l2": "inputs larger than L2 (4.2 GB weights, ~1 GB activations per step)",
-                   "cuda_graph": used_graph},
+        "config": workload_config(),
+        "execution": {"parallelism": "single GPU" if world == 1 else
+                      f"cfg{layout.cfg} x sp{layout.sp} (Ulysses, NCCL)", "cuda_graph": used_graph,
+                      "step_flops": flops, "text_kv": "projected once, cached across denoise steps (the context "
+                      "is constant); not counted in step_flops"},
         "steps_per_s": 1e3 / ms_per_step, "step_tflops_per_gpu": tflops / world,
         "pct_bf16_peak": tflops / world / peaks["bf16_tflops"], "pct_bf16_peak_sustained": tflops / world / peak,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 2,
@@ -334,73 +351,88 @@ def profile_traffic(label: str) -> float | None:
 # ---------------------------------------------------------------------------------------
 
 
-def cpu_block_sample(threads: int) -> dict:
-    """Time one of config 3's 28 blocks (B=2, T=6144, bf16) of the CPU oracle and scale
-    it to a full step (x28; patchify/adaLN/head are <1% of the FLOPs and are left out)."""
-    from types import SimpleNamespace
+def cpu_reference_setup(threads: int, num_layers: int | None = None):
+    """Config-3 weights (bf16, N(0, 0.02), q/k RMSNorm gains +1, in the reference's
+    parameter order) and inputs on the host for the CPU oracle."""
+    import ltx_dit
 
     from oracle import ltx_oracle
 
     torch.set_num_threads(threads)
     c = CFG3
+    cfg = ltx_dit.DiTConfig.video_only(num_layers=num_layers or c["num_layers"], heads=c["heads"],
+                                       head_dim=c["head_dim"], cross_dim=c["cross_dim"])
+    with torch.device("meta"):
+        shapes = [(n, tuple(p.shape)) for n, p in ltx_dit.LTXModel(cfg).named_parameters()]
+    g = torch.Generator().manual_seed(1)
+    w = {}
+    for name, shape in shapes:
+        t = torch.randn(shape, generator=g, dtype=torch.bfloat16).mul_(0.02)
+        if name.endswith(("q_norm.weight", "k_norm.weight")):
+            t.add_(1.0)
+        w[name] = t
     t = c["f"] * c["h"] * c["w"]
-    d = c["heads"] * c["head_dim"]
-    cfg = SimpleNamespace(num_layers=1, video_heads=c["heads"], video_head_dim=c["head_dim"], video_cross_dim=4096,
-                          norm_eps=1e-6, gated_attention=True, cross_attention_adaln=False, audio_heads=2,
-                          audio_head_dim=32)
-    shapes = []
-    for blk in ("attn1", "attn2"):
-        cin = d if blk == "attn1" else c["cross_dim"]
-        shapes += [(f"blocks.0.{blk}.q_norm.weight", (d,)), (f"blocks.0.{blk}.k_norm.weight", (d,)),
-                   (f"blocks.0.{blk}.to_q.weight", (d, d)), (f"blocks.0.{blk}.to_q.bias", (d,)),
-                   (f"blocks.0.{blk}.to_k.weight", (d, cin)), (f"blocks.0.{blk}.to_k.bias", (d,)),
-                   (f"blocks.0.{blk}.to_v.weight", (d, cin)), (f"blocks.0.{blk}.to_v.bias", (d,)),
-                   (f"blocks.0.{blk}.to_gate_logits.weight", (c["heads"], d)),
-                   (f"blocks.0.{blk}.to_gate_logits.bias", (c["heads"],)),
-                   (f"blocks.0.{blk}.to_out.weight", (d, d)), (f"blocks.0.{blk}.to_out.bias", (d,))]
-    shapes += [("blocks.0.ff.proj_in.weight", (4 * d, d)), ("blocks.0.ff.proj_out.weight", (d, 4 * d)),
-               ("blocks.0.scale_shift_table", (6, d))]
-    w = ltx_oracle.synthetic_state_dict(shapes, 1, dtype=torch.bfloat16)
-    g = torch.Generator().manual_seed(3)
-    x = torch.randn(2, t, d, generator=g).to(torch.bfloat16)
+    latent = torch.randn(1, t, 128, generator=g).to(torch.bfloat16)
     ctx = torch.randn(2, c["text"], c["cross_dim"], generator=g).to(torch.bfloat16)
-    mod = (torch.randn(2, 1, 6 * d, generator=g) * 0.1).to(torch.bfloat16)
-    pos = ltx_oracle.video_positions(2, c["f"], c["h"], c["w"], 24.0)
-    pe = ltx_oracle.rope_tables(pos, d, torch.bfloat16, 10000.0, [20, 2048, 2048], c["heads"])
-    va = ltx_oracle.StreamArgs(x=x, context=ctx, mod=mod, embedded=None, pe=pe, cross_pe=None, cross_ss=None,
-                               cross_gate=None, prompt_mod=None, enabled=True)
+    pos = ltx_oracle.video_positions(1, c["f"], c["h"], c["w"], 24.0)
+    kf = torch.zeros(1, t, 1)
+    kf[:, : c["h"] * c["w"]] = 1.0
+    sigmas = torch.tensor([c["sigma"], c["sigma_next"]])
+    return cfg, w, (latent, pos, ctx[:1], ctx[1:], sigmas, kf)
+
+
+def cpu_oracle_step(cfg, w, inputs) -> float:
+    """One CFG denoise step (patchify, adaLN, every block, head, X0, CFG, Euler) of the
+    CPU oracle; returns its wall time in seconds."""
+    from oracle import ltx_oracle
+
+    latent, pos, cpos, cneg, sigmas, kf = inputs
     t0 = time.perf_counter()
     with torch.inference_mode():
-        ltx_oracle.block(w, cfg, 0, va, None)
-    sec = time.perf_counter() - t0
-    step_sec = sec * c["num_layers"]
-    return {"value": 2 * t / step_sec, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"1 of 28 blocks of one config-3 CFG step (B=2, T={t}, bf16) on the CPU oracle, "
-                      f"{sec:.2f} s, scaled x28 (steps/s {1 / step_sec:.5f})",
-            "block_sec": sec}
+        ltx_oracle.cfg_denoise_step(w, cfg, latent, pos, cpos, cneg, sigmas, 0, CFG3["cfg_scale"], keyframes_mask=kf)
+    return time.perf_counter() - t0
+
+
+def cpu_full_steps(threads: int, warmup: int, steps: int, budget_s: float) -> dict:
+    """The CPU oracle (the reference's PyTorch math, restated op for op) running whole
+    config-3 CFG steps on `threads` host cores. Warm-up: `warmup` one-block samples
+    (untimed; they start the thread pool and the allocator). Timed: whole 28-block steps,
+    as many of the `steps` requested as fit in `budget_s` seconds by the warm-up's
+    estimate (at least one)."""
+    from dataclasses import replace
+
+    cfg, w, inputs = cpu_reference_setup(threads)
+    one_block = replace(cfg, num_layers=1)
+    est = None
+    for _ in range(max(1, warmup)):
+        est = cpu_oracle_step(one_block, w, inputs) * cfg.num_layers
+    n = int(max(1, min(steps, budget_s // max(est, 1e-3))))
+    times = [cpu_oracle_step(cfg, w, inputs) for _ in range(n)]
+    sec = sum(times) / n
+    t = CFG3["f"] * CFG3["h"] * CFG3["w"]
+    return {"value": 2 * t / sec, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} whole config-3 CFG step(s) ({cfg.num_layers} blocks, B=2, T={t}, bf16) of the CPU oracle, "
+                      f"{sec:.2f} s each (steps/s {1 / sec:.5f}); warm-up {max(1, warmup)} one-block sample(s)",
+            "steps_timed": n, "step_s": sec, "timed_s": sum(times)}
 
 
 def run_reference(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    vals = []
-    if args.warmup > 0:
-        cpu_block_sample(threads)  # one untimed sample warms the thread pool and caches
-    samples = []
-    for _ in range(max(1, args.steps)):
-        s = cpu_block_sample(threads)
-        samples.append(s)
-        vals.append(s["value"])
-    v = statistics.median(vals)
-    cpu = dict(samples[0])
-    cpu["value"] = v
-    cpu.pop("block_sec", None)
-    return {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 2 * CFG3["f"] * CFG3["h"] * CFG3["w"] / v * 1e3,
+    cpu = cpu_full_steps(threads, args.warmup, args.steps, budget_s=90.0)
+    n, sec = cpu.pop("steps_timed"), cpu.pop("step_s")
+    cpu.pop("timed_s")
+    v = cpu["value"]
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": n,
+            "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE config 3: full-size video DiT CFG denoise step", "latent_tokens":
-                       CFG3["f"] * CFG3["h"] * CFG3["w"], "global_batch": 2, "parallelism": "CPU, host cores"},
+            "config": workload_config(),
+            "execution": {"parallelism": f"CPU, {threads} host threads (rank 0 only)", "cuda_graph": False,
+                          "step_flops": step_flops(text_kv_cached=False),
+                          "text_kv": "recomputed every step, as the reference does",
+                          "note": "steps = whole steps timed (as many of the requested ones as fit in 90 s); "
+                                  "warm-up = one-block samples"},
             "cpu_baseline": cpu, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -418,6 +450,9 @@ PROBES = {
     "vae": "video VAE decoder (ConvVideoDecoder), latent (1, 128, 9, 16, 24) -> 65 frames of 512x768, assumed "
            "block layout base 128, [res_x 5, compress_all 2] x 3 + res_x 5 (random weights), bf16",
     "conv3d": "one 3x3x3 decoder convolution at the last stage: 128 -> 128 channels over 65x128x192 voxels",
+    "gpu_bar": "the reference's GPU libraries at the step's shapes on the same B200: torch SDPA (cuDNN and "
+               "flash backends, the reference's cuDNN-first sdpa) against our attention at config 3 (d=64) and "
+               "config 4 (d=128), and cuBLAS (F.linear) against our GEMMs at the five config-3 GEMM shapes",
 }
 
 # Assumed production layout of the video decoder (the real one is read from the
@@ -483,6 +518,88 @@ def vae_cpu_sample(decode_flops: float) -> dict:
             "kind": "port", "sample": f"one output frame of the last-stage 128->128 3x3x3 convolution "
                                       f"({fl / 1e9:.1f} GFLOP) on the CPU oracle, median of 5: {sec:.3f} s, "
                                       f"{fl / sec / 1e12:.3f} TFLOP/s, scaled to the decode's convolution FLOPs"}
+
+
+def _time_ms(fn, warmup: int, steps: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_gpu_bar(args, dev: torch.device) -> dict:
+    """Per-op comparison with the libraries the reference calls on a GPU (its sdpa tries
+    cuDNN first, ltx_nn.py:15,22-26; its projections are nn.Linear, ltx_nn.py:188-192,
+    244-245), same shapes, same process, CUDA events. Our GEMM rows use the plain bias
+    epilogue (the step fuses more into some of them)."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    import _native as nat
+
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+    w_, k_ = max(args.warmup, 3), max(args.steps, 10)
+    peaks = load_peaks()
+    rows = {}
+    t = CFG3["f"] * CFG3["h"] * CFG3["w"]
+    for name, heads, hd in (("attention cfg3 B=2 H=32 T=6144 d=64", 32, 64),
+                            ("attention cfg4 B=2 H=32 T=6144 d=128", 32, 128)):
+        d = heads * hd
+        qkv = rnd(2 * t, 3 * d + heads)
+        o = torch.empty(2 * t, d, device=dev, dtype=torch.bfloat16)
+        flops = 4.0 * 2 * heads * t * t * hd
+        ours = _time_ms(lambda: nat.attention(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:3 * d], o, 2, t, t, heads,
+                                              hd, hd ** -0.5, qkv[:, 3 * d:]), w_, k_)
+        ours_ng = _time_ms(lambda: nat.attention(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:3 * d], o, 2, t, t,
+                                                 heads, hd, hd ** -0.5, None), w_, k_)
+        # the reference's layout: (B, T, H, d) views transposed to (B, H, T, d)
+        q4 = qkv[:, :d].reshape(2, t, heads, hd).transpose(1, 2)
+        k4 = qkv[:, d:2 * d].reshape(2, t, heads, hd).transpose(1, 2)
+        v4 = qkv[:, 2 * d:3 * d].reshape(2, t, heads, hd).transpose(1, 2)
+        row = {"flops": flops, "ours_ms": ours, "ours_no_gate_ms": ours_ng}
+        for bname, be in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION)):
+            try:
+                with sdpa_kernel([be]):
+                    row[f"torch_{bname}_ms"] = _time_ms(lambda: F.scaled_dot_product_attention(q4, k4, v4), w_, k_)
+            except RuntimeError as e:  # backend not available for this shape / build
+                row[f"torch_{bname}_ms"] = None
+                row[f"torch_{bname}_error"] = str(e).splitlines()[0][:160]
+        rows[name] = row
+    d = CFG3["heads"] * CFG3["head_dim"]
+    m = 2 * t
+    for name, n, k in (("qkv+gate", 3 * d + CFG3["heads"], d), ("attn out / text out", d, d),
+                       ("text q+gate", d + CFG3["heads"], d), ("ffn in", 4 * d, d), ("ffn out", d, 4 * d)):
+        a, wt, bias = rnd(m, k), rnd(n, k, scale=k ** -0.5), rnd(n)
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        epi = nat.epilogue(bias=bias)
+        npad = (n + 7) // 8 * 8
+        wp = torch.zeros(npad, k, device=dev, dtype=torch.bfloat16)
+        wp[:n] = wt
+        bp = torch.zeros(npad, device=dev, dtype=torch.bfloat16)
+        bp[:n] = bias
+        outp = torch.empty(m, npad, device=dev, dtype=torch.bfloat16)
+        ours = _time_ms(lambda: nat.linear(a, wp, outp, nat.epilogue(bias=bp)), w_, k_) if npad != n else \
+            _time_ms(lambda: nat.linear(a, wt, out, epi), w_, k_)
+        cub = _time_ms(lambda: F.linear(a, wt, bias), w_, k_)
+        rows[f"gemm {name} M={m} N={n} K={k}"] = {"flops": 2.0 * m * n * k, "ours_ms": ours, "torch_cublas_ms": cub}
+    for r in rows.values():
+        for key in list(r):
+            if key.endswith("_ms") and r[key]:
+                r[key.replace("_ms", "_TFLOPs")] = r["flops"] / (r[key] / 1e3) / 1e12
+        lib = [v for kk, v in r.items() if kk.startswith("torch_") and kk.endswith("_ms") and v]
+        r["best_library_over_ours"] = min(lib) / r["ours_ms"] if lib else None
+    return {"probe": "gpu_bar", "what": PROBES["gpu_bar"], "peak_bf16_tflops": peaks["bf16_tflops"],
+            "torch": torch.__version__, "cudnn": torch.backends.cudnn.version(), "ops": rows}
 
 
 def run_probe(args, dev: torch.device) -> dict:
@@ -628,6 +745,9 @@ def main():
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.probe == "gpu_bar":
+        print(json.dumps(run_gpu_bar(args, dev)), flush=True)
+        return
     if args.probe:
         print(json.dumps(run_probe(args, dev)), flush=True)
         return
@@ -643,8 +763,9 @@ def main():
     try:
         line = run_ours(args, rank, world, dev)
         if line is not None and not args.no_cpu_baseline:
-            cb = cpu_block_sample(os.cpu_count() or 1)
-            cb.pop("block_sec", None)
+            cb = cpu_full_steps(os.cpu_count() or 1, warmup=1, steps=1, budget_s=0.0)
+            for k in ("steps_timed", "step_s", "timed_s"):
+                cb.pop(k)
             line["cpu_baseline"] = cb
         if line is not None:
             json_out.write(json.dumps(line) + "\n")

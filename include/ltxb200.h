@@ -166,10 +166,6 @@ typedef struct {
 
 int ltx_linear(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, int64_t ldc, int64_t M, int64_t N,
                int64_t K, const ltx_epilogue* epi, int dtype, void* stream);
-/* Tuning knob (process-wide): force single-CTA tcgen05 tiles of 128 or 256 columns, or 0
- * for the automatic choice (256-column tiles computed by CTA pairs when N >= 512 and
- * M >= 256). No counterpart in the reference (cuBLASLt picks its own). */
-int ltx_gemm_set_tile_n(int bn);
 
 /* ---------------------------------------------------------------------------------- */
 /* Attention: softmax(Q K^T * scale) V per (sample, head), non-causal, no mask, with   */
@@ -223,8 +219,10 @@ int ltx_guide_rescale(const void* cond, const void* uncond, const void* ptb, con
  * 786,432) and rejects larger n with an error. The scratch's completion counter starts
  * at zero at module load and every call leaves it zero. One scratch per device: calls
  * that overlap in time on the same device (several streams or threads) race on it. The
- * first call on a device looks up the scratch's address (cudaGetSymbolAddress); make
- * that first call before any stream capture. No counterpart in the reference. */
+ * first call on a device looks up the scratch's address (cudaGetSymbolAddress, once per
+ * device and thread-safe); make that first call before any stream capture. The address
+ * is kept for the life of the process, so after a cudaDeviceReset of a device this entry
+ * point must not be called on it again. No counterpart in the reference. */
 int ltx_guide_rescale_noalloc(const void* cond, const void* uncond, const void* ptb, const void* mod, int64_t n,
                               float cfg_scale, float stg_scale, float modality_scale, float rescale_scale, void* out,
                               int dtype, void* stream);

@@ -375,8 +375,8 @@ def linear(a: torch.Tensor, w: torch.Tensor, c: torch.Tensor, epi: Epilogue | No
 
 
 def gemm_set_tile_n(bn: int) -> None:
+    """Test hook (include/ltxb200_testing.h): force the calling thread's GEMM tile width."""
     _call("ltx_gemm_set_tile_n", bn)
-
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, batch: int, tq: int, tk: int,
@@ -408,8 +408,21 @@ def sp_unpack(src: torch.Tensor, parts: int, dst: torch.Tensor) -> None:
     _call("ltx_sp_unpack", _ptr(src), rows, parts, w, _ptr(dst), _ld(dst), _dt(src), _stream(src))
 
 
+def _same_elementwise(*ts: torch.Tensor) -> None:
+    """The element-wise entry points take flat buffers: every tensor must be contiguous
+    and have the first one's element count, dtype and device."""
+    ref = ts[0]
+    for t in ts:
+        if not t.is_contiguous():
+            raise ValueError("element-wise operands must be contiguous")
+        if t.numel() != ref.numel() or t.dtype != ref.dtype or t.device != ref.device:
+            raise ValueError(f"element-wise operands differ: {tuple(t.shape)} {t.dtype} {t.device} vs "
+                             f"{tuple(ref.shape)} {ref.dtype} {ref.device}")
+
+
 def guide(cond: torch.Tensor, uncond: torch.Tensor, ptb: torch.Tensor, mod: torch.Tensor, cfg_scale: float,
           stg_scale: float, modality_scale: float, out: torch.Tensor) -> None:
+    _same_elementwise(cond, uncond, ptb, mod, out)
     _call("ltx_guide", _ptr(cond), _ptr(uncond), _ptr(ptb), _ptr(mod), cond.numel(), cfg_scale, stg_scale,
           modality_scale, _ptr(out), _dt(cond), _stream(cond))
 
@@ -513,6 +526,9 @@ def guide_rescale_workspace(n: int, device: torch.device) -> torch.Tensor:
 def guide_rescale(cond: torch.Tensor, uncond: torch.Tensor, ptb: torch.Tensor, mod: torch.Tensor, cfg_scale: float,
                   stg_scale: float, modality_scale: float, rescale_scale: float, out: torch.Tensor,
                   workspace: torch.Tensor) -> None:
+    _same_elementwise(cond, uncond, ptb, mod, out)
+    if not workspace.is_contiguous() or workspace.dtype != torch.uint8 or workspace.device != cond.device:
+        raise ValueError("workspace must be a contiguous uint8 tensor on the operands' device")
     _call("ltx_guide_rescale", _ptr(cond), _ptr(uncond), _ptr(ptb), _ptr(mod), cond.numel(), cfg_scale, stg_scale,
           modality_scale, rescale_scale, _ptr(out), _ptr(workspace), workspace.numel(), _dt(cond), _stream(cond))
 
@@ -521,11 +537,13 @@ def guide_rescale_noalloc(cond: torch.Tensor, uncond: torch.Tensor, ptb: torch.T
                           cfg_scale: float, stg_scale: float, modality_scale: float, rescale_scale: float,
                           out: torch.Tensor) -> None:
     """guide_rescale with the library's static scratch (no workspace, n <= 1,048,576)."""
+    _same_elementwise(cond, uncond, ptb, mod, out)
     _call("ltx_guide_rescale_noalloc", _ptr(cond), _ptr(uncond), _ptr(ptb), _ptr(mod), cond.numel(), cfg_scale,
           stg_scale, modality_scale, rescale_scale, _ptr(out), _dt(cond), _stream(cond))
 
 
 def euler(sample: torch.Tensor, denoised: torch.Tensor, sigma: float, sigma_next: float, out: torch.Tensor) -> None:
+    _same_elementwise(sample, denoised, out)
     _call("ltx_euler", _ptr(sample), _ptr(denoised), sample.numel(), sigma, sigma_next, _ptr(out), _dt(sample),
           _stream(sample))
 

@@ -81,16 +81,25 @@ static std::atomic<uint64_t> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int num_sms() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cache[dev] = n;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
+}
+
+void ensure_smem_limit(std::atomic<uint64_t>& done, const void* kern, int bytes) {
+  int dev = 0;
+  LTX_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t(1) << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return;
+  LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (bit != 0) done.fetch_or(bit, std::memory_order_release);
 }
 
 }  // namespace ltx

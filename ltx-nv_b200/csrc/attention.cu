@@ -701,13 +701,8 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   const CUtensorMap tk = make_tmap_bf16_2d(k, cols, uint64_t(B) * Tk, uint64_t(ldk), 64, 128);
   const CUtensorMap tv = make_tmap_bf16_2d(v, cols, uint64_t(B) * Tk, uint64_t(ldv), 64, 128);
   auto kern = fmha_tc_kernel<D>;
-  static int attr_dev = -1;
-  int dev = 0;
-  LTX_CUDA(cudaGetDevice(&dev));
-  if (attr_dev != dev) {
-    LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    attr_dev = dev;
-  }
+  static std::atomic<uint64_t> smem_done{0};
+  ensure_smem_limit(smem_done, kern, Cfg::SMEM);
   dim3 grid(unsigned((Tq + 2 * Cfg::BM - 1) / (2 * Cfg::BM)), unsigned(H), unsigned(B));
   const float scale_log2 = scale * 1.4426950408889634f;
   kern<<<grid, 352, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), scale_log2,
@@ -724,13 +719,8 @@ void launch_fmha_kv1(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   const CUtensorMap tk = make_tmap_bf16_2d(k, cols, uint64_t(B) * Tk, uint64_t(ldk), 64, 128);
   const CUtensorMap tv = make_tmap_bf16_2d(v, cols, uint64_t(B) * Tk, uint64_t(ldv), 64, 128);
   auto kern = fmha_kv1_kernel<D>;
-  static int attr_dev = -1;
-  int dev = 0;
-  LTX_CUDA(cudaGetDevice(&dev));
-  if (attr_dev != dev) {
-    LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    attr_dev = dev;
-  }
+  static std::atomic<uint64_t> smem_done{0};
+  ensure_smem_limit(smem_done, kern, Cfg::SMEM);
   const int n_qt = int((Tq + 127) / 128);
   const int64_t n_tasks = int64_t(B) * H * n_qt;
   const int grid = int(std::min<int64_t>(n_tasks, num_sms()));

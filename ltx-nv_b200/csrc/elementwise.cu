@@ -8,6 +8,7 @@
 // at the points where the reference's op-by-op PyTorch code rounds (each torch op on a
 // bf16 tensor returns a rounded bf16 tensor).
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <type_traits>
 
@@ -1081,16 +1082,19 @@ extern "C" int ltx_guide_rescale_noalloc(const void* cond, const void* uncond, c
                                         std::to_string(kGuideStaticBytes) + " bytes (at most " +
                                         std::to_string(int64_t(kGuideStaticBlocks) * kGuideElemsPerBlock) +
                                         " elements); use ltx_guide_rescale with a workspace"};
-  // device address of the scratch, looked up once per device
+  // Device address of the scratch, looked up once per device with that device current.
+  // std::call_once makes the first call thread-safe; a lookup that fails leaves the flag
+  // unset, so the next call retries it.
+  static std::once_flag scratch_once[64];
   static void* scratch_ptr[64] = {};
   int dev = 0;
   LTX_CUDA(cudaGetDevice(&dev));
   LTX_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range");
-  if (scratch_ptr[dev] == nullptr) {
+  std::call_once(scratch_once[dev], [dev] {
     void* ptr = nullptr;
     LTX_CUDA(cudaGetSymbolAddress(&ptr, g_guide_scratch));
     scratch_ptr[dev] = ptr;
-  }
+  });
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto ws = static_cast<GuideWs*>(scratch_ptr[dev]);
   if (dtype == LTX_F32)

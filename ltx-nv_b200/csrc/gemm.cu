@@ -534,13 +534,8 @@ void launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, 
   constexpr int64_t TM = PAIR ? 2 * kBM : kBM;
   const int64_t tiles = ((M + TM - 1) / TM) * ((N + BN - 1) / BN);
   auto kern = gemm_tc_kernel<BN, PAIR>;
-  static int attr_dev = -1;
-  int dev = 0;
-  LTX_CUDA(cudaGetDevice(&dev));
-  if (attr_dev != dev) {
-    LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    attr_dev = dev;
-  }
+  static std::atomic<uint64_t> smem_done{0};
+  ensure_smem_limit(smem_done, kern, Cfg::SMEM);
   auto Cp = static_cast<__nv_bfloat16*>(C);
   if constexpr (PAIR) {
     // one CTA pair per two SMs, persistent over the 256-row tiles
@@ -698,9 +693,10 @@ __global__ void __launch_bounds__(192, 1)
 
 }  // namespace detail
 
-// Tile-width override for tuning / tests: 0 = automatic (256-column tiles on CTA pairs
-// when N >= 512 and M >= 256, else 128), 128 or 256 force single-CTA tiles of that width.
-static int g_gemm_bn_override = 0;
+// Tile-width override for tests: 0 = automatic (256-column tiles on CTA pairs when
+// N >= 512 and M >= 256, else 128), 128 or 256 force single-CTA tiles of that width.
+// Thread-local, so it changes only the calling thread's GEMMs.
+static thread_local int g_gemm_bn_override = 0;
 
 }  // namespace ltx
 
@@ -804,14 +800,8 @@ extern "C" int ltx_proj_out_cfg_euler(const void* x, int64_t ldx, const void* W,
     check_vec_ptr(vel_out, "vel_out");
     const CUtensorMap ta = make_tmap_bf16_2d(x, uint64_t(K), uint64_t(2 * T), uint64_t(ldx), kBK, kBM);
     const CUtensorMap tb = make_tmap_bf16_2d(W, uint64_t(K), 128, uint64_t(K), kBK, 128);
-    static int attr_dev = -1;
-    int dev = 0;
-    LTX_CUDA(cudaGetDevice(&dev));
-    if (attr_dev != dev) {
-      LTX_CUDA(cudaFuncSetAttribute(head_cfg_euler_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    HeadCfg::SMEM));
-      attr_dev = dev;
-    }
+    static std::atomic<uint64_t> smem_done{0};
+    ensure_smem_limit(smem_done, head_cfg_euler_kernel, HeadCfg::SMEM);
     head_cfg_euler_kernel<<<unsigned((T + kBM - 1) / kBM), 192, HeadCfg::SMEM, s>>>(
         ta, tb, int(T), int(K), static_cast<const __nv_bfloat16*>(bias), static_cast<const __nv_bfloat16*>(latent),
         timesteps, cfg_scale - 1.f, sigma, sigma_next - sigma, static_cast<__nv_bfloat16*>(vel_out),

@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include <string>
 
@@ -34,6 +35,15 @@ int num_sms();
 
 // Process-wide count of kernels this library has launched (ltx_launch_count).
 void note_launch();
+
+// Raises the dynamic shared-memory limit of `kern` to `bytes` on the current device the
+// first time a call site launches it there. `done` is the call site's static bitmask of
+// devices already configured (thread-safe; devices >= 64 are configured on every call).
+void ensure_smem_limit(std::atomic<uint64_t>& done, const void* kern, int bytes);
+template <class K>
+inline void ensure_smem_limit(std::atomic<uint64_t>& done, K* kern, int bytes) {
+  ensure_smem_limit(done, reinterpret_cast<const void*>(kern), bytes);
+}
 
 }  // namespace ltx
 

@@ -284,13 +284,8 @@ void launch_conv(const void* x, int B, const void* w, const void* bias, const vo
   const uint32_t box[4] = {64, uint32_t(cs.wb), uint32_t(cs.hb), 1};
   const CUtensorMap tx = make_tmap_bf16_4d(x, dims, strides, box);
   auto kern = conv3d_tc_kernel<BN, MH>;
-  static int attr_dev = -1;
-  int dev = 0;
-  LTX_CUDA(cudaGetDevice(&dev));
-  if (attr_dev != dev) {
-    LTX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    attr_dev = dev;
-  }
+  static std::atomic<uint64_t> smem_done{0};
+  ensure_smem_limit(smem_done, kern, Cfg::SMEM);
   const int64_t tiles = int64_t(cs.bf) * cs.th * cs.tw * ((cs.cout + BN - 1) / BN);
   const int grid = int(std::min<int64_t>(tiles, num_sms()));
   kern<<<grid, 192, Cfg::SMEM, s>>>(tx, tw, static_cast<const __nv_bfloat16*>(bias),

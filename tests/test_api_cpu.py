@@ -18,9 +18,12 @@ ROOT = Path(__file__).resolve().parents[1]
 
 
 def header_functions() -> list[str]:
-    text = (ROOT / "include" / "ltxb200.h").read_text()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(ltx_[a-z0-9_]+)\s*\(", text)))
+    """Every function declared in include/*.h (the public ABI and the test hooks)."""
+    names = set()
+    for h in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(ltx_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_exports_every_declared_symbol():

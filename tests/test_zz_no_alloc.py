@@ -11,9 +11,12 @@ DEV = "cuda"
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_noalloc_matches_workspace_variant_two_calls(dtype):
+@pytest.mark.parametrize("n", [2, 4096, 4097, 6144 * 128, 256 * 4096])
+def test_noalloc_matches_workspace_variant_two_calls(dtype, n):
+    """n covers the smallest input, one block (4096 elements per block), two blocks, one
+    benchmark video latent (192 blocks) and the limit, where 256 blocks fill the static
+    scratch exactly."""
     torch.manual_seed(21)
-    n = 6144 * 128  # one benchmark video latent
     xs = [(torch.randn(n, device=DEV) * (1.0 + 0.1 * i)).to(dtype) for i in range(4)]
     ws = nat.guide_rescale_workspace(n, xs[0].device)
     for cfg, stg, mod, rs in ((3.0, 1.0, 3.0, 0.7), (4.5, 0.0, 1.0, 1.0)):
