@@ -3,8 +3,9 @@
  * denoising step.
  *
  * Conventions
- *  - Every pointer argument is a device pointer owned by the caller; the library never
- *    allocates device memory on these paths.
+ *  - Every pointer argument is a device pointer owned by the caller. The library
+ *    allocates device memory in one place only: ltx_dit_reserve sizes the workspace an
+ *    ltx_ctx owns for the whole-step entry point (freed by ltx_ctx_destroy).
  *  - `stream` is a cudaStream_t passed as void*; every call is asynchronous on it and
  *    performs no device synchronisation.
  *  - Every entry point returns LTX_OK (0) or an ltx_status error code; ltx_last_error()
@@ -304,6 +305,121 @@ int ltx_vae_latent_in(const void* latent, int B, int C, int F, int H, int W, con
  * reference's (B, c, F, H*p, W*p) bf16 tensor; mode 1 -> decode_video's (F, H*p, W*p, c)
  * float frames of sample 0, (v + 1) / 2 clamped to [0, 1] (ltx_vae.py:218-222). */
 int ltx_vae_unpatchify(const void* x, int B, int F, int H, int W, int c, int p, int mode, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------------- */
+/* Whole denoise step: one CFG step of the video DiT (3 and 5) for   */
+/* a C or C++ caller that links this library without Python.                           */
+/* Replaces LTXModel.forward (standalone/ltx_dit.py:354-378) on the B=2 [cond, uncond] */
+/* batch followed by X0 + guide + euler_step (ltx_dit.py:551-606, CFG-only guidance),   */
+/* the sequence the reference's native port leaves unbuilt (cuda_c_standalone/Makefile: */
+/* the dit/ and runner/ targets, 11,21-27).                                             */
+/* ---------------------------------------------------------------------------------- */
+
+/* Opaque per-device context: the cache of encoded TMA descriptors (keyed by pointer,
+ * extents, row stride and box, so a hit is always valid), the step workspace and the
+ * step-invariant tables (RoPE tables, text-context K/V) of the last step. One context
+ * per device and thread; calls on one context must not overlap. */
+typedef struct ltx_ctx ltx_ctx;
+
+int ltx_ctx_create(int device, ltx_ctx** ctx);
+/* Frees the workspace (on the context's device) and the context. NULL is a no-op. */
+int ltx_ctx_destroy(ltx_ctx* ctx);
+
+/* Video-only DiT configuration (DiTConfig of ltx_dit.py:28-82 with cross-adaLN off and
+ * no audio stream: the text context keeps its own width cross_dim). */
+typedef struct {
+  int num_layers;
+  int heads, head_dim;             /* hidden D = heads * head_dim */
+  int in_channels, out_channels;   /* latent channels (128, 128) */
+  int cross_dim;                   /* text context width C */
+  int ffn_dim;                     /* FeedForward inner width (4 * D) */
+  int gated_attention;             /* to_gate_logits present in both attentions */
+  float norm_eps;                  /* 1e-6 */
+  double theta;                    /* RoPE theta (10000) */
+  float max_pos[3];                /* (20, 2048, 2048) */
+  float timestep_scale_multiplier; /* 1000 */
+  int dtype;                       /* LTX_BF16 or LTX_F32 */
+} ltx_dit_config;
+
+/* Device pointers of one block, in the storage dtype. Packed weights are row blocks of
+ * the reference's nn.Linear weights, each packed matrix zero-padded to a multiple of 8
+ * rows (its bias to the same length):
+ *   attn1_qkvg = [attn1.to_q; to_k; to_v; to_gate_logits]   (3D + H (+pad), D)
+ *   attn2_qg   = [attn2.to_q; to_gate_logits]               (D + H (+pad), D)
+ *   attn2_kv   = [attn2.to_k; to_v]                          (2D, C)
+ * (without gated attention the gate rows are absent). ff biases may be NULL
+ * (ff_bias = False). Names follow BasicAVTransformerBlock (ltx_dit.py:209-235). */
+typedef struct {
+  const void* scale_shift_table; /* (6, D) */
+  const void* attn1_qkvg_w;
+  const void* attn1_qkvg_b;
+  const void* attn1_q_norm;      /* (D) RMSNorm gains */
+  const void* attn1_k_norm;
+  const void* attn1_out_w;       /* (D, D) */
+  const void* attn1_out_b;
+  const void* attn2_qg_w;
+  const void* attn2_qg_b;
+  const void* attn2_kv_w;
+  const void* attn2_kv_b;
+  const void* attn2_q_norm;
+  const void* attn2_k_norm;
+  const void* attn2_out_w;
+  const void* attn2_out_b;
+  const void* ff_in_w;           /* (F, D) */
+  const void* ff_in_b;
+  const void* ff_out_w;          /* (D, F) */
+  const void* ff_out_b;
+} ltx_dit_block_weights;
+
+/* Model-level device pointers (LTXModel, ltx_dit.py:325-352) and the host array of the
+ * num_layers blocks. */
+typedef struct {
+  const void* patchify_w;        /* (D, in_channels) */
+  const void* patchify_b;        /* (D) */
+  const void* keyframes_emb;     /* (D) keyframes_abs_pos_embedding, or NULL */
+  const void* t_linear_1_w;      /* adaln_single.emb.timestep_embedder.linear_1 (D, 256) */
+  const void* t_linear_1_b;
+  const void* t_linear_2_w;      /* ... linear_2 (D, D) */
+  const void* t_linear_2_b;
+  const void* adaln_w;           /* adaln_single.linear (6D, D) */
+  const void* adaln_b;
+  const void* scale_shift_table; /* (2, D) output head */
+  const void* proj_out_w;        /* (out_channels, D) */
+  const void* proj_out_b;
+  const ltx_dit_block_weights* blocks;
+} ltx_dit_weights;
+
+/* Step flags. REUSE_TEXT_KV: use the text-context K/V projections of the previous step
+ * on this context (the caller asserts that the contexts and weights are unchanged: they
+ * are constant over a denoise loop, ltx_dit.py:609-621). REUSE_ROPE: use the previous
+ * step's RoPE tables (same positions). Without a previous step they are computed. */
+enum { LTX_STEP_REUSE_TEXT_KV = 1, LTX_STEP_REUSE_ROPE = 2 };
+
+typedef struct {
+  const void* latent;          /* (T, in_channels) current latent of the video */
+  const float* positions;      /* (3, T, 2) fp32 [start, end) bounds (video_positions of one sample) */
+  const void* context_pos;     /* (S, C) conditional text context */
+  const void* context_neg;     /* (S, C) unconditional text context */
+  const float* keyframes_mask; /* (T) fp32, > 0 on conditioned tokens, or NULL */
+  int64_t T, S;
+  float sigma, sigma_next, cfg_scale;
+  int flags;
+} ltx_dit_step_args;
+
+/* Device bytes the context needs for steps of T latent tokens and S text tokens. */
+size_t ltx_dit_workspace_bytes(const ltx_dit_config* cfg, int64_t T, int64_t S);
+/* Sizes the context's workspace for (cfg, T, S): the one call of this library that
+ * allocates device memory (cudaMalloc on the context's device; freed by
+ * ltx_ctx_destroy). It also uploads the RoPE frequency grid (computed in float64 on the
+ * host, ltx_nn.py:34-46). Synchronous. ltx_dit_step itself allocates nothing, so it can
+ * be captured in a CUDA graph once reserved. */
+int ltx_dit_reserve(ltx_ctx* ctx, const ltx_dit_config* cfg, int64_t T, int64_t S);
+/* One CFG denoise step on `stream`: velocity (2, T, out) [cond; uncond] (may be NULL in
+ * bf16), denoised (T, out) (may be NULL in bf16) and new_latent (T, out). The same
+ * kernels with the same arguments as ltx_dit.cfg_denoise_step, so the results are
+ * bit-identical. Calls on one context must not overlap in time. */
+int ltx_dit_step(ltx_ctx* ctx, const ltx_dit_config* cfg, const ltx_dit_weights* weights, const ltx_dit_step_args* args,
+                 void* velocity, void* denoised, void* new_latent, void* stream);
 
 #ifdef __cplusplus
 }

@@ -67,7 +67,68 @@ class Epilogue(ctypes.Structure):
     ]
 
 
-# name -> (restype, argtypes); the exported symbols of include/ltxb200.h.
+class DitConfig(ctypes.Structure):
+    """Mirror of ltx_dit_config (include/ltxb200.h)."""
+
+    _fields_ = [
+        ("num_layers", ctypes.c_int),
+        ("heads", ctypes.c_int),
+        ("head_dim", ctypes.c_int),
+        ("in_channels", ctypes.c_int),
+        ("out_channels", ctypes.c_int),
+        ("cross_dim", ctypes.c_int),
+        ("ffn_dim", ctypes.c_int),
+        ("gated_attention", ctypes.c_int),
+        ("norm_eps", ctypes.c_float),
+        ("theta", ctypes.c_double),
+        ("max_pos", ctypes.c_float * 3),
+        ("timestep_scale_multiplier", ctypes.c_float),
+        ("dtype", ctypes.c_int),
+    ]
+
+
+DIT_BLOCK_FIELDS = ["scale_shift_table", "attn1_qkvg_w", "attn1_qkvg_b", "attn1_q_norm", "attn1_k_norm",
+                    "attn1_out_w", "attn1_out_b", "attn2_qg_w", "attn2_qg_b", "attn2_kv_w", "attn2_kv_b",
+                    "attn2_q_norm", "attn2_k_norm", "attn2_out_w", "attn2_out_b", "ff_in_w", "ff_in_b", "ff_out_w",
+                    "ff_out_b"]
+
+
+class DitBlockWeights(ctypes.Structure):
+    """Mirror of ltx_dit_block_weights (include/ltxb200.h)."""
+
+    _fields_ = [(n, c_vp) for n in DIT_BLOCK_FIELDS]
+
+
+class DitWeights(ctypes.Structure):
+    """Mirror of ltx_dit_weights (include/ltxb200.h)."""
+
+    _fields_ = [(n, c_vp) for n in ("patchify_w", "patchify_b", "keyframes_emb", "t_linear_1_w", "t_linear_1_b",
+                                     "t_linear_2_w", "t_linear_2_b", "adaln_w", "adaln_b", "scale_shift_table",
+                                     "proj_out_w", "proj_out_b")] + [("blocks", ctypes.POINTER(DitBlockWeights))]
+
+
+class DitStepArgs(ctypes.Structure):
+    """Mirror of ltx_dit_step_args (include/ltxb200.h)."""
+
+    _fields_ = [
+        ("latent", c_vp),
+        ("positions", c_vp),
+        ("context_pos", c_vp),
+        ("context_neg", c_vp),
+        ("keyframes_mask", c_vp),
+        ("T", c_i64),
+        ("S", c_i64),
+        ("sigma", ctypes.c_float),
+        ("sigma_next", ctypes.c_float),
+        ("cfg_scale", ctypes.c_float),
+        ("flags", ctypes.c_int),
+    ]
+
+
+STEP_REUSE_TEXT_KV, STEP_REUSE_ROPE = 1, 2
+
+# name -> (restype, argtypes); the exported symbols of include/ltxb200.h (and the test
+# hooks of include/ltxb200_testing.h).
 _SIGNATURES = {
     "ltx_last_error": (ctypes.c_char_p, []),
     "ltx_abi_version": (ctypes.c_int, []),
@@ -128,6 +189,12 @@ _SIGNATURES = {
     "ltx_proj_out_cfg_euler": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, ctypes.c_int, c_i64, c_vp, c_vp,
                                               ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp,
                                               ctypes.c_int, c_vp]),
+    "ltx_ctx_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(c_vp)]),
+    "ltx_ctx_destroy": (ctypes.c_int, [c_vp]),
+    "ltx_dit_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(DitConfig), c_i64, c_i64]),
+    "ltx_dit_reserve": (ctypes.c_int, [c_vp, ctypes.POINTER(DitConfig), c_i64, c_i64]),
+    "ltx_dit_step": (ctypes.c_int, [c_vp, ctypes.POINTER(DitConfig), ctypes.POINTER(DitWeights),
+                                    ctypes.POINTER(DitStepArgs), c_vp, c_vp, c_vp, c_vp]),
 }
 
 _lib = None
@@ -556,3 +623,30 @@ def proj_out_cfg_euler(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, lat
     _call("ltx_proj_out_cfg_euler", _ptr(x), _ld(x), _ptr(w), _ptr(bias), t, c, x.shape[1], _ptr(latent),
           _ptr(timesteps), cfg_scale, sigma, sigma_next, _ptr(vel_out), _ptr(denoised), _ptr(new_latent), _dt(x),
           _stream(x))
+
+
+# ---------------------------------------------------------------------------------------
+# Whole-step entry point (ltx_ctx / ltx_dit_step)
+# ---------------------------------------------------------------------------------------
+def ctx_create(device: int) -> int:
+    h = c_vp()
+    _call("ltx_ctx_create", device, ctypes.byref(h))
+    return h.value
+
+
+def ctx_destroy(ctx: int) -> None:
+    _call("ltx_ctx_destroy", ctx)
+
+
+def dit_workspace_bytes(cfg: DitConfig, t: int, s: int) -> int:
+    return int(load_library().ltx_dit_workspace_bytes(ctypes.byref(cfg), t, s))
+
+
+def dit_reserve(ctx: int, cfg: DitConfig, t: int, s: int) -> None:
+    _call("ltx_dit_reserve", ctx, ctypes.byref(cfg), t, s)
+
+
+def dit_step(ctx: int, cfg: DitConfig, weights: DitWeights, args: DitStepArgs, velocity: torch.Tensor | None,
+             denoised: torch.Tensor | None, new_latent: torch.Tensor) -> None:
+    _call("ltx_dit_step", ctx, ctypes.byref(cfg), ctypes.byref(weights), ctypes.byref(args), _ptr(velocity),
+          _ptr(denoised), _ptr(new_latent), _stream(new_latent), label="ltx_dit_step" if _profile is not None else None)

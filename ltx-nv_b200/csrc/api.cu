@@ -6,6 +6,7 @@
 #include <atomic>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "ltx_common.cuh"
 #include "ltx_internal.h"
@@ -30,6 +31,37 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+struct TmapKey {
+  const void* ptr;
+  uint64_t inner, outer, ld;
+  uint32_t box_inner, box_outer;
+  bool operator==(const TmapKey& o) const {
+    return ptr == o.ptr && inner == o.inner && outer == o.outer && ld == o.ld && box_inner == o.box_inner &&
+           box_outer == o.box_outer;
+  }
+};
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.ptr);
+    for (uint64_t v : {k.inner, k.outer, k.ld, uint64_t(k.box_inner) << 32 | k.box_outer})
+      h = (h ^ v) * 0x100000001b3ull + (h >> 29);
+    return size_t(h);
+  }
+};
+struct TmapCache {
+  std::mutex mu;
+  std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> maps;
+};
+static thread_local TmapCache* t_tmap_cache = nullptr;
+
+TmapCache* tmap_cache_new() { return new TmapCache(); }
+void tmap_cache_delete(TmapCache* c) { delete c; }
+TmapScope::TmapScope(TmapCache* c) : prev_(t_tmap_cache) { t_tmap_cache = c; }
+TmapScope::~TmapScope() { t_tmap_cache = prev_; }
+
+static CUtensorMap encode_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                                       uint32_t box_inner, uint32_t box_outer);
+
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
                               uint32_t box_outer) {
   if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
@@ -37,6 +69,23 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, u
   if ((ld * 2) % 16 != 0) throw ApiError{LTX_ERR_INVALID, "TMA row stride must be a multiple of 16 bytes"};
   if (box_inner * 2 > 128 || box_outer > 256 || box_inner == 0 || box_outer == 0)
     throw ApiError{LTX_ERR_INVALID, "TMA box out of range"};
+  TmapCache* cache = t_tmap_cache;
+  if (cache == nullptr) return encode_tmap_bf16_2d(ptr, inner, outer, ld, box_inner, box_outer);
+  const TmapKey key{ptr, inner, outer, ld, box_inner, box_outer};
+  {
+    std::lock_guard<std::mutex> lock(cache->mu);
+    auto it = cache->maps.find(key);
+    if (it != cache->maps.end()) return it->second;
+  }
+  const CUtensorMap m = encode_tmap_bf16_2d(ptr, inner, outer, ld, box_inner, box_outer);
+  std::lock_guard<std::mutex> lock(cache->mu);
+  if (cache->maps.size() >= 8192) cache->maps.clear();
+  cache->maps.emplace(key, m);
+  return m;
+}
+
+static CUtensorMap encode_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                                       uint32_t box_inner, uint32_t box_outer) {
   auto fn = encode_fn();
   if (fn == nullptr) throw ApiError{LTX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable"};
   CUtensorMap m;

@@ -30,6 +30,24 @@ CUtensorMap make_tmap_bf16_4d(const void* ptr, const uint64_t (&dims)[4], const 
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
                               uint32_t box_outer);
 
+// Cache of encoded tensor maps, keyed by everything a 2-D map encodes (address,
+// extents, row stride, box), so a hit is always the descriptor a fresh encoding would
+// give. While a TmapScope is alive on a thread, make_tmap_bf16_2d consults the scope's
+// cache before encoding (the ltx_ctx of the whole-step entry point owns one).
+struct TmapCache;
+TmapCache* tmap_cache_new();
+void tmap_cache_delete(TmapCache* c);
+class TmapScope {
+ public:
+  explicit TmapScope(TmapCache* c);
+  ~TmapScope();
+  TmapScope(const TmapScope&) = delete;
+  TmapScope& operator=(const TmapScope&) = delete;
+
+ private:
+  TmapCache* prev_;
+};
+
 // Number of SMs of the current device (cached per device).
 int num_sms();
 

@@ -7,3 +7,4 @@
 #include "attention.cu"
 #include "parallel.cu"
 #include "vae.cu"
+#include "dit_step.cu"

@@ -793,6 +793,110 @@ def cfg_denoise_step(model: LTXModel, latent: torch.Tensor, positions: torch.Ten
     return vel.view(2, t, c), den.view(1, t, c), nxt.view(1, t, c)
 
 
+class NativeStep:
+    """cfg_denoise_step through the library's whole-step C entry point (ltx_dit_step):
+    the path a C or C++ caller takes without Python. It owns an ltx_ctx (TMA descriptor
+    cache, step workspace sized for T latent and S text tokens) and the weight table of
+    `model` (the packed attention weights of ltx_nn). Video-only models without
+    cross-adaLN (3, 5). Results equal cfg_denoise_step bit for bit."""
+
+    def __init__(self, model: LTXModel, tokens: int, text_tokens: int):
+        cfg = model.cfg
+        if cfg.cross_attention_adaln:
+            raise NotImplementedError("ltx_dit_step runs the video DiT without cross-adaLN")
+        dev = model.proj_out.weight.device
+        self.device = dev
+        dtype = model.proj_out.weight.dtype
+        c = nat.DitConfig()
+        c.num_layers, c.heads, c.head_dim = cfg.num_layers, cfg.video_heads, cfg.video_head_dim
+        c.in_channels, c.out_channels, c.cross_dim = cfg.video_in, cfg.video_out, cfg.video_cross_dim
+        c.ffn_dim = model.blocks[0].ff.proj_in.out_features
+        c.gated_attention = int(cfg.gated_attention)
+        c.norm_eps, c.theta = cfg.norm_eps, cfg.theta
+        c.max_pos[:] = [float(v) for v in cfg.video_max_pos]
+        c.timestep_scale_multiplier = float(cfg.timestep_scale_multiplier)
+        c.dtype = nat.LTX_BF16 if dtype == torch.bfloat16 else nat.LTX_F32
+        self.cfg_c = c
+        keep = []
+
+        def p(t):
+            if t is None:
+                return None
+            t = t.detach()
+            if not t.is_contiguous():
+                raise ValueError("weights must be contiguous")
+            keep.append(t)
+            return t.data_ptr()
+
+        blocks = (nat.DitBlockWeights * cfg.num_layers)()
+        for i, blk in enumerate(model.blocks):
+            wqkv, bqkv = blk.attn1.packed_self()
+            wq, bq = blk.attn2.packed_q()
+            wkv, bkv = blk.attn2.packed_kv()
+            vals = [blk.scale_shift_table, wqkv, bqkv, blk.attn1.q_norm.weight, blk.attn1.k_norm.weight,
+                    blk.attn1.to_out.weight, blk.attn1.to_out.bias, wq, bq, wkv, bkv, blk.attn2.q_norm.weight,
+                    blk.attn2.k_norm.weight, blk.attn2.to_out.weight, blk.attn2.to_out.bias, blk.ff.proj_in.weight,
+                    blk.ff.proj_in.bias, blk.ff.proj_out.weight, blk.ff.proj_out.bias]
+            for name, v in zip(nat.DIT_BLOCK_FIELDS, vals):
+                setattr(blocks[i], name, p(v))
+        te = model.adaln_single.emb.timestep_embedder
+        w = nat.DitWeights()
+        w.patchify_w, w.patchify_b = p(model.patchify_proj.weight), p(model.patchify_proj.bias)
+        kf = model.keyframes_abs_pos_embedding
+        w.keyframes_emb = p(kf.reshape(-1)) if kf is not None else None
+        w.t_linear_1_w, w.t_linear_1_b = p(te.linear_1.weight), p(te.linear_1.bias)
+        w.t_linear_2_w, w.t_linear_2_b = p(te.linear_2.weight), p(te.linear_2.bias)
+        w.adaln_w, w.adaln_b = p(model.adaln_single.linear.weight), p(model.adaln_single.linear.bias)
+        w.scale_shift_table = p(model.scale_shift_table)
+        w.proj_out_w, w.proj_out_b = p(model.proj_out.weight), p(model.proj_out.bias)
+        w.blocks = blocks
+        self.weights, self._blocks, self._keep = w, blocks, keep
+        self.dtype, self.T, self.S = dtype, tokens, text_tokens
+        self.ctx = nat.ctx_create(dev.index if dev.index is not None else torch.cuda.current_device())
+        nat.dit_reserve(self.ctx, c, tokens, text_tokens)
+
+    def close(self) -> None:
+        if getattr(self, "ctx", None):
+            nat.ctx_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+    def __call__(self, latent: torch.Tensor, positions: torch.Tensor, context_pos: torch.Tensor,
+                 context_neg: torch.Tensor, sigmas: torch.Tensor, idx: int, cfg_scale: float,
+                 keyframes_mask: torch.Tensor | None = None, reuse: bool = False, out: tuple | None = None):
+        """Same arguments and results as cfg_denoise_step. reuse=True keeps the RoPE tables
+        and text K/V of the previous call (same positions and contexts). `out` optionally
+        gives (velocity (2, T, C), denoised (1, T, C), next latent (1, T, C)) buffers."""
+        sigma, sigma_next = _sigma_pair(sigmas, idx)
+        _, t, c = latent.shape
+        dt = self.dtype
+        lat = latent.to(dt).reshape(t, c).contiguous()
+        pos = positions.reshape(-1, 3, t, 2)[0].to(torch.float32).contiguous()
+        cp = context_pos.to(dt).reshape(-1, context_pos.shape[-1]).contiguous()
+        cn = context_neg.to(dt).reshape(-1, context_neg.shape[-1]).contiguous()
+        kf = keyframes_mask.reshape(-1, t)[0].to(torch.float32).contiguous() if keyframes_mask is not None else None
+        a = nat.DitStepArgs()
+        a.latent, a.positions, a.context_pos, a.context_neg = lat.data_ptr(), pos.data_ptr(), cp.data_ptr(), cn.data_ptr()
+        a.keyframes_mask = kf.data_ptr() if kf is not None else None
+        a.T, a.S = t, cp.shape[0]
+        a.sigma, a.sigma_next, a.cfg_scale = sigma, sigma_next, float(cfg_scale)
+        a.flags = (nat.STEP_REUSE_TEXT_KV | nat.STEP_REUSE_ROPE) if reuse else 0
+        if out is None:
+            vel = torch.empty(2, t, c, device=lat.device, dtype=dt)
+            den = torch.empty(1, t, c, device=lat.device, dtype=dt)
+            nxt = torch.empty(1, t, c, device=lat.device, dtype=dt)
+        else:
+            vel, den, nxt = out
+        self._args = (lat, pos, cp, cn, kf)  # alive until the stream has consumed them
+        nat.dit_step(self.ctx, self.cfg_c, self.weights, a, vel, den, nxt)
+        return vel, den, nxt
+
+
 _guide_ws: dict = {}
 
 

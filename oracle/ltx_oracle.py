@@ -60,7 +60,7 @@ def freq_grid(theta: float, n_axes: int, inner_dim: int, double: bool = True) ->
 def rope_tables(positions, dim, out_dtype, theta, max_pos, heads, double=True):
     """ltx_nn.py:63-96: positions (B, n_axes, T, 2) -> (cos, sin) each (B, H, T, dim/2/H)."""
     n_axes = positions.shape[1]
-    freqs = freq_grid(float(theta), n_axes, dim, double)
+    freqs = freq_grid(float(theta), n_axes, dim, double).to(positions.device)
     grid = (positions[..., 0] + positions[..., 1]) / 2.0
     frac = torch.stack([grid[:, i] / max_pos[i] for i in range(n_axes)], dim=-1)
     ang = (freqs * (frac.unsqueeze(-1) * 2 - 1)).transpose(-1, -2).flatten(2)
@@ -90,7 +90,7 @@ def apply_rope(x, tables):
 def timestep_sinusoid(t, dim=256, max_period=10000):
     """standalone/common.py:138-148 ([cos, sin], flip_sin_to_cos)."""
     half = dim // 2
-    freqs = torch.exp(-math.log(max_period) * torch.arange(0, half, dtype=torch.float32) / half)
+    freqs = torch.exp(-math.log(max_period) * torch.arange(0, half, dtype=torch.float32, device=t.device) / half)
     args = t[:, None].float() * freqs[None, :]
     emb = torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
     if dim % 2:
@@ -284,7 +284,7 @@ def block(w, cfg, i, va: StreamArgs | None, aa: StreamArgs | None, keep=None):
                              p + "audio_prompt_scale_shift_table", rms_norm(ax, eps), aa, ah, ad)
     if run_a2v or run_v2a:
         vx_pre, ax_pre = vx, ax
-        kv_mask = keep if keep is not None else torch.ones(4, vx.shape[0], dtype=vx.dtype)
+        kv_mask = keep if keep is not None else torch.ones(4, vx.shape[0], dtype=vx.dtype, device=vx.device)
         if run_a2v and bool((kv_mask[2] != 0).any()):
             s, shv, g = av_ada(w[p + "scale_shift_table_a2v_ca_video"], vx.shape[0], va.cross_ss, va.cross_gate,
                                slice(0, 2))
@@ -410,8 +410,8 @@ def cfg_denoise_step(w, cfg, latent, positions, context_pos, context_neg, sigmas
     (ltx_dit.py:591-593), CFG guide, Euler. latent (1, T, C). Returns
     (velocity (2, T, C), denoised (1, T, C), next latent (1, T, C))."""
     t = latent.shape[1]
-    sigma = sigmas[idx]
-    dm = torch.ones(1, t, 1) if denoise_mask is None else denoise_mask
+    sigma = sigmas[idx].to(latent.device)
+    dm = torch.ones(1, t, 1, device=latent.device) if denoise_mask is None else denoise_mask
     sigma_b = sigma.expand(2)
     lat2 = latent.repeat(2, 1, 1)
     ts = dm.repeat(2, 1, 1) * sigma_b.view(2, 1, 1)

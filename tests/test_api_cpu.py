@@ -49,6 +49,32 @@ def test_library_status_codes_without_a_gpu():
     assert lib.ltx_philox_offset_increment(1572864, 1184) == philox_oracle.offset_increment(1572864, 1184)
 
 
+def test_whole_step_entry_points_without_a_gpu():
+    """ltx_dit_workspace_bytes is host arithmetic; the context / step entry points
+    validate their arguments and report errors as status codes, never by crashing."""
+    lib = nat.load_library()
+    c = nat.DitConfig()
+    c.num_layers, c.heads, c.head_dim = 28, 32, 64
+    c.in_channels = c.out_channels = 128
+    c.cross_dim, c.ffn_dim, c.gated_attention = 4096, 8192, 1
+    c.norm_eps, c.theta, c.timestep_scale_multiplier, c.dtype = 1e-6, 10000.0, 1000.0, nat.LTX_BF16
+    c.max_pos[:] = [20.0, 2048.0, 2048.0]
+    t, s, d = 6144, 128, 2048
+    nbytes = nat.dit_workspace_bytes(c, t, s)
+    # x, h, o (2T x D), the shared QKV / text-q / FFN buffer (2T x F), text K/V of every block
+    assert nbytes >= 2 * (3 * 2 * t * d + 2 * t * 8192 + 28 * 2 * s * 2 * d)
+    assert nbytes < 2 * (3 * 2 * t * d + 2 * t * 8192 + 28 * 2 * s * 2 * d) + 64 << 20
+    assert lib.ltx_dit_workspace_bytes(None, t, s) == 0
+    assert lib.ltx_ctx_destroy(None) == 0
+    st = lib.ltx_dit_step(None, ctypes.byref(c), None, None, None, None, None, None)
+    assert st == 1 and b"NULL" in lib.ltx_last_error()
+    st = lib.ltx_dit_reserve(None, ctypes.byref(c), t, s)
+    assert st == 1
+    h = ctypes.c_void_p()
+    assert lib.ltx_ctx_create(0, ctypes.byref(h)) != 0  # no CUDA device here
+    assert h.value is None
+
+
 def test_vae_decoder_parameter_layout_matches_reference():
     """ConvVideoDecoder has the reference's parameter names, shapes and order (and its
     per-channel statistics buffers), so reference state dicts load unchanged."""
