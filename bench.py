@@ -45,8 +45,22 @@ import torch  # noqa: E402
 
 METRIC = "DiT denoise steps/s & latent tokens/s at 1/2/4/8 B200; % BF16 TC peak"
 UNIT = "latent tokens/s"
-CFG3 = dict(num_layers=28, heads=32, head_dim=64, cross_dim=4096, f=16, h=16, w=24, text=128, sigma=0.5,
-            sigma_next=0.25, cfg_scale=3.0)
+CONFIGS = {
+    # BASELINE.json configs; 1 (FP32 CPU loop) and 2 (microbench) are parity-test cases
+    3: dict(kind="video", num_layers=28, heads=32, head_dim=64, cross_dim=4096, f=16, h=16, w=24, text=128,
+            sigma=0.5, sigma_next=0.25, cfg_scale=3.0, loop=None,
+            workload="BASELINE config 3: full-size video DiT CFG denoise step"),
+    4: dict(kind="av", num_layers=48, heads=32, head_dim=128, cross_dim=3840, f=16, h=16, w=24, text=1024,
+            audio_tokens=126, audio_text=1024, audio_cross=2048, sigma=0.5, sigma_next=0.25, cfg_scale=3.0, loop=None,
+            workload="BASELINE config 4: dual-stream audio-video DiT CFG denoise step (video 4096 wide, 6144 "
+                     "tokens; audio 2048 wide, 126 tokens; A<->V attention in every block; text 1024x3840 and "
+                     "1024x2048)"),
+    5: dict(kind="video", num_layers=28, heads=32, head_dim=64, cross_dim=4096, f=33, h=22, w=38, text=128,
+            cfg_scale=3.0, loop=30,
+            workload="BASELINE config 5: long high-res video, 27588 tokens, steps of the 30-step Euler loop "
+                     "(ltx2_scheduler_sigmas(30))"),
+}
+CFG3 = CONFIGS[3]
 
 
 def step_flops(c=CFG3, batch=2, text_kv_cached=True) -> float:
@@ -67,13 +81,21 @@ def workload_config(c=CFG3) -> dict:
     """The `config` object of both arms' JSON lines (the workload only, so the two arms'
     objects are equal; how it ran goes in `execution`)."""
     t = c["f"] * c["h"] * c["w"]
-    return {"workload": "BASELINE config 3: full-size video DiT CFG denoise step",
-            "model": f"LTX-2.5 video DiT {c['num_layers']} blocks, hidden {c['heads'] * c['head_dim']}, "
-                     f"{c['heads']}x{c['head_dim']} heads, FFN {4 * c['heads'] * c['head_dim']} (random-init "
-                     "N(0,0.02))",
-            "global_batch": 2, "latent_tokens": t, "seq_len": t, "text_tokens": c["text"],
-            "sigma": c["sigma"], "sigma_next": c["sigma_next"], "cfg_scale": c["cfg_scale"],
-            "l2": "inputs larger than L2 (4.2 GB weights, ~1 GB activations per step)"}
+    d = c["heads"] * c["head_dim"]
+    kind = "audio-video DiT" if c["kind"] == "av" else "video DiT"
+    out = {"workload": c["workload"],
+           "model": f"LTX-2.5 {kind} {c['num_layers']} blocks, hidden {d}, {c['heads']}x{c['head_dim']} heads, "
+                    f"FFN {4 * d} (random-init N(0,0.02))",
+           "global_batch": 2, "latent_tokens": t, "seq_len": t, "text_tokens": c["text"],
+           "cfg_scale": c["cfg_scale"],
+           "l2": "inputs larger than L2 (weights of several GB, activations of ~1 GB or more per step)"}
+    if c.get("loop"):
+        out["schedule"] = f"ltx2_scheduler_sigmas({c['loop']}), step k uses sigmas[k % {c['loop']}]"
+    else:
+        out["sigma"], out["sigma_next"] = c["sigma"], c["sigma_next"]
+    if c["kind"] == "av":
+        out.update(audio_tokens=c["audio_tokens"], audio_text_tokens=c["audio_text"], audio_hidden=2048)
+    return out
 
 
 def load_peaks() -> dict:
@@ -137,14 +159,23 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 
 
-def build_model(dev: torch.device, seed: int = 1):
-    """Config-3 model with N(0, 0.02) weights drawn on the device by the Philox kernel
+def dit_config(c):
+    import ltx_dit
+
+    if c["kind"] == "av":
+        return ltx_dit.DiTConfig(num_layers=c["num_layers"], video_heads=c["heads"], video_head_dim=c["head_dim"],
+                                 video_cross_dim=c["cross_dim"], audio_cross_dim=c["audio_cross"],
+                                 cross_attention_adaln=False)
+    return ltx_dit.DiTConfig.video_only(num_layers=c["num_layers"], heads=c["heads"], head_dim=c["head_dim"],
+                                        cross_dim=c["cross_dim"])
+
+
+def build_model(dev: torch.device, seed: int = 1, c=CFG3):
+    """The config's model with N(0, 0.02) weights drawn on the device by the Philox kernel
     (q/k RMSNorm gains offset by +1, as in the oracle's synthetic weights)."""
     import ltx_dit
 
-    c = CFG3
-    cfg = ltx_dit.DiTConfig.video_only(num_layers=c["num_layers"], heads=c["heads"], head_dim=c["head_dim"],
-                                       cross_dim=c["cross_dim"])
+    cfg = dit_config(c)
     with torch.device("meta"):
         model = ltx_dit.LTXModel(cfg)
     gen = ltx_dit.PhiloxGenerator(seed, dev)
@@ -158,43 +189,63 @@ def build_model(dev: torch.device, seed: int = 1):
     return model.eval(), cfg
 
 
-def make_inputs(dev: torch.device, seed: int = 7):
+def make_inputs(dev: torch.device, seed: int = 7, c=CFG3):
+    """Latent(s), text contexts, positions, keyframe mask and sigma schedule of the config."""
     import ltx_dit
 
-    c = CFG3
     t = c["f"] * c["h"] * c["w"]
     gen = ltx_dit.PhiloxGenerator(seed, dev)
-    latent = gen.randn(1, t, 128, dtype=torch.bfloat16)
-    ctx = gen.randn(2, c["text"], c["cross_dim"], dtype=torch.bfloat16)
-    pos = ltx_dit.video_positions(1, c["f"], c["h"], c["w"], 24.0, dev)
+    inp = dict(latent=gen.randn(1, t, 128, dtype=torch.bfloat16),
+               ctx=gen.randn(2, c["text"], c["cross_dim"], dtype=torch.bfloat16),
+               pos=ltx_dit.video_positions(1, c["f"], c["h"], c["w"], 24.0, dev))
     kf = torch.zeros(1, t, 1, device=dev)
     kf[:, : c["h"] * c["w"]] = 1.0
-    sigmas = torch.tensor([c["sigma"], c["sigma_next"]], dtype=torch.float32)
-    return latent, ctx, pos, kf, sigmas
+    inp["kf"] = kf
+    if c.get("loop"):
+        inp["sigmas"] = ltx_dit.ltx2_scheduler_sigmas(c["loop"])
+    else:
+        inp["sigmas"] = torch.tensor([c["sigma"], c["sigma_next"]], dtype=torch.float32)
+    if c["kind"] == "av":
+        ta = c["audio_tokens"]
+        inp["a_latent"] = gen.randn(1, ta, 128, dtype=torch.bfloat16)
+        inp["a_ctx"] = gen.randn(2, c["audio_text"], c["audio_cross"], dtype=torch.bfloat16)
+        inp["a_pos"] = ltx_dit.audio_positions(1, ta, dev)
+    return inp
 
 
 def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
     import _native as nat
     import ltx_dit
 
-    c = CFG3
+    c = CONFIGS[args.config]
     t = c["f"] * c["h"] * c["w"]
-    model, cfg = build_model(dev)
-    latent, ctx, pos, kf, sigmas = make_inputs(dev, seed=7)
-    cpos, cneg = ctx[:1], ctx[1:]
-    if world > 1:
+    model, cfg = build_model(dev, c=c)
+    inp = make_inputs(dev, seed=7, c=c)
+    latent, pos, kf, sigmas = inp["latent"], inp["pos"], inp["kf"], inp["sigmas"]
+    cpos, cneg = inp["ctx"][:1], inp["ctx"][1:]
+    n_sig = len(sigmas) - 1
+    if c["kind"] == "av":
+        if world > 1:
+            raise SystemExit("config 4 runs on one GPU (the audio stream is not sharded)")
+        layout = None
+        a_lat, a_pos, a_ctx = inp["a_latent"], inp["a_pos"], inp["a_ctx"]
+
+        def step(lat, idx=0):
+            return ltx_dit.av_cfg_denoise_step(model, lat, a_lat, pos, a_pos, cpos, cneg, a_ctx[:1], a_ctx[1:],
+                                               sigmas, idx % n_sig, c["cfg_scale"], v_keyframes_mask=kf)[0]
+    elif world > 1:
         import ltx_parallel
 
         pdn = ltx_parallel.ParallelDenoiser(model)
         layout = pdn.layout
 
-        def step(lat):
-            return pdn.step(lat, pos, cpos, cneg, sigmas, 0, c["cfg_scale"], keyframes_mask=kf)
+        def step(lat, idx=0):
+            return pdn.step(lat, pos, cpos, cneg, sigmas, idx % n_sig, c["cfg_scale"], keyframes_mask=kf)
     else:
         layout = None
 
-        def step(lat):
-            return ltx_dit.cfg_denoise_step(model, lat, pos, cpos, cneg, sigmas, 0, c["cfg_scale"],
+        def step(lat, idx=0):
+            return ltx_dit.cfg_denoise_step(model, lat, pos, cpos, cneg, sigmas, idx % n_sig, c["cfg_scale"],
                                             keyframes_mask=kf)[2]
 
     stream = torch.cuda.current_stream(dev)
@@ -203,7 +254,9 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         step(latent)
     torch.cuda.synchronize(dev)
     graph = None
-    if not args.no_graph:
+    # a denoise loop (config 5) walks the schedule: every step has its own sigmas, so it
+    # runs eagerly (a captured graph would replay one step's sigmas)
+    if not args.no_graph and not c.get("loop"):
         # one step captured in a CUDA graph (N > 1: the NCCL collectives of the step are
         # captured too; every rank captures the same sequence after the eager warm-up
         # has initialised the communicators)
@@ -230,9 +283,12 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
     ev1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
         ev0.record(stream)
-        for _ in range(args.steps):
+        lat = latent
+        for k in range(args.steps):
             if graph is not None:
                 graph.replay()
+            elif c.get("loop"):
+                lat = step(lat, k)
             else:
                 step(latent)
         ev1.record(stream)
@@ -259,9 +315,9 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
     e1 = torch.cuda.Event(enable_timing=True)
     e2e_steps = max(1, min(args.steps, 10))
     e0.record(stream)
-    for _ in range(e2e_steps):
+    for k in range(e2e_steps):
         lat_dev = host_in.to(dev, non_blocking=True)
-        out = step(lat_dev)
+        out = step(lat_dev, k)
         host_out.copy_(out, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize(dev)
@@ -285,7 +341,9 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
     if rank != 0:
         return None
     peaks = load_peaks()
-    flops = step_flops()
+    # algorithmic FLOPs of the step as executed: 2MNK per GEMM and 4*B*H*Tq*Tk*d per
+    # attention launch of the profiled step (config 3: equals step_flops())
+    flops = sum((kernel_flops(k) or 0.0) * v["launches"] for k, v in kern.items())
     tflops = flops / (ms_per_step / 1e3) / 1e12
     # dominant kernel by total time
     dom_label, dom = max(kern.items(), key=lambda kv: kv[1]["total_ms"])
@@ -305,7 +363,7 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": workload_config(),
+        "config": workload_config(c),
         "execution": {"parallelism": "single GPU" if world == 1 else
                       f"cfg{layout.cfg} x sp{layout.sp} (Ulysses, NCCL)", "cuda_graph": used_graph,
                       "step_flops": flops, "text_kv": "projected once, cached across denoise steps (the context "
@@ -416,18 +474,77 @@ def cpu_full_steps(threads: int, warmup: int, steps: int, budget_s: float) -> di
             "steps_timed": n, "step_s": sec, "timed_s": sum(times)}
 
 
+def cpu_one_block_sample(c, threads: int) -> dict:
+    """Configs 4 and 5 are too slow for a whole step on the CPU: the CPU oracle runs the
+    config's model with ONE block (patchify, adaLN, one block, head, and for config 5
+    X0 + CFG + Euler), timed once after a small warm-up, and the time is multiplied by
+    the number of blocks. Labelled extrapolated."""
+    import ltx_dit
+
+    from oracle import ltx_oracle
+
+    torch.set_num_threads(threads)
+    cfg = dit_config({**c, "num_layers": 1})
+    with torch.device("meta"):
+        shapes = [(n, tuple(p.shape)) for n, p in ltx_dit.LTXModel(cfg).named_parameters()]
+    g = torch.Generator().manual_seed(1)
+    w = {}
+    for name, shape in shapes:
+        x = torch.randn(shape, generator=g, dtype=torch.bfloat16).mul_(0.02)
+        if name.endswith(("q_norm.weight", "k_norm.weight")):
+            x.add_(1.0)
+        w[name] = x
+    t = c["f"] * c["h"] * c["w"]
+    lat = torch.randn(1, t, 128, generator=g).to(torch.bfloat16)
+    ctx = torch.randn(2, c["text"], c["cross_dim"], generator=g).to(torch.bfloat16)
+    pos = ltx_oracle.video_positions(1, c["f"], c["h"], c["w"], 24.0)
+    sig = torch.tensor([0.5, 0.25])
+
+    def run(tv_pos, tv_lat, tv_ctx):
+        with torch.inference_mode():
+            if c["kind"] == "av":
+                ta = c["audio_tokens"]
+                s2 = torch.full((2,), 0.5)
+                vid = ltx_oracle.Modality(latent=tv_lat.repeat(2, 1, 1), sigma=s2,
+                                          timesteps=torch.full((2, tv_lat.shape[1], 1), 0.5),
+                                          positions=tv_pos.repeat(2, 1, 1, 1), context=tv_ctx)
+                aud = ltx_oracle.Modality(latent=torch.randn(2, ta, 128, generator=g).to(torch.bfloat16), sigma=s2,
+                                          timesteps=torch.full((2, ta, 1), 0.5),
+                                          positions=ltx_oracle.audio_positions(2, ta),
+                                          context=torch.randn(2, c["audio_text"], c["audio_cross"],
+                                                              generator=g).to(torch.bfloat16))
+                ltx_oracle.forward(w, cfg, vid, aud)
+            else:
+                ltx_oracle.cfg_denoise_step(w, cfg, tv_lat, tv_pos, tv_ctx[:1], tv_ctx[1:], sig, 0, c["cfg_scale"])
+
+    run(pos[:, :, :256], lat[:, :256], ctx)  # warm-up on 256 tokens
+    t0 = time.perf_counter()
+    run(pos, lat, ctx)
+    sec = time.perf_counter() - t0
+    step_sec = sec * c["num_layers"]
+    return {"value": 2 * t / step_sec, "unit": UNIT, "cores": threads, "kind": "port", "extrapolated": True,
+            "sample": f"one-block model of this config (B=2, T={t}, bf16) on the CPU oracle: {sec:.2f} s, "
+                      f"multiplied by {c['num_layers']} blocks (extrapolated; patchify, adaLN and head counted "
+                      f"{c['num_layers']} times)"}
+
+
 def run_reference(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    cpu = cpu_full_steps(threads, args.warmup, args.steps, budget_s=90.0)
-    n, sec = cpu.pop("steps_timed"), cpu.pop("step_s")
-    cpu.pop("timed_s")
+    c = CONFIGS[args.config]
+    if args.config == 3:
+        cpu = cpu_full_steps(threads, args.warmup, args.steps, budget_s=90.0)
+        n, sec = cpu.pop("steps_timed"), cpu.pop("step_s")
+        cpu.pop("timed_s")
+    else:
+        cpu = cpu_one_block_sample(c, threads)
+        n, sec = 1, 2 * c["f"] * c["h"] * c["w"] / cpu["value"]
     v = cpu["value"]
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": n,
             "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": workload_config(),
+            "config": workload_config(c),
             "execution": {"parallelism": f"CPU, {threads} host threads (rank 0 only)", "cuda_graph": False,
                           "step_flops": step_flops(text_kv_cached=False),
                           "text_kv": "recomputed every step, as the reference does",
@@ -730,6 +847,9 @@ def main():
     ap.add_argument("--probe", choices=sorted(PROBES), default=None,
                     help="time one kernel of the step at its config-3 shape instead of the step")
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=3,
+                    help="BASELINE.json workload: 3 (default, the headline), 4 (audio-video, one GPU) or 5 "
+                         "(27588-token denoise loop)")
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -766,9 +886,12 @@ def main():
     try:
         line = run_ours(args, rank, world, dev)
         if line is not None and not args.no_cpu_baseline:
-            cb = cpu_full_steps(os.cpu_count() or 1, warmup=1, steps=1, budget_s=0.0)
-            for k in ("steps_timed", "step_s", "timed_s"):
-                cb.pop(k)
+            if args.config == 3:
+                cb = cpu_full_steps(os.cpu_count() or 1, warmup=1, steps=1, budget_s=0.0)
+                for k in ("steps_timed", "step_s", "timed_s"):
+                    cb.pop(k)
+            else:
+                cb = cpu_one_block_sample(CONFIGS[args.config], os.cpu_count() or 1)
             line["cpu_baseline"] = cb
         if line is not None:
             json_out.write(json.dumps(line) + "\n")

@@ -793,6 +793,51 @@ def cfg_denoise_step(model: LTXModel, latent: torch.Tensor, positions: torch.Ten
     return vel.view(2, t, c), den.view(1, t, c), nxt.view(1, t, c)
 
 
+@torch.inference_mode()
+def av_cfg_denoise_step(model: LTXModel, v_latent: torch.Tensor, a_latent: torch.Tensor, v_positions: torch.Tensor,
+                        a_positions: torch.Tensor, v_context_pos: torch.Tensor, v_context_neg: torch.Tensor,
+                        a_context_pos: torch.Tensor, a_context_neg: torch.Tensor, sigmas: torch.Tensor, idx: int,
+                        cfg_scale: float, v_keyframes_mask: torch.Tensor | None = None):
+    """One CFG denoise step of the audio-video model: the B = 2 [cond, uncond] forward of
+    both streams with A<->V attention in every block, then X0 + CFG + Euler per stream in
+    the proj_out epilogues (ltx_dit.py:565-606 with CFG-only guidance).
+
+    v_latent (1, Tv, C), a_latent (1, Ta, C), positions (1, 3, Tv, 2) / (1, 1, Ta, 2),
+    contexts (1, S, C_v) / (1, S_a, C_a). Returns (next video latent (1, Tv, C), next audio
+    latent (1, Ta, C))."""
+    dtype = model.proj_out.weight.dtype
+    dev = v_latent.device
+    sigma, sigma_next = _sigma_pair(sigmas, idx)
+    sig = torch.full((2,), sigma, device=dev, dtype=torch.float32)
+
+    def modality(lat, pos, cpos, cneg, kf):
+        t = lat.shape[1]
+        return Modality(latent=lat.to(dtype).expand(2, -1, -1), sigma=sig,
+                        timesteps=torch.full((2, t, 1), sigma, device=dev, dtype=torch.float32),
+                        positions=pos.expand(2, -1, -1, -1), context=torch.cat([cpos, cneg], dim=0).to(dtype),
+                        keyframes_mask=kf.expand(2, -1, -1) if kf is not None else None)
+
+    video = modality(v_latent, v_positions, v_context_pos, v_context_neg, v_keyframes_mask)
+    audio = modality(a_latent, a_positions, a_context_pos, a_context_neg, None)
+    va, aa = model.prepare(video, audio, uniform_timesteps=True)
+    model.run_blocks(va, aa)
+    outs = []
+    for st, lat, proj in ((va, v_latent, model.proj_out), (aa, a_latent, model.audio_proj_out)):
+        h = model.head_hidden(st)
+        t, c = lat.shape[1], lat.shape[2]
+        lat2 = lat.to(dtype).reshape(t, c).contiguous()
+        ts2 = torch.full((2, t), sigma, device=dev, dtype=torch.float32)
+        nxt = torch.empty(t, c, device=dev, dtype=dtype)
+        if dtype == torch.bfloat16:
+            nat.proj_out_cfg_euler(h, proj.weight, proj.bias, lat2, ts2, cfg_scale, sigma, sigma_next, nxt)
+        else:
+            vel = torch.empty(2 * t, c, device=dev, dtype=dtype)
+            nat.linear(h, proj.weight, vel, nat.epilogue(bias=proj.bias))
+            nat.cfg_euler(vel, lat2, ts2, cfg_scale, sigma, sigma_next, nxt)
+        outs.append(nxt.view(1, t, c))
+    return outs[0], outs[1]
+
+
 class NativeStep:
     """cfg_denoise_step through the library's whole-step C entry point (ltx_dit_step):
     the path a C or C++ caller takes without Python. It owns an ltx_ctx (TMA descriptor

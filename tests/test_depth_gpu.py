@@ -87,7 +87,19 @@ def _oracle_runs(host, run):
     return ref_cpu, ref_gpu, truth
 
 
-def _cfg_step_vs_oracle(cfg, f, h, w, text, cross_dim, seed, label):
+def _time_ms(fn, reps=3):
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def _cfg_step_vs_oracle(cfg, f, h, w, text, cross_dim, seed, label, time_both=False):
     model, host = philox_model(cfg, seed)
     t = f * h * w
     g = torch.Generator().manual_seed(seed + 100)
@@ -97,11 +109,13 @@ def _cfg_step_vs_oracle(cfg, f, h, w, text, cross_dim, seed, label):
     kf = torch.zeros(1, t, 1)
     kf[:, : h * w] = 1.0
     sigmas = torch.tensor([0.5, 0.25])
-    ours = ltx_dit.cfg_denoise_step(model, latent.to(DEV), pos.to(DEV), ctx[:1].to(DEV), ctx[1:].to(DEV), sigmas, 0,
-                                    3.0, keyframes_mask=kf.to(DEV))
+    args = (latent.to(DEV), pos.to(DEV), ctx[:1].to(DEV), ctx[1:].to(DEV), sigmas, 0, 3.0)
+    ours = ltx_dit.cfg_denoise_step(model, *args, keyframes_mask=kf.to(DEV))
     torch.cuda.synchronize()
     assert nat.device_error_flags() == 0
     ours = [o.cpu() for o in ours]
+    t_native = _time_ms(lambda: ltx_dit.cfg_denoise_step(model, *args, keyframes_mask=kf.to(DEV))) \
+        if time_both else None
     del model
     torch.cuda.empty_cache()
 
@@ -112,13 +126,21 @@ def _cfg_step_vs_oracle(cfg, f, h, w, text, cross_dim, seed, label):
 
     ref_cpu, ref_gpu, truth = _oracle_runs(host, run)
     _check(label, ["velocity", "denoised", "next latent"], ours, ref_cpu, ref_gpu, truth)
+    if time_both:
+        # the GPU bar: the reference's module (restated op for op) on cuBLAS + cuDNN SDPA,
+        # eager, against the native step, eager (no CUDA graph on either side)
+        wdev = _dev_weights(host, torch.bfloat16)
+        t_ref = _time_ms(lambda: run(wdev, DEV, torch.bfloat16))
+        print(f"  step time on this B200 (eager): native {t_native:.1f} ms, reference module on cuBLAS/cuDNN "
+              f"{t_ref:.1f} ms ({t_ref / t_native:.2f}x)")
+        assert t_native < t_ref
 
 
 def test_config3_all_28_blocks_cfg_step_matches_oracle():
     """BASELINE config 3 exactly as benchmarked: 28 blocks, D=2048, 32x64, FFN 8192,
     T=6144, text 128x4096, sigma 0.5 -> 0.25, CFG 3, keyframe mask on the first frame."""
     cfg = ltx_dit.DiTConfig.video_only(num_layers=28, heads=32, head_dim=64, cross_dim=4096)
-    _cfg_step_vs_oracle(cfg, 16, 16, 24, 128, 4096, seed=11, label="config 3, 28 blocks, T=6144")
+    _cfg_step_vs_oracle(cfg, 16, 16, 24, 128, 4096, seed=11, label="config 3, 28 blocks, T=6144", time_both=True)
 
 
 def test_config5_tokens_two_blocks_cfg_step_matches_oracle():
@@ -160,8 +182,15 @@ def test_config4_full_width_av_eight_blocks_matches_oracle():
                    ltx_dit.Modality(**{k: v.to(DEV) for k, v in aud.items()}), None)
     v_next = native_next(vid["latent"], vx, vid["timesteps"])
     a_next = native_next(aud["latent"], ax, aud["timesteps"])
+    # the fused audio-video step (X0 + CFG + Euler in both heads' proj_out epilogues) is
+    # the same arithmetic: identical next latents
+    fv, fa = ltx_dit.av_cfg_denoise_step(model, v_lat.to(DEV), a_lat.to(DEV), vid["positions"][:1].to(DEV),
+                                         aud["positions"][:1].to(DEV), vid["context"][:1].to(DEV),
+                                         vid["context"][1:].to(DEV), aud["context"][:1].to(DEV),
+                                         aud["context"][1:].to(DEV), sigmas, 0, 3.0)
     torch.cuda.synchronize()
     assert nat.device_error_flags() == 0
+    assert torch.equal(fv, v_next) and torch.equal(fa, a_next)
     ours = [vx.cpu(), ax.cpu(), v_next.cpu(), a_next.cpu()]
     del model
     torch.cuda.empty_cache()
