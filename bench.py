@@ -225,14 +225,22 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
     cpos, cneg = inp["ctx"][:1], inp["ctx"][1:]
     n_sig = len(sigmas) - 1
     if c["kind"] == "av":
-        if world > 1:
-            raise SystemExit("config 4 runs on one GPU (the audio stream is not sharded)")
-        layout = None
         a_lat, a_pos, a_ctx = inp["a_latent"], inp["a_pos"], inp["a_ctx"]
+        if world > 1:
+            import ltx_parallel
 
-        def step(lat, idx=0):
-            return ltx_dit.av_cfg_denoise_step(model, lat, a_lat, pos, a_pos, cpos, cneg, a_ctx[:1], a_ctx[1:],
-                                               sigmas, idx % n_sig, c["cfg_scale"], v_keyframes_mask=kf)[0]
+            pdn = ltx_parallel.ParallelDenoiser(model)
+            layout = pdn.layout
+
+            def step(lat, idx=0):
+                return pdn.step_av(lat, a_lat, pos, a_pos, cpos, cneg, a_ctx[:1], a_ctx[1:], sigmas, idx % n_sig,
+                                   c["cfg_scale"], v_keyframes_mask=kf)[0]
+        else:
+            layout = None
+
+            def step(lat, idx=0):
+                return ltx_dit.av_cfg_denoise_step(model, lat, a_lat, pos, a_pos, cpos, cneg, a_ctx[:1], a_ctx[1:],
+                                                   sigmas, idx % n_sig, c["cfg_scale"], v_keyframes_mask=kf)[0]
     elif world > 1:
         import ltx_parallel
 

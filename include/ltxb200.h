@@ -263,6 +263,24 @@ int ltx_sp_pack(const void* src, int64_t ld_src, int64_t rows, int parts, int n_
 int ltx_sp_unpack(const void* src, int64_t rows, int parts, int w, void* dst, int64_t ld_dst, int dtype,
                   void* stream);
 
+/* Split-KV attention across ranks (the audio queries of the video-to-audio attention,
+ * ltx_dit.py:299-307, against video keys sharded by sequence parallelism). No counterpart
+ * in the reference, which attends over all keys on one GPU (ltx_nn.py:227).
+ * ltx_attention_partial: softmax(Q K^T * scale) V over this part of the keys, bf16
+ * inputs as ltx_attention (head_dim 64 or 128), no gate; writes o_part (B*Tq, ldo) fp32 =
+ * O / l and lse (B*Tq, ld_lse) fp32 = log2(sum_j 2^(s_j * scale * log2(e))) per head. */
+int ltx_attention_partial(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                          float* o_part, int64_t ldo, float* lse, int64_t ld_lse, int B, int64_t Tq, int64_t Tk,
+                          int heads, int head_dim, float scale, void* stream);
+/* Merge of `parts` partials into the attention over all keys: o_parts (parts, rows,
+ * heads*head_dim) and lse_parts (parts, rows, heads) contiguous fp32 (what an all-gather
+ * of ltx_attention_partial outputs holds); out (rows, ldo) bf16 = the merged output with
+ * the gate 2*sigmoid(logit) of gate_logits (rows, ld_gate) applied as ltx_attention does
+ * (NULL: no gate). */
+int ltx_attention_merge(const float* o_parts, const float* lse_parts, int parts, int64_t rows, int heads,
+                        int head_dim, const void* gate_logits, int64_t ld_gate, void* out, int64_t ldo,
+                        void* stream);
+
 /* ---------------------------------------------------------------------------------- */
 /* Video VAE decoder (ConvVideoDecoder, ltx_vae.py:167-222). Activations are           */
 /* channels-last (B, F, H, W, C) bf16; the reference's tensors are (B, C, F, H, W).    */

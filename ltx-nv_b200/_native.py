@@ -189,6 +189,11 @@ _SIGNATURES = {
     "ltx_proj_out_cfg_euler": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, ctypes.c_int, c_i64, c_vp, c_vp,
                                               ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp,
                                               ctypes.c_int, c_vp]),
+    "ltx_attention_partial": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                             ctypes.c_int, c_i64, c_i64, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                             c_vp]),
+    "ltx_attention_merge": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int, c_i64, ctypes.c_int, ctypes.c_int, c_vp, c_i64,
+                                           c_vp, c_i64, c_vp]),
     "ltx_ctx_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(c_vp)]),
     "ltx_ctx_destroy": (ctypes.c_int, [c_vp]),
     "ltx_dit_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(DitConfig), c_i64, c_i64]),
@@ -452,6 +457,29 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor
     _call("ltx_attention", _ptr(q), _ld(q), _ptr(k), _ld(k), _ptr(v), _ld(v), _ptr(o), _ld(o), batch, tq, tk, heads,
           head_dim, scale, _ptr(gate_logits), _ld(gate_logits) if gate_logits is not None else 0, _dt(q), _stream(q),
           label=f"attention B={batch} H={heads} Tq={tq} Tk={tk} d={head_dim}" if _profile is not None else None)
+
+
+def attention_partial(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o_part: torch.Tensor, lse: torch.Tensor,
+                      batch: int, tq: int, tk: int, heads: int, head_dim: int, scale: float) -> None:
+    """Split-KV partial attention: o_part (B*Tq, >=H*d) fp32 = O / l over these keys,
+    lse (B*Tq, >=H) fp32 = log2-sum-exp of the scaled scores (q/k/v bf16 row-major views)."""
+    if o_part.dtype != torch.float32 or lse.dtype != torch.float32:
+        raise TypeError("o_part and lse must be float32")
+    _call("ltx_attention_partial", _ptr(q), _ld(q), _ptr(k), _ld(k), _ptr(v), _ld(v), _ptr(o_part), _ld(o_part),
+          _ptr(lse), _ld(lse), batch, tq, tk, heads, head_dim, scale, _stream(q),
+          label=f"attention_partial B={batch} H={heads} Tq={tq} Tk={tk} d={head_dim}" if _profile is not None else None)
+
+
+def attention_merge(o_parts: torch.Tensor, lse_parts: torch.Tensor, gate_logits: torch.Tensor | None,
+                    out: torch.Tensor, heads: int, head_dim: int) -> None:
+    """out (rows, >=H*d) bf16 = merge of o_parts (R, rows, H*d) / lse_parts (R, rows, H) fp32
+    (contiguous) with the gate 2*sigmoid(logit) applied."""
+    r, rows = o_parts.shape[0], o_parts.shape[1]
+    if not (o_parts.is_contiguous() and lse_parts.is_contiguous()) or o_parts.shape[2] != heads * head_dim \
+            or tuple(lse_parts.shape) != (r, rows, heads):
+        raise ValueError("o_parts (R, rows, H*d) and lse_parts (R, rows, H) must be contiguous")
+    _call("ltx_attention_merge", _ptr(o_parts), _ptr(lse_parts), r, rows, heads, head_dim, _ptr(gate_logits),
+          _ld(gate_logits) if gate_logits is not None else 0, _ptr(out), _ld(out), _stream(out))
 
 
 def cfg_euler(vel: torch.Tensor, latent: torch.Tensor, timesteps: torch.Tensor, cfg_scale: float, sigma: float,

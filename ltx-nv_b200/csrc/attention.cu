@@ -66,7 +66,8 @@ template <int D>
 __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
     fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
-                   int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate) {
+                   int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
+                   float* __restrict__ o32, float* __restrict__ lse, int64_t ld_lse) {
   using Cfg = FaCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = fa_align1024(smem_raw);
@@ -401,27 +402,48 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
       const float inv_l = 1.f / l_run;
       float g = 1.f;
       const int64_t orow = int64_t(b) * Tq + qi;
-      if (gate != nullptr && qi < Tq) {
-        const float lg = __bfloat162float(gate[orow * ld_gate + h]);
-        const float sg = round_bf16(1.f / (1.f + expf(-lg)));
-        g = round_bf16(2.f * sg);
-      }
-      __nv_bfloat16* op = O + orow * ldo + int64_t(h) * D;
+      if (o32 != nullptr) {
+        // partial attention over a part of the keys (split-KV): fp32 O / l and the
+        // row's log2-sum-exp of the scaled scores, log2(sum_j 2^(s_j * scale * log2 e)),
+        // for a later merge; no gate
+        float* op32 = o32 + orow * ldo + int64_t(h) * D;
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t rr[32];
-        tmem_ld32(o_tmem + uint32_t(c0), rr);
-        tmem_wait_ld();
-        if (qi < Tq) {
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t rr[32];
+          tmem_ld32(o_tmem + uint32_t(c0), rr);
+          tmem_wait_ld();
+          if (qi < Tq) {
 #pragma unroll
-          for (int e8 = 0; e8 < 32; e8 += 8) {
-            float v[8];
+            for (int e4 = 0; e4 < 32; e4 += 4)
+              *reinterpret_cast<float4*>(op32 + c0 + e4) =
+                  make_float4(__uint_as_float(rr[e4]) * inv_l, __uint_as_float(rr[e4 + 1]) * inv_l,
+                              __uint_as_float(rr[e4 + 2]) * inv_l, __uint_as_float(rr[e4 + 3]) * inv_l);
+          }
+        }
+        if (qi < Tq) lse[orow * ld_lse + h] = m_ref + log2f(l_run);
+      } else {
+        if (gate != nullptr && qi < Tq) {
+          const float lg = __bfloat162float(gate[orow * ld_gate + h]);
+          const float sg = round_bf16(1.f / (1.f + expf(-lg)));
+          g = round_bf16(2.f * sg);
+        }
+        __nv_bfloat16* op = O + orow * ldo + int64_t(h) * D;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float o = round_bf16(__uint_as_float(rr[e8 + e]) * inv_l);
-              v[e] = gate != nullptr ? o * g : o;
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t rr[32];
+          tmem_ld32(o_tmem + uint32_t(c0), rr);
+          tmem_wait_ld();
+          if (qi < Tq) {
+#pragma unroll
+            for (int e8 = 0; e8 < 32; e8 += 8) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float o = round_bf16(__uint_as_float(rr[e8 + e]) * inv_l);
+                v[e] = gate != nullptr ? o * g : o;
+              }
+              st8<__nv_bfloat16>(op + c0 + e8, v);
             }
-            st8<__nv_bfloat16>(op + c0 + e8, v);
           }
         }
       }
@@ -743,7 +765,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const float* __restrict_
 template <int D>
 void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
                     int64_t ldo, int B, int64_t Tq, int64_t Tk, int H, float scale, const void* gate,
-                    int64_t ld_gate, cudaStream_t s) {
+                    int64_t ld_gate, cudaStream_t s, float* o32 = nullptr, float* lse = nullptr,
+                    int64_t ld_lse = 0) {
   using Cfg = FaCfg<D>;
   const uint64_t cols = uint64_t(H) * D;
   const CUtensorMap tq = make_tmap_bf16_2d(q, cols, uint64_t(B) * Tq, uint64_t(ldq), 64, 128);
@@ -754,8 +777,10 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   ensure_smem_limit(smem_done, kern, Cfg::SMEM);
   dim3 grid(unsigned((Tq + 2 * Cfg::BM - 1) / (2 * Cfg::BM)), unsigned(H), unsigned(B));
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), scale_log2,
-                                    static_cast<const __nv_bfloat16*>(gate), ld_gate), ltx::note_launch();
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk),
+                                             scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate, o32, lse,
+                                             ld_lse),
+      ltx::note_launch();
 }
 
 template <int D>

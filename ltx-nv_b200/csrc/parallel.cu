@@ -70,3 +70,108 @@ extern "C" int ltx_sp_unpack(const void* src, int64_t rows, int parts, int w, vo
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
+
+// ---------------------------------------------------------------------------------
+// Split-KV attention across ranks (the video-to-audio attention under sequence
+// parallelism: the audio queries attend to video keys that are sharded over the ranks).
+// Each rank computes a partial attention over its keys (fp32 O / l and the log2-sum-exp
+// of the scaled scores per (row, head)); after an all-gather every rank merges the R
+// partials exactly as one softmax over all keys would weigh them:
+//   M = max_r lse_r,  w_r = 2^(lse_r - M),  O = sum_r w_r O_r / sum_r w_r,
+// then applies the output gate 2 * sigmoid(logit) with the roundings of the fused
+// attention epilogue.
+// ---------------------------------------------------------------------------------
+namespace ltx {
+namespace detail {
+
+// One thread per (row, head, 8-column group).
+__global__ void attn_merge_kernel(const float* __restrict__ o_parts, const float* __restrict__ lse_parts, int R,
+                                  int64_t rows, int H, int D, const __nv_bfloat16* __restrict__ gate,
+                                  int64_t ld_gate, __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int g8 = D / 8;
+  const int64_t total = rows * H * g8;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int c8 = int(i % g8);
+    const int64_t rh = i / g8;
+    const int h = int(rh % H);
+    const int64_t r = rh / H;
+    float m = -INFINITY;
+    for (int p = 0; p < R; ++p) m = fmaxf(m, lse_parts[(int64_t(p) * rows + r) * H + h]);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}, wsum = 0.f;
+    for (int p = 0; p < R; ++p) {
+      const float w = exp2f(lse_parts[(int64_t(p) * rows + r) * H + h] - m);
+      const float* src = o_parts + (int64_t(p) * rows + r) * (int64_t(H) * D) + int64_t(h) * D + c8 * 8;
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 b = *reinterpret_cast<const float4*>(src + 4);
+      acc[0] += w * a.x, acc[1] += w * a.y, acc[2] += w * a.z, acc[3] += w * a.w;
+      acc[4] += w * b.x, acc[5] += w * b.y, acc[6] += w * b.z, acc[7] += w * b.w;
+      wsum += w;
+    }
+    float g = 1.f;
+    if (gate != nullptr) {
+      const float sg = round_bf16(1.f / (1.f + expf(-__bfloat162float(gate[r * ld_gate + h]))));
+      g = round_bf16(2.f * sg);
+    }
+    const float inv = 1.f / wsum;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float o = round_bf16(acc[e] * inv);
+      v[e] = gate != nullptr ? o * g : o;
+    }
+    st8<__nv_bfloat16>(out + r * ldo + int64_t(h) * D + c8 * 8, v);
+  }
+}
+
+}  // namespace detail
+}  // namespace ltx
+
+extern "C" int ltx_attention_partial(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                                     float* o_part, int64_t ldo, float* lse, int64_t ld_lse, int B, int64_t Tq,
+                                     int64_t Tk, int heads, int head_dim, float scale, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(q && k && v && o_part && lse, "NULL argument");
+  LTX_REQUIRE(B > 0 && Tq > 0 && Tk > 0 && heads > 0, "B, Tq, Tk and heads must be positive");
+  LTX_REQUIRE(int64_t(B) * Tq < (int64_t(1) << 31) && int64_t(B) * Tk < (int64_t(1) << 31), "too many rows");
+  LTX_UNSUPPORTED(head_dim == 64 || head_dim == 128, "partial attention supports head_dim 64 and 128 (bf16)");
+  const int64_t inner = int64_t(heads) * head_dim;
+  LTX_REQUIRE(ldq >= inner && ldk >= inner && ldv >= inner && ldo >= inner, "leading dimensions too small");
+  LTX_REQUIRE(ld_lse >= heads, "ld_lse must be >= heads");
+  LTX_REQUIRE(ldq % 8 == 0 && ldk % 8 == 0 && ldv % 8 == 0 && ldo % 4 == 0,
+              "leading dims must be multiples of 8 (q, k, v) and 4 (o_part)");
+  check_vec_ptr(q, "q");
+  check_vec_ptr(k, "k");
+  check_vec_ptr(v, "v");
+  check_vec_ptr(o_part, "o_part");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (head_dim == 64)
+    launch_fmha_tc<64>(q, ldq, k, ldk, v, ldv, nullptr, ldo, B, Tq, Tk, heads, scale, nullptr, 0, s, o_part, lse,
+                       ld_lse);
+  else
+    launch_fmha_tc<128>(q, ldq, k, ldk, v, ldv, nullptr, ldo, B, Tq, Tk, heads, scale, nullptr, 0, s, o_part, lse,
+                        ld_lse);
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_attention_merge(const float* o_parts, const float* lse_parts, int parts, int64_t rows, int heads,
+                                   int head_dim, const void* gate_logits, int64_t ld_gate, void* out, int64_t ldo,
+                                   void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(o_parts && lse_parts && out, "NULL argument");
+  LTX_REQUIRE(parts > 0 && rows > 0 && heads > 0 && head_dim > 0 && head_dim % 8 == 0, "bad sizes");
+  LTX_REQUIRE(ldo >= int64_t(heads) * head_dim && ldo % 8 == 0, "ldo too small or not a multiple of 8");
+  if (gate_logits) LTX_REQUIRE(ld_gate >= heads, "ld_gate must be >= heads");
+  check_vec_ptr(o_parts, "o_parts");
+  check_vec_ptr(out, "out");
+  const int64_t total = rows * heads * (head_dim / 8);
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = int64_t(num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  attn_merge_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      o_parts, lse_parts, parts, rows, heads, head_dim, static_cast<const __nv_bfloat16*>(gate_logits), ld_gate,
+      static_cast<__nv_bfloat16*>(out), ldo),
+      ltx::note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}

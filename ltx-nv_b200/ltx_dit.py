@@ -472,8 +472,14 @@ class LTXModel(torch.nn.Module):
         kv = torch.empty(kv_in.shape[0], wkv.shape[0], device=q_in.device, dtype=q_in.dtype)
         nat.linear(kv_in, wkv, kv, nat.epilogue(bias=bkv))
         attn._norm_rope(kv[:, :inner], kv_st.T, attn.k_norm.weight, k_pe)
-        o = attn.attend(qg[:, :inner], kv[:, :inner], kv[:, inner:2 * inner], qg[:, inner:] if gated else None,
-                        q_st.B, q_st.T, kv_st.T)
+        if self._sp is not None and kv_st.name == "video":
+            # video-to-audio under sequence parallelism: the video keys are sharded over
+            # the ranks, the audio queries are replicated -> split-KV attention merged
+            # across the ranks (ltx_parallel)
+            o = self._sp.split_kv_attention(attn, qg, kv, q_st.B, q_st.T, kv_st.T, gated)
+        else:
+            o = attn.attend(qg[:, :inner], kv[:, :inner], kv[:, inner:2 * inner], qg[:, inner:] if gated else None,
+                            q_st.B, q_st.T, kv_st.T)
         runs, b = [], 0
         kept = keep if keep is not None else [1.0] * out_st.B
         while b < out_st.B:

@@ -16,6 +16,11 @@ the next latent's shards inside each SP group, so every rank holds the full next
 Each rank runs the same kernels on the same rows as the single-GPU step, so the result
 equals the single-GPU result.
 
+The audio-video model (step_av) keeps the audio stream (126 tokens) replicated on every
+rank of a CFG group: audio-to-video attention reads the full audio keys locally, and
+video-to-audio attention runs over the sharded video keys as split-KV partial attentions
+(fp32 O / l and log2-sum-exp per row and head) merged after an all_gather.
+
 No remote memory is read by any kernel: NCCL moves every byte into local HBM first.
 """
 
@@ -117,6 +122,30 @@ class SequenceParallel:
             nat.sp_unpack(back.view(p, rows, dp), p, o[b * rows:(b + 1) * rows])
         return o
 
+    def split_kv_attention(self, attn, qg: torch.Tensor, kv: torch.Tensor, batch: int, tq: int, tk_local: int,
+                           gated: bool) -> torch.Tensor:
+        """Attention of replicated queries qg (B*Tq, >= H*d (+H gate logits)) over keys and
+        values sharded over the SP group (kv (B*Tk_local, 2*H*d) on each rank): partial
+        attention over the local keys (fp32 O / l and log2-sum-exp per row and head), an
+        all_gather of the partials, and the exact softmax merge with the gate applied.
+        Every rank ends with the same (B*Tq, H*d) output."""
+        heads, d = attn.heads, attn.dim_head
+        inner = heads * d
+        rows = batch * tq
+        dev = qg.device
+        o_part = torch.empty(rows, inner, device=dev, dtype=torch.float32)
+        lse = torch.empty(rows, heads, device=dev, dtype=torch.float32)
+        nat.attention_partial(qg[:, :inner], kv[:, :inner], kv[:, inner:2 * inner], o_part, lse, batch, tq, tk_local,
+                              heads, d, d ** -0.5)
+        o_all = torch.empty(self.size * rows, inner, device=dev, dtype=torch.float32)
+        lse_all = torch.empty(self.size * rows, heads, device=dev, dtype=torch.float32)
+        dist.all_gather_into_tensor(o_all, o_part, group=self.group)
+        dist.all_gather_into_tensor(lse_all, lse, group=self.group)
+        o = torch.empty(rows, inner, device=dev, dtype=qg.dtype)
+        nat.attention_merge(o_all.view(self.size, rows, inner), lse_all.view(self.size, rows, heads),
+                            qg[:, inner:inner + heads] if gated else None, o, heads, d)
+        return o
+
 
 class ParallelDenoiser:
     """CFG x SP execution of ltx_dit.cfg_denoise_step across the default process group."""
@@ -177,3 +206,64 @@ class ParallelDenoiser:
         nxt = torch.empty(t, c, device=dev, dtype=dtype)
         dist.all_gather_into_tensor(nxt, nxt_l, group=self.sp_group)
         return nxt.view(1, t, c)
+
+    @torch.inference_mode()
+    def step_av(self, v_latent: torch.Tensor, a_latent: torch.Tensor, v_positions: torch.Tensor,
+                a_positions: torch.Tensor, v_context_pos: torch.Tensor, v_context_neg: torch.Tensor,
+                a_context_pos: torch.Tensor, a_context_neg: torch.Tensor, sigmas: torch.Tensor, idx: int,
+                cfg_scale: float, v_keyframes_mask: torch.Tensor | None = None):
+        """ltx_dit.av_cfg_denoise_step across the process group: the video tokens are
+        sharded over the SP ranks as in step(); the audio stream (126 tokens) is
+        replicated on every rank of a CFG group, audio-to-video attention reads the full
+        audio keys locally, and video-to-audio attention merges partial attentions over the
+        sharded video keys (SequenceParallel.split_kv_attention). Returns the next video
+        latent (1, Tv, C) and the next audio latent (1, Ta, C) on every rank."""
+        lay, model = self.layout, self.model
+        dtype = model.proj_out.weight.dtype
+        dev = v_latent.device
+        _, tv, c = v_latent.shape
+        ta = a_latent.shape[1]
+        t0, t1 = lay.tokens(tv)
+        tl = t1 - t0
+        sigma, sigma_next = ltx_dit._sigma_pair(sigmas, idx)
+        nb = 1 if lay.cfg == 2 else 2
+
+        def ctx_of(cpos, cneg):
+            if lay.cfg == 2:
+                return (cpos if lay.sample == 0 else cneg).to(dtype)
+            return torch.cat([cpos, cneg], dim=0).to(dtype)
+
+        sig = torch.full((nb,), sigma, device=dev)
+        vlat_l = v_latent[:, t0:t1].to(dtype)
+        video = ltx_dit.Modality(
+            latent=vlat_l.expand(nb, -1, -1), sigma=sig, timesteps=torch.full((nb, tl, 1), sigma, device=dev),
+            positions=v_positions[:, :, t0:t1].expand(nb, -1, -1, -1), context=ctx_of(v_context_pos, v_context_neg),
+            keyframes_mask=v_keyframes_mask[:, t0:t1].expand(nb, -1, -1) if v_keyframes_mask is not None else None)
+        alat = a_latent.to(dtype)
+        audio = ltx_dit.Modality(latent=alat.expand(nb, -1, -1), sigma=sig,
+                                 timesteps=torch.full((nb, ta, 1), sigma, device=dev),
+                                 positions=a_positions.expand(nb, -1, -1, -1),
+                                 context=ctx_of(a_context_pos, a_context_neg))
+        va, aa = model.prepare(video, audio, uniform_timesteps=True)
+        model.run_blocks(va, aa)
+        outs = []
+        for st, lat2, proj, rows, group_gather in ((va, vlat_l.reshape(tl, c), model.proj_out, tl, True),
+                                                   (aa, alat.reshape(ta, c), model.audio_proj_out, ta, False)):
+            h = model.head_hidden(st)
+            vel_l = torch.empty(nb * rows, c, device=dev, dtype=dtype)
+            nat.linear(h, proj.weight, vel_l, nat.epilogue(bias=proj.bias))
+            if lay.cfg == 2:
+                vel = torch.empty(2 * rows, c, device=dev, dtype=dtype)
+                dist.all_gather_into_tensor(vel, vel_l, group=self.cfg_group)
+            else:
+                vel = vel_l
+            ts = torch.full((2, rows), sigma, device=dev, dtype=torch.float32)
+            nxt_l = torch.empty(rows, c, device=dev, dtype=dtype)
+            nat.cfg_euler(vel, lat2.contiguous(), ts, cfg_scale, sigma, sigma_next, nxt_l)
+            if group_gather and lay.sp > 1:
+                nxt = torch.empty(tv, c, device=dev, dtype=dtype)
+                dist.all_gather_into_tensor(nxt, nxt_l, group=self.sp_group)
+                outs.append(nxt.view(1, tv, c))
+            else:
+                outs.append(nxt_l.view(1, rows, c))
+        return outs[0], outs[1]

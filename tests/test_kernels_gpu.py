@@ -528,3 +528,41 @@ def test_proj_out_cfg_euler_bf16(t, k):
     nxt2 = torch.empty_like(den)
     nat.cfg_euler(vel, lat, ts, 3.0, 0.75, 0.625, nxt2, den2)
     assert torch.equal(den, den2) and torch.equal(nxt, nxt2)
+
+
+@pytest.mark.parametrize("hd,parts,tk", [(64, 2, 6144), (64, 4, 6144), (128, 4, 1536)])
+def test_split_kv_attention_merge_matches_full_attention(hd, parts, tk):
+    """Split-KV attention as the video-to-audio attention runs under sequence
+    parallelism: the keys cut into `parts` contiguous shards (one per rank), a partial
+    attention per shard (fp32 O / l and log2-sum-exp), then the merge with the gate.
+    Against the single-pass attention over all keys and against fp32 SDPA."""
+    torch.manual_seed(3)
+    heads, tq = 32, 126
+    d = heads * hd
+    q = torch.randn(tq, d + heads, device=DEV).to(torch.bfloat16)
+    kv = torch.randn(tk, 2 * d, device=DEV).to(torch.bfloat16)
+    full = torch.empty(tq, d, device=DEV, dtype=torch.bfloat16)
+    nat.attention(q[:, :d], kv[:, :d], kv[:, d:], full, 1, tq, tk, heads, hd, hd ** -0.5, q[:, d:])
+    sl = tk // parts
+    o_all = torch.empty(parts, tq, d, device=DEV)
+    lse_all = torch.empty(parts, tq, heads, device=DEV)
+    for r in range(parts):
+        shard = kv[r * sl:(r + 1) * sl]
+        nat.attention_partial(q[:, :d], shard[:, :d], shard[:, d:], o_all[r], lse_all[r], 1, tq, sl, heads, hd,
+                              hd ** -0.5)
+    merged = torch.empty(tq, d, device=DEV, dtype=torch.bfloat16)
+    nat.attention_merge(o_all, lse_all, q[:, d:], merged, heads, hd)
+    torch.cuda.synchronize()
+    assert nat.device_error_flags() == 0
+    q4 = q[:, :d].float().view(tq, heads, hd).transpose(0, 1)
+    k4 = kv[:, :d].float().view(tk, heads, hd).transpose(0, 1)
+    v4 = kv[:, d:].float().view(tk, heads, hd).transpose(0, 1)
+    ref = torch.nn.functional.scaled_dot_product_attention(q4, k4, v4).transpose(0, 1)
+    ref = (ref * (2 * torch.sigmoid(q[:, d:].float()))[..., None]).reshape(tq, d)
+    e_full, e_merged = rel_l2(full, ref), rel_l2(merged, ref)
+    assert e_merged < 1e-2 and e_merged < 1.5 * e_full + 1e-3, (e_merged, e_full)
+    assert rel_l2(merged, full) < 1e-2
+    # the partial log-sum-exp is the natural one over the scaled scores, in log2 units
+    s = torch.einsum("hqd,hkd->hqk", q4, k4[:, :sl]) * hd ** -0.5
+    lse_ref = torch.logsumexp(s, dim=-1).transpose(0, 1) / math.log(2.0)
+    assert torch.allclose(lse_all[0], lse_ref, atol=2e-2, rtol=1e-3)

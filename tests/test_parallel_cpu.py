@@ -4,6 +4,7 @@ unpack semantics of ltx_sp_pack / ltx_sp_unpack (include/ltxb200.h) are restated
 in torch so the exchange can run without a GPU; attention over the exchanged buffers
 must equal attention over the full sequence."""
 
+import math
 import os
 import socket
 
@@ -95,6 +96,59 @@ def test_ulysses_exchange_equals_full_attention_gloo(world):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(err < 1e-5 for _, err in res), res
+
+
+def merge_ref(o_all, lse_all):
+    """The merge of ltx_attention_merge (without the gate): weights 2^(lse_r - max)."""
+    m = lse_all.max(dim=0, keepdim=True).values
+    w = torch.exp2(lse_all - m)  # (R, rows, H)
+    num = (o_all.view(*lse_all.shape, -1) * w[..., None]).sum(0)
+    return num / w.sum(0)[..., None]
+
+
+def _split_kv_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.manual_seed(1)
+        heads, d, tq, tk = 4, 16, 10, 12 * world
+        scale = d ** -0.5
+        qh = torch.randn(heads, tq, d)  # replicated audio queries
+        kf, vf = torch.randn(heads, tk, d), torch.randn(heads, tk, d)  # all video keys
+        lay = Layout.make(world, rank, cfg=1)
+        t0, t1 = lay.tokens(tk)
+        k, v = kf[:, t0:t1], vf[:, t0:t1]  # this rank's shard
+        s = torch.einsum("hqd,hkd->hqk", qh, k) * scale
+        o_part = torch.softmax(s, dim=-1) @ v  # O / l over the local keys
+        lse = torch.logsumexp(s, dim=-1) / math.log(2.0)  # log2-sum-exp
+        o_all = torch.empty(world * heads, tq, d)
+        lse_all = torch.empty(world * heads, tq)
+        dist.all_gather_into_tensor(o_all, o_part.contiguous())
+        dist.all_gather_into_tensor(lse_all, lse.contiguous())
+        o_all, lse_all = o_all.view(world, heads, tq, d), lse_all.view(world, heads, tq)
+        merged = merge_ref(o_all.permute(0, 2, 1, 3).reshape(world, tq, heads * d), lse_all.permute(0, 2, 1))
+        ref = F.scaled_dot_product_attention(qh, kf, vf).transpose(0, 1)
+        q.put((rank, float((merged - ref).abs().max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_split_kv_merge_equals_full_attention_gloo(world):
+    """Video-to-audio attention under sequence parallelism: each rank attends the
+    replicated audio queries to its shard of the video keys, the (O / l, log2-sum-exp)
+    partials are all-gathered and merged; every rank must get the attention over all keys."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_split_kv_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(world)]

@@ -84,3 +84,84 @@ def test_parallel_step_equals_single_gpu(world, cfg_split):
         p.join(timeout=120)
         assert p.exitcode == 0
     assert all(d == 0.0 for _, d, _, _ in res), res
+
+
+def _av_worker(rank, world, port, cfg_split, q):
+    import sys
+    from datetime import timedelta
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    for p in (str(root), str(root / "ltx-nv_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        import ltx_dit
+        import ltx_parallel
+
+        # config-4 widths (video 32x128, audio 32x64, A<->V attention), 2 blocks, small tokens
+        cfg = ltx_dit.DiTConfig(num_layers=2, video_cross_dim=3840, cross_attention_adaln=False)
+        with torch.device("meta"):
+            model = ltx_dit.LTXModel(cfg)
+        gen = ltx_dit.PhiloxGenerator(13, dev)
+        sd = {}
+        for name, p in model.named_parameters():
+            w = gen.randn(*p.shape, dtype=torch.bfloat16).mul_(0.02)
+            if name.endswith(("q_norm.weight", "k_norm.weight")):
+                w.add_(1.0)
+            sd[name] = w
+        model.load_state_dict(sd, assign=True)
+        f, h, w_ = 4, 8, 16
+        tv, ta = f * h * w_, 126
+        v_lat = gen.randn(1, tv, 128, dtype=torch.bfloat16)
+        a_lat = gen.randn(1, ta, 128, dtype=torch.bfloat16)
+        v_ctx = gen.randn(2, 256, 3840, dtype=torch.bfloat16)
+        a_ctx = gen.randn(2, 256, 2048, dtype=torch.bfloat16)
+        v_pos = ltx_dit.video_positions(1, f, h, w_, 24.0, dev)
+        a_pos = ltx_dit.audio_positions(1, ta, dev)
+        kf = torch.zeros(1, tv, 1, device=dev)
+        kf[:, : h * w_] = 1
+        sigmas = torch.tensor([0.5, 0.25])
+        args = (v_lat, a_lat, v_pos, a_pos, v_ctx[:1], v_ctx[1:], a_ctx[:1], a_ctx[1:], sigmas, 0, 3.0)
+        ref_v, ref_a = ltx_dit.av_cfg_denoise_step(model, *args, v_keyframes_mask=kf)
+        pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=cfg_split)
+        out_v, out_a = pdn.step_av(*args, v_keyframes_mask=kf)
+        torch.cuda.synchronize()
+        model._sp = None
+
+        def rel(a, b):
+            return float((a.float() - b.float()).norm() / b.float().norm())
+
+        q.put((rank, rel(out_v, ref_v), rel(out_a, ref_a), pdn.layout.cfg, pdn.layout.sp))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,cfg_split", [(2, 1), (4, 2)])
+def test_parallel_av_step_matches_single_gpu(world, cfg_split):
+    """Audio-video step under sequence parallelism (audio replicated, video-to-audio
+    attention merged from split-KV partials) against the single-GPU av_cfg_denoise_step.
+    The split softmax rounds differently from the single pass, so the check is relative
+    L2 <= 1e-2 (a few 1e-3 expected); video is token-local except self-attention, whose
+    Ulysses exchange is exact."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_av_worker, args=(r, world, port, cfg_split, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    print("\nAV SP rel-L2 per rank (video, audio):", [(r, v, a) for r, v, a, _, _ in res])
+    assert all(v < 1e-2 and a < 1e-2 for _, v, a, _, _ in res), res
