@@ -16,6 +16,13 @@ extern "C" {
  * GEMMs are not affected. Every choice gives bit-identical results. */
 int ltx_gemm_set_tile_n(int bn);
 
+/* Failure-detection probe: one thread waits on an mbarrier that nothing arrives on,
+ * through the bounded wait of the tcgen05 kernels, for at most `limit_cycles` SM cycles
+ * (<= 1e8, about 50 ms); it then gives up, sets bit 1 (wait timed out) of the device
+ * error word that ltx_device_error_flags reads, writes 1 to the device int `returned`
+ * (2 would mean the wait completed) and returns. The context stays usable. */
+int ltx_test_bounded_wait(unsigned long long limit_cycles, int* returned, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

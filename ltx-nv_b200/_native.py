@@ -154,6 +154,7 @@ _SIGNATURES = {
     "ltx_linear": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64,
                                   ctypes.POINTER(Epilogue), ctypes.c_int, c_vp]),
     "ltx_gemm_set_tile_n": (ctypes.c_int, [ctypes.c_int]),
+    "ltx_test_bounded_wait": (ctypes.c_int, [ctypes.c_ulonglong, c_vp, c_vp]),
     "ltx_attention": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, ctypes.c_int, c_i64, c_i64,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, ctypes.c_int, c_vp]),
     "ltx_cfg_euler": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_float,
@@ -444,6 +445,11 @@ def linear(a: torch.Tensor, w: torch.Tensor, c: torch.Tensor, epi: Epilogue | No
     _call("ltx_linear", _ptr(a), _ld(a), _ptr(w), _ld(w), _ptr(c), _ld(c), m, n, k,
           ctypes.byref(epi) if epi is not None else None, _dt(a), _stream(a),
           label=f"linear M={m} N={n} K={k}" if _profile is not None else None)
+
+
+def test_bounded_wait(limit_cycles: int, returned: torch.Tensor) -> None:
+    """Test hook (include/ltxb200_testing.h): a bounded mbarrier wait that must expire."""
+    _call("ltx_test_bounded_wait", limit_cycles, _ptr(returned), _stream(returned))
 
 
 def gemm_set_tile_n(bn: int) -> None:

@@ -174,3 +174,37 @@ extern "C" int ltx_device_error_flags(int* flags, int clear, void* stream) {
   }
   LTX_API_END
 }
+
+// ---------------------------------------------------------------------------------
+// Test hook (include/ltxb200_testing.h): one thread waits on an mbarrier that nothing
+// ever arrives on, through the same bounded wait the tcgen05 kernels use, with a short
+// limit; it must give up, set the device error word and return.
+// ---------------------------------------------------------------------------------
+namespace ltx {
+namespace detail {
+__global__ void bounded_wait_probe_kernel(unsigned long long limit_cycles, int* returned) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = mbar_wait_limit(&bar, 0, &abort_flag, limit_cycles, 1000u);
+    *returned = ok ? 2 : 1;
+  }
+}
+}  // namespace detail
+}  // namespace ltx
+
+extern "C" int ltx_test_bounded_wait(unsigned long long limit_cycles, int* returned, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(returned != nullptr, "returned is NULL");
+  LTX_REQUIRE(limit_cycles > 0 && limit_cycles <= 100000000ull, "limit must be in (0, 1e8] cycles");
+  ltx::detail::bounded_wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_cycles, returned),
+      ltx::note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}

@@ -174,18 +174,22 @@ LTX_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // Wait for the phase with the given parity to complete. Returns false (and flags the
 // device error word) if the wait exceeds the cycle budget; `abort` is a shared flag
 // that lets the other roles of the CTA give up promptly once one of them timed out.
-LTX_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+LTX_DEVICE bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort, unsigned long long limit,
+                                uint32_t sleep_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (mbar_try_wait_sleep(bar, parity, sleep_ns)) return true;
     if (abort != nullptr && *abort) return false;
-    if (clock64() - t0 > LTX_WAIT_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       ltx_flag_error(LTX_DEVERR_MBAR_TIMEOUT);
       if (abort != nullptr) *abort = 1;
       return false;
     }
   }
+}
+LTX_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_limit(bar, parity, abort, LTX_WAIT_LIMIT_CYCLES, 100000u);
 }
 
 // ---------------------------------------------------------------------------------

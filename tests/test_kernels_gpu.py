@@ -566,3 +566,23 @@ def test_split_kv_attention_merge_matches_full_attention(hd, parts, tk):
     s = torch.einsum("hqd,hkd->hqk", q4, k4[:, :sl]) * hd ** -0.5
     lse_ref = torch.logsumexp(s, dim=-1).transpose(0, 1) / math.log(2.0)
     assert torch.allclose(lse_all[0], lse_ref, atol=2e-2, rtol=1e-3)
+
+
+def test_bounded_wait_expires_and_reports_on_the_host():
+    """Failure detection without a GPU fault: a bounded mbarrier wait on a barrier that
+    nothing arrives on (the wait the tcgen05 kernels use, with a 2M-cycle limit instead
+    of ~4 s) gives up, sets the device error word and returns; the host reads the flag,
+    clears it, and the context keeps working."""
+    assert nat.device_error_flags(clear=True) == 0
+    ret = torch.zeros(1, dtype=torch.int32, device=DEV)
+    nat.test_bounded_wait(2_000_000, ret)
+    torch.cuda.synchronize()
+    assert int(ret.item()) == 1  # returned after giving up (2 would mean the wait completed)
+    assert nat.device_error_flags(clear=True) == 1  # LTX_DEVERR_MBAR_TIMEOUT
+    assert nat.device_error_flags() == 0
+    x = torch.randn(4096, device=DEV).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    nat.gelu_tanh(x, y)
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.gelu(x.float(), approximate="tanh")
+    assert rel_l2(y, ref) < 1e-2
