@@ -180,6 +180,22 @@ int ltx_linear(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, 
 int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
                   int64_t ldo, int B, int64_t Tq, int64_t Tk, int heads, int head_dim, float scale,
                   const void* gate_logits, int64_t ld_gate, int dtype, void* stream);
+/* ltx_attention with a workspace; same operands, and results equal up to bf16 rounding
+ * of P within the split rows. The bf16 kernel runs one CTA per (sample, head, 256
+ * queries); when these units leave the last wave of SMs partly filled, the units of that
+ * wave are split over 2-8 key ranges whose fp32 partials the last CTA of each unit merges
+ * (same as ltx_attention otherwise). The workspace (device memory,
+ * ltx_attention_workspace_bytes bytes, 16-byte aligned) must be zero-filled before its
+ * first use; every call leaves its counters at zero, so one workspace serves any sequence
+ * of calls issued to one stream (calls that may run concurrently need one each). NULL,
+ * or fewer bytes than the shape needs, runs without the split. Same reference as
+ * ltx_attention. ltx_attention_workspace_bytes returns 0 when the shape has nothing to
+ * split (then the two calls are the same). */
+size_t ltx_attention_workspace_bytes(int B, int64_t Tq, int64_t Tk, int heads, int head_dim);
+int ltx_attention_ws(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
+                     int64_t ldo, int B, int64_t Tq, int64_t Tk, int heads, int head_dim, float scale,
+                     const void* gate_logits, int64_t ld_gate, void* workspace, size_t workspace_bytes, int dtype,
+                     void* stream);
 
 /* ---------------------------------------------------------------------------------- */
 /* Denoise update: X0 conversion + CFG guidance + Euler step.                          */

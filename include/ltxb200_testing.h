@@ -16,11 +16,18 @@ extern "C" {
  * GEMMs are not affected. Every choice gives bit-identical results. */
 int ltx_gemm_set_tile_n(int bn);
 
-/* Failure-detection probe: one thread waits on an mbarrier that nothing arrives on,
+/* Force every (sample, head, 256-query) unit of the calling thread's subsequent
+ * ltx_attention_ws calls (bf16, Tk > 128) to run as `parts` key-range parts merged by the
+ * last one (1..8; parts = 1 runs each unit through the part kernel over all its keys),
+ * 0 for the automatic plan, or -1 to never split. Shapes whose key tiles (Tk / 128, Tk
+ * a multiple of 128) `parts` does not divide run unsplit. Thread-local;
+ * ltx_attention_workspace_bytes follows it. */
+ one thread waits on an mbarrier that nothing arrives on,
  * through the bounded wait of the tcgen05 kernels, for at most `limit_cycles` SM cycles
  * (<= 1e8, about 50 ms); it then gives up, sets bit 1 (wait timed out) of the device
  * error word that ltx_device_error_flags reads, writes 1 to the device int `returned`
  * (2 would mean the wait completed) and returns. The context stays usable. */
+int ltx_test_attention_force_split(int parts);
 int ltx_test_bounded_wait(unsigned long long limit_cycles, int* returned, void* stream);
 
 #ifdef __cplusplus

@@ -155,6 +155,7 @@ _SIGNATURES = {
                                   ctypes.POINTER(Epilogue), ctypes.c_int, c_vp]),
     "ltx_gemm_set_tile_n": (ctypes.c_int, [ctypes.c_int]),
     "ltx_test_bounded_wait": (ctypes.c_int, [ctypes.c_ulonglong, c_vp, c_vp]),
+    "ltx_test_attention_force_split": (ctypes.c_int, [ctypes.c_int]),
     "ltx_attention": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, ctypes.c_int, c_i64, c_i64,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, ctypes.c_int, c_vp]),
     "ltx_cfg_euler": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_float,
@@ -190,6 +191,10 @@ _SIGNATURES = {
     "ltx_proj_out_cfg_euler": (ctypes.c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, ctypes.c_int, c_i64, c_vp, c_vp,
                                               ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp, c_vp, c_vp,
                                               ctypes.c_int, c_vp]),
+    "ltx_attention_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int, c_i64, c_i64, ctypes.c_int, ctypes.c_int]),
+    "ltx_attention_ws": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, ctypes.c_int, c_i64,
+                                        c_i64, ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, c_vp,
+                                        ctypes.c_size_t, ctypes.c_int, c_vp]),
     "ltx_attention_partial": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                              ctypes.c_int, c_i64, c_i64, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                              c_vp]),
@@ -452,16 +457,47 @@ def test_bounded_wait(limit_cycles: int, returned: torch.Tensor) -> None:
     _call("ltx_test_bounded_wait", limit_cycles, _ptr(returned), _stream(returned))
 
 
+def attention_force_split(parts: int) -> None:
+    """Test hook (include/ltxb200_testing.h): run every unit of the calling thread's
+    attention calls as `parts` key-range parts (0: the automatic plan; -1: never split)."""
+    _call("ltx_test_attention_force_split", parts)
+
+
 def gemm_set_tile_n(bn: int) -> None:
     """Test hook (include/ltxb200_testing.h): force the calling thread's GEMM tile width."""
     _call("ltx_gemm_set_tile_n", bn)
 
 
+_attn_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def attention_workspace(batch: int, tq: int, tk: int, heads: int, head_dim: int,
+                        device: torch.device) -> torch.Tensor | None:
+    """The zero-filled attention workspace of the current stream on `device`, grown to
+    what this shape needs (ltx_attention_workspace_bytes); None when the shape needs none.
+    Calls on one stream run in order and share it; every stream has its own."""
+    n = load_library().ltx_attention_workspace_bytes(batch, tq, tk, heads, head_dim)
+    if n == 0:
+        return None
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    ws = _attn_ws.get(key)
+    if ws is None or ws.numel() < n:
+        ws = torch.zeros(n, dtype=torch.uint8, device=device)
+        _attn_ws[key] = ws
+    return ws
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, batch: int, tq: int, tk: int,
-              heads: int, head_dim: int, scale: float, gate_logits: torch.Tensor | None = None) -> None:
-    """q (B*Tq, >=H*d), k/v (B*Tk, >=H*d), o (B*Tq, >=H*d) row-major views; gate (B*Tq, >=H)."""
-    _call("ltx_attention", _ptr(q), _ld(q), _ptr(k), _ld(k), _ptr(v), _ld(v), _ptr(o), _ld(o), batch, tq, tk, heads,
-          head_dim, scale, _ptr(gate_logits), _ld(gate_logits) if gate_logits is not None else 0, _dt(q), _stream(q),
+              heads: int, head_dim: int, scale: float, gate_logits: torch.Tensor | None = None,
+              split_tail: bool = True) -> None:
+    """q (B*Tq, >=H*d), k/v (B*Tk, >=H*d), o (B*Tq, >=H*d) row-major views; gate (B*Tq, >=H).
+    bf16 runs through ltx_attention_ws with the stream's workspace; split_tail=False
+    passes no workspace (the single-pass launch of ltx_attention)."""
+    ws = attention_workspace(batch, tq, tk, heads, head_dim, q.device) \
+        if split_tail and q.dtype == torch.bfloat16 else None
+    _call("ltx_attention_ws", _ptr(q), _ld(q), _ptr(k), _ld(k), _ptr(v), _ld(v), _ptr(o), _ld(o), batch, tq, tk,
+          heads, head_dim, scale, _ptr(gate_logits), _ld(gate_logits) if gate_logits is not None else 0, _ptr(ws),
+          ws.numel() if ws is not None else 0, _dt(q), _stream(q),
           label=f"attention B={batch} H={heads} Tq={tq} Tk={tk} d={head_dim}" if _profile is not None else None)
 
 

@@ -60,15 +60,46 @@ LTX_DEVICE uint8_t* fa_align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-template <int D>
-// d 64: 11 warps, three share one SM sub-partition's 16K registers, so <= 168 per
-// thread; d 128: 10 warps, <= 204.
-__global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
-    fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
-                   int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
-                   float* __restrict__ o32, float* __restrict__ lse, int64_t ld_lse) {
+// Split of one attention call. A unit is (sample b, head h, 256 queries), numbered
+// u = x + nq2 (h + H b) in grid order, so neighbouring units share K and V in L2.
+// fmha_tc_kernel runs units [0, n_full) whole, one CTA each, in full waves of the SMs.
+// The n_split units after them would only partly fill a last wave; fmha_part_kernel
+// runs each of them as split_k parts over contiguous key ranges, CTA p = su * split_k + j
+// being part j of unit n_full + su. A part writes fp32 O / l and the row's log2-sum-exp
+// to slot p of part_o / part_lse; the last part of a unit to finish (arrival counter
+// counters[su], reset by that CTA) merges the split_k parts in part order, applies the
+// gate and writes O.
+struct FaSched {
+  int B, H, nq2, n_full, n_split, split_k;
+  float* part_o;    // [n_split * split_k][256][D]
+  float* part_lse;  // [n_split * split_k][256]
+  int* counters;    // [n_split], zero before the first launch, left at zero
+};
+
+constexpr int kFaMaxSplit = 8;
+
+// Exponential pairs (of the 64 in a 128-key row of S) computed on the FMA pipe by the
+// cubic of ex2_poly2 instead of the special-function unit, bit j = pair j.
+#ifndef LTX_FA_POLY_PAIRS
+#define LTX_FA_POLY_PAIRS 0x888888888a8a8888ull
+#endif
+constexpr uint64_t kFaPolyPairs = LTX_FA_POLY_PAIRS;
+
+// One CTA's work. PART = false: a whole unit (all keys); PART = true: tk_part keys from
+// key tile kv0 on, of unit n_full + su, merged as above (Tk is a multiple of the key
+// tile and every part has the same tk_part keys). The two run in separate kernels,
+// each with its own register allocation.
+template <int D, bool PART>
+__device__ __forceinline__ void fmha_body(const CUtensorMap* tmQ_, const CUtensorMap* tmK_,
+                                          const CUtensorMap* tmV_, __nv_bfloat16* __restrict__ O, int64_t ldo,
+                                          int Tq, int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate,
+                                          int64_t ld_gate, float* __restrict__ o32, float* __restrict__ lse,
+                                          int64_t ld_lse, const int h, const int b, const int q0, const int kv0,
+                                          const int tk_part, const int su, const int part, const FaSched& sch) {
   using Cfg = FaCfg<D>;
+  const CUtensorMap& tmQ = *tmQ_;
+  const CUtensorMap& tmK = *tmK_;
+  const CUtensorMap& tmV = *tmV_;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = fa_align1024(smem_raw);
   uint8_t* sQ = smem;                          // Q tile i at sQ + i * TILE
@@ -84,11 +115,14 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
   uint64_t* o_done = p_full + 2;             // [2] P_i V_t completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* merge_flag = abort_flag + 1;  // PART: this CTA merges its unit
 
   const int warp = warp_id(), lane = lane_id();
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = blockIdx.x * 2 * Cfg::BM;
-  const int n_kv = (Tk + Cfg::BN - 1) / Cfg::BN;
+  // A part's keys are tk_part keys from tile kv0 on, tk_part a kernel parameter like Tk:
+  // the key count that bounds the loops and decides full tiles must stay a launch
+  // constant (computed per CTA, it made the softmax loop a third slower).
+  const int tk_eff = PART ? tk_part : Tk;
+  const int n_kv = (tk_eff + Cfg::BN - 1) / Cfg::BN;  // key tiles of this CTA
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -135,7 +169,7 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
         if (!mbar_wait(&kv_empty[s], (r & 1) ^ 1, abort_flag)) break;
         uint8_t* sk = sKV + (2 * s) * Cfg::TILE_BYTES;
         uint8_t* sv = sk + Cfg::TILE_BYTES;
-        const int row = b * Tk + t * Cfg::BN;
+        const int row = b * Tk + (PART ? kv0 * Cfg::BN : 0) + t * Cfg::BN;
         mbar_arrive_expect_tx(&k_full[s], Cfg::TILE_BYTES);
 #pragma unroll
         for (int j = 0; j < Cfg::SUB; ++j)
@@ -303,7 +337,7 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
         tc_fence_before();
         mbar_arrive(&s_free[qt]);
       }
-      const int valid = Tk - t * Cfg::BN;
+      const int valid = tk_eff - t * Cfg::BN;
       if (valid < Cfg::BN) {
 #pragma unroll
         for (int e = 0; e < 128; ++e)
@@ -327,21 +361,20 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
         m_ref = m_new;
       }
       // x = s * scale_log2 - m_ref and the row sum in packed fp32x2 (two lanes per
-      // instruction); on full tiles 9 pairs in 32 take the FMA-pipe exponential (one in
-      // four, plus one: the measured optimum of this loop's schedule).
+      // instruction); on full tiles the pairs set in kFaPolyPairs take the FMA-pipe
+      // exponential, the others the special-function unit.
       const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
       const uint64_t nm2 = f2_pack(-m_ref, -m_ref);
       uint64_t rs2[4] = {0, 0, 0, 0};  // bit pattern of (0.f, 0.f)
-      const bool full = valid >= Cfg::BN;
       uint32_t pk[64];
+      const bool full = valid >= Cfg::BN;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float x0, x1, p0, p1;
           f2_unpack(f2_fma(f2_pack(sv[c * 32 + e], sv[c * 32 + e + 1]), sc2, nm2), x0, x1);
-          const int q = (e >> 1) & 7;
-          if (full && ((q & 3) == 3 || (c == 1 && q == 1))) {
+          if (full && ((kFaPolyPairs >> (c * 16 + (e >> 1))) & 1u)) {
             ex2_poly2(x0, x1, p0, p1);
           } else {
             p0 = ex2_approx(x0);
@@ -396,7 +429,118 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
       tc_fence_before();
       mbar_arrive(&p_full[qt]);
     }
-    if (ok && mbar_wait(&o_done[qt], uint32_t(n_kv - 1) & 1, abort_flag)) {
+    const bool have = ok && mbar_wait(&o_done[qt], uint32_t(n_kv - 1) & 1, abort_flag);
+    if constexpr (PART) {
+      // fp32 O / l and the log2-sum-exp of this key range to slot su * split_k + part;
+      // every part CTA counts itself in exactly once (also after an abort, so the counter
+      // always returns to zero) and the last one merges all parts in part order.
+      const int r = qt * Cfg::BM + row;
+      const int qi = q0 + r;
+      const int64_t slot = int64_t(su) * sch.split_k + part;
+      if (have) {
+        tc_fence_after();
+        const float inv_l = 1.f / l_run;
+        float* dst = sch.part_o + (slot * 256 + r) * D;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t rr[32];
+          tmem_ld32(o_tmem + uint32_t(c0), rr);
+          tmem_wait_ld();
+          if (qi < Tq) {
+#pragma unroll
+            for (int e4 = 0; e4 < 32; e4 += 4)
+              __stcg(reinterpret_cast<float4*>(dst + c0 + e4),
+                     make_float4(__uint_as_float(rr[e4]) * inv_l, __uint_as_float(rr[e4 + 1]) * inv_l,
+                                 __uint_as_float(rr[e4 + 2]) * inv_l, __uint_as_float(rr[e4 + 3]) * inv_l));
+          }
+        }
+        if (qi < Tq) __stcg(sch.part_lse + slot * 256 + r, m_ref + log2f(l_run));
+      }
+      __threadfence();
+      named_bar_sync(1, 2 * Cfg::BM);  // the 8 softmax warps
+      if (threadIdx.x == 0) {
+        const int last = atomicAdd(&sch.counters[su], 1) == sch.split_k - 1;
+        if (last) atomicExch(&sch.counters[su], 0);
+        *merge_flag = last;
+      }
+      named_bar_sync(1, 2 * Cfg::BM);
+      if (*merge_flag) {
+        // All MMAs and loads of this CTA are complete (every softmax thread waited for its
+        // tile's last P V before the barrier above), so shared memory is free: stage the
+        // per-row part weights 2^(lse_j - max), 1 / sum and the gate there, then merge with
+        // whole warps reading contiguous rows of the parts, many loads in flight.
+        __threadfence();
+        float* mw = reinterpret_cast<float*>(smem);  // [kFaMaxSplit][256]
+        float* minv = mw + kFaMaxSplit * 256;        // [256]
+        float* mg = minv + 256;                      // [256]
+        const int64_t slot0 = int64_t(su) * sch.split_k;
+        {
+          float w[kFaMaxSplit];
+          float lmax = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < kFaMaxSplit; ++j) {
+            w[j] = (j < sch.split_k && qi < Tq) ? __ldcg(sch.part_lse + (slot0 + j) * 256 + r) : -INFINITY;
+            lmax = fmaxf(lmax, w[j]);
+          }
+          float wsum = 0.f;
+#pragma unroll
+          for (int j = 0; j < kFaMaxSplit; ++j) {
+            w[j] = (j < sch.split_k && qi < Tq) ? exp2f(w[j] - lmax) : 0.f;
+            wsum += w[j];
+            mw[j * 256 + r] = w[j];
+          }
+          minv[r] = qi < Tq ? 1.f / wsum : 0.f;
+          float g = 1.f;
+          if (gate != nullptr && qi < Tq) {
+            const float lg = __bfloat162float(gate[(int64_t(b) * Tq + qi) * ld_gate + h]);
+            const float sg = round_bf16(1.f / (1.f + expf(-lg)));
+            g = round_bf16(2.f * sg);
+          }
+          mg[r] = g;
+        }
+        named_bar_sync(1, 2 * Cfg::BM);
+        constexpr int C4 = D / 4;  // float4 chunks per row; 256 * C4 is a multiple of 1024
+        const float* src = sch.part_o + slot0 * 256 * D;
+        const int tid = int(threadIdx.x);
+        for (int c = tid; c < 256 * C4; c += 4 * 256) {
+          float4 acc[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int cc = c + u * 256, rr = cc / C4, col = (cc % C4) * 4;
+            acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < kFaMaxSplit; ++j) {
+              if (j < sch.split_k) {
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(src + (int64_t(j) * 256 + rr) * D + col));
+                const float wj = mw[j * 256 + rr];
+                acc[u].x += wj * a.x;
+                acc[u].y += wj * a.y;
+                acc[u].z += wj * a.z;
+                acc[u].w += wj * a.w;
+              }
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int cc = c + u * 256, rr = cc / C4, col = (cc % C4) * 4;
+            const int qr = q0 + rr;
+            if (qr < Tq) {
+              const float inv = minv[rr], g = mg[rr];
+              float o0 = round_bf16(acc[u].x * inv), o1 = round_bf16(acc[u].y * inv);
+              float o2 = round_bf16(acc[u].z * inv), o3 = round_bf16(acc[u].w * inv);
+              if (gate != nullptr) {
+                o0 *= g;
+                o1 *= g;
+                o2 *= g;
+                o3 *= g;
+              }
+              *reinterpret_cast<uint2*>(O + (int64_t(b) * Tq + qr) * ldo + int64_t(h) * D + col) =
+                  make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+            }
+          }
+        }
+      }
+    } else if (have) {
       tc_fence_after();
       const int qi = q0 + qt * Cfg::BM + row;
       const float inv_l = 1.f / l_run;
@@ -454,6 +598,45 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
+}
+
+template <int D>
+// d 64: 11 warps, three share one SM sub-partition's 16K registers, so <= 168 per
+// thread; d 128: 10 warps (registers are allocated for 12, so also <= 168).
+__global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
+    fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
+                   int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
+                   float* __restrict__ o32, float* __restrict__ lse, int64_t ld_lse, const int n_whole) {
+  // Let the part kernel (launched after this one with programmatic stream
+  // serialisation) take SMs as soon as this grid's last wave is resident: it needs
+  // nothing this grid writes.
+  asm volatile("griddepcontrol.launch_dependents;");
+  // whole units only: the units from n_whole on run as parts (fmha_part_kernel)
+  if (int(blockIdx.x) + int(gridDim.x) * (int(blockIdx.y) + int(gridDim.y) * int(blockIdx.z)) >= n_whole) return;
+  const FaSched none{};
+  fmha_body<D, false>(&tmQ, &tmK, &tmV, O, ldo, Tq, Tk, scale_log2, gate, ld_gate, o32, lse, ld_lse,
+                      int(blockIdx.y), int(blockIdx.z), int(blockIdx.x) * 2 * FaCfg<D>::BM, 0, 0, -1, -1, none);
+}
+
+// The split units' parts, one CTA each (CTA p = part p % split_k of unit n_full + p /
+// split_k), launched after fmha_tc_kernel has run the whole units in full waves.
+template <int D>
+__global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
+    fmha_part_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
+                     int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
+                     const int tk_part, const FaSched sch) {
+  const int p = int(blockIdx.x);
+  const int su = p / sch.split_k, part = p % sch.split_k;
+  const int unit = sch.n_full + su;
+  const int kv0 = part * (tk_part / FaCfg<D>::BN);
+  fmha_body<D, true>(&tmQ, &tmK, &tmV, O, ldo, Tq, Tk, scale_log2, gate, ld_gate, nullptr, nullptr, 0,
+                     (unit / sch.nq2) % sch.H, unit / (sch.nq2 * sch.H), (unit % sch.nq2) * 2 * FaCfg<D>::BM, kv0,
+                     tk_part, su, part, sch);
+  // Complete only after the whole-unit grid has: work queued behind this launch then
+  // sees both grids' outputs.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------
@@ -762,11 +945,85 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const float* __restrict_
   for (int c = 0; c < D; ++c) op[c] = (acc[c] / l) * g;
 }
 
+// Split plan of one launch. The R = units mod SMs units beyond the last whole wave
+// are split into k parts of n/k key tiles each (k divides the n key tiles; Tk a multiple
+// of the key tile) when that ends sooner. Measured on the B200, in key-tile times: a
+// whole unit costs about kFaWholeFixedTiles + n, a part kFaPartFixedTiles + n/k (the
+// part's extra launch, partial stores and merge); the tail costs one round of whole
+// units without the split and ceil(R k / SMs) rounds of parts with it.
+struct FaPlan {
+  int n_full = 0, split_k = 1, n_split = 0;
+  int64_t slots() const { return int64_t(n_split) * split_k; }
+};
+// Attention workspace: [counters: kFaCounterBytes][part_lse: slots x 256 fp32]
+// [part_o: slots x 256 x D fp32]. The counters sit at offset 0 for every shape and every
+// launch leaves them at zero, so one zero-filled workspace serves any sequence of calls
+// on one stream.
+constexpr size_t kFaCounterBytes = 4096;
+constexpr int kFaMinTilesPerPart = 3;
+constexpr int kFaMaxSlotsPerSm = 4;  // bounds the workspace
+constexpr double kFaWholeFixedTiles = 11.0, kFaPartFixedTiles = 16.0;
+
+inline FaPlan fa_plan(int64_t units, int64_t Tk, int sms) {
+  FaPlan p;
+  p.n_full = int(units);
+  const int64_t R = units % sms;
+  const int n = int(Tk / 128);
+  if (R == 0 || Tk % 128 != 0 || R > int64_t(kFaCounterBytes / sizeof(int))) return p;
+  double best = kFaWholeFixedTiles + n;
+  int best_k = 1;
+  for (int k = 2; k <= kFaMaxSplit && k * kFaMinTilesPerPart <= n; ++k) {
+    if (n % k != 0 || R * k > int64_t(kFaMaxSlotsPerSm) * sms) continue;
+    const double cost = double((R * k + sms - 1) / sms) * (kFaPartFixedTiles + double(n / k));
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_k = k;
+    }
+  }
+  if (best_k > 1) {
+    p.n_full = int(units - R);
+    p.split_k = best_k;
+    p.n_split = int(R);
+  }
+  return p;
+}
+
+// Test hook (ltx_test_attention_force_split): > 0 runs every unit as that many parts,
+// < 0 never splits.
+static thread_local int g_fa_force_split = 0;
+
+inline FaPlan fa_plan_for(int B, int64_t Tq, int64_t Tk, int H) {
+  const int64_t units = int64_t(B) * H * ((Tq + 255) / 256);
+  const int k = g_fa_force_split;
+  if (k < 0) {
+    FaPlan p;
+    p.n_full = int(units);
+    return p;
+  }
+  if (k > 0) {
+    FaPlan p;
+    if (Tk % 128 == 0 && (Tk / 128) % k == 0 && units <= int64_t(kFaCounterBytes / sizeof(int))) {
+      p.n_full = 0;
+      p.n_split = int(units);
+      p.split_k = k;
+    } else {
+      p.n_full = int(units);
+    }
+    return p;
+  }
+  return fa_plan(units, Tk, num_sms());
+}
+
+inline size_t fa_workspace_bytes(const FaPlan& p, int D) {
+  if (p.n_split == 0) return 0;
+  return kFaCounterBytes + size_t(p.slots()) * 256 * 4 + size_t(p.slots()) * 256 * size_t(D) * 4;
+}
+
 template <int D>
 void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
                     int64_t ldo, int B, int64_t Tq, int64_t Tk, int H, float scale, const void* gate,
                     int64_t ld_gate, cudaStream_t s, float* o32 = nullptr, float* lse = nullptr,
-                    int64_t ld_lse = 0) {
+                    int64_t ld_lse = 0, void* workspace = nullptr, size_t ws_bytes = 0) {
   using Cfg = FaCfg<D>;
   const uint64_t cols = uint64_t(H) * D;
   const CUtensorMap tq = make_tmap_bf16_2d(q, cols, uint64_t(B) * Tq, uint64_t(ldq), 64, 128);
@@ -775,12 +1032,45 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   auto kern = fmha_tc_kernel<D>;
   static std::atomic<uint64_t> smem_done{0};
   ensure_smem_limit(smem_done, kern, Cfg::SMEM);
-  dim3 grid(unsigned((Tq + 2 * Cfg::BM - 1) / (2 * Cfg::BM)), unsigned(H), unsigned(B));
+  const int nq2 = int((Tq + 2 * Cfg::BM - 1) / (2 * Cfg::BM));
+  FaSched sch{B, H, nq2, int(int64_t(B) * H * nq2), 0, 1, nullptr, nullptr, nullptr};
+  if (o32 == nullptr && workspace != nullptr) {
+    const FaPlan p = fa_plan_for(B, Tq, Tk, H);
+    if (p.n_split > 0 && ws_bytes >= fa_workspace_bytes(p, D)) {
+      char* w = static_cast<char*>(workspace);
+      sch.n_full = p.n_full;
+      sch.n_split = p.n_split;
+      sch.split_k = p.split_k;
+      sch.counters = reinterpret_cast<int*>(w);
+      sch.part_lse = reinterpret_cast<float*>(w + kFaCounterBytes);
+      sch.part_o = reinterpret_cast<float*>(w + kFaCounterBytes + size_t(p.slots()) * 256 * 4);
+    }
+  }
+  const dim3 grid{unsigned(nq2), unsigned(H), unsigned(B)};
   const float scale_log2 = scale * 1.4426950408889634f;
   kern<<<grid, Cfg::THREADS, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk),
                                              scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate, o32, lse,
-                                             ld_lse),
+                                             ld_lse, sch.n_full),
       ltx::note_launch();
+  if (sch.n_split > 0) {
+    auto pk = fmha_part_kernel<D>;
+    static std::atomic<uint64_t> smem_done_p{0};
+    ensure_smem_limit(smem_done_p, pk, Cfg::SMEM);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(unsigned(sch.n_split * sch.split_k));
+    lc.blockDim = dim3(Cfg::THREADS);
+    lc.dynamicSmemBytes = Cfg::SMEM;
+    lc.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    LTX_CUDA(cudaLaunchKernelEx(&lc, pk, tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk),
+                                scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate,
+                                int(Tk / sch.split_k), sch));
+    ltx::note_launch();
+  }
 }
 
 template <int D>
@@ -870,9 +1160,15 @@ extern "C" int ltx_value_gate(const void* v, int64_t ldv, const void* gate_logit
   LTX_API_END
 }
 
-extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
-                             void* o, int64_t ldo, int B, int64_t Tq, int64_t Tk, int heads, int head_dim,
-                             float scale, const void* gate_logits, int64_t ld_gate, int dtype, void* stream) {
+extern "C" size_t ltx_attention_workspace_bytes(int B, int64_t Tq, int64_t Tk, int heads, int head_dim) {
+  if (B <= 0 || Tq <= 0 || Tk <= 128 || heads <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
+  return fa_workspace_bytes(fa_plan_for(B, Tq, Tk, heads), head_dim);
+}
+
+extern "C" int ltx_attention_ws(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                                void* o, int64_t ldo, int B, int64_t Tq, int64_t Tk, int heads, int head_dim,
+                                float scale, const void* gate_logits, int64_t ld_gate, void* workspace,
+                                size_t workspace_bytes, int dtype, void* stream) {
   LTX_API_BEGIN
   LTX_REQUIRE(dtype == LTX_F32 || dtype == LTX_BF16, "dtype must be F32 or BF16");
   LTX_REQUIRE(q && k && v && o, "q, k, v and o must be non-NULL");
@@ -895,9 +1191,11 @@ extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t 
     else if (Tk <= 128)
       launch_fmha_kv1<128>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
     else if (head_dim == 64)
-      launch_fmha_tc<64>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
+      launch_fmha_tc<64>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s, nullptr,
+                         nullptr, 0, workspace, workspace_bytes);
     else
-      launch_fmha_tc<128>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s);
+      launch_fmha_tc<128>(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, scale, gate_logits, ld_gate, s, nullptr,
+                          nullptr, 0, workspace, workspace_bytes);
   } else {
     dim3 grid(unsigned((Tq + 127) / 128), unsigned(heads), unsigned(B));
     auto Qp = static_cast<const float*>(q);
@@ -913,5 +1211,19 @@ extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t 
     }
   }
   LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                             void* o, int64_t ldo, int B, int64_t Tq, int64_t Tk, int heads, int head_dim,
+                             float scale, const void* gate_logits, int64_t ld_gate, int dtype, void* stream) {
+  return ltx_attention_ws(q, ldq, k, ldk, v, ldv, o, ldo, B, Tq, Tk, heads, head_dim, scale, gate_logits, ld_gate,
+                          nullptr, 0, dtype, stream);
+}
+
+extern "C" int ltx_test_attention_force_split(int parts) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(parts >= -1 && parts <= kFaMaxSplit, "parts must be in [-1, 8]");
+  g_fa_force_split = parts;
   LTX_API_END
 }

@@ -39,7 +39,7 @@ inline size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
 // Workspace layout of one step (offsets in bytes from the workspace base).
 struct StepLayout {
-  size_t x, h, big, o, kv, ctx2, cos, sin, tmod, emb, tproj, th, ts, tin, freqs, maxpos, total;
+  size_t x, h, big, o, kv, ctx2, cos, sin, tmod, emb, tproj, th, ts, tin, freqs, maxpos, attn, attn_bytes, total;
   int64_t rows1, rows2, big_cols, n_freq;
 };
 
@@ -74,6 +74,9 @@ inline StepLayout step_layout(const ltx_dit_config& c, int64_t T, int64_t S) {
   L.tin = take(2 * sizeof(float));
   L.freqs = take(size_t(L.n_freq) * sizeof(float));
   L.maxpos = take(3 * sizeof(float));
+  // self-attention's split-tail workspace (zero-filled by ltx_dit_reserve)
+  L.attn_bytes = c.dtype == LTX_BF16 ? ltx_attention_workspace_bytes(2, T, T, c.heads, c.head_dim) : 0;
+  L.attn = take(L.attn_bytes);
   L.total = off;
   return L;
 }
@@ -204,6 +207,7 @@ extern "C" int ltx_dit_reserve(ltx_ctx* ctx, const ltx_dit_config* cfg, int64_t 
   char* base = static_cast<char*>(ctx->ws);
   LTX_CUDA(cudaMemcpy(base + L.freqs, freqs.data(), freqs.size() * sizeof(float), cudaMemcpyHostToDevice));
   LTX_CUDA(cudaMemcpy(base + L.maxpos, cfg->max_pos, 3 * sizeof(float), cudaMemcpyHostToDevice));
+  if (L.attn_bytes > 0) LTX_CUDA(cudaMemset(base + L.attn, 0, L.attn_bytes));
   ctx->cfg = *cfg;
   ctx->T = T;
   ctx->S = S;
@@ -330,8 +334,9 @@ extern "C" int ltx_dit_step(ltx_ctx* ctx, const ltx_dit_config* cfg, const ltx_d
     ok(ltx_qk_norm_rope_pair(big, rows1, D, M, T, int(H), int(hd), bw.attn1_q_norm, bw.attn1_k_norm, eps, cosb, sinb,
                              D / 2, 0, dt, stream),
        "q/k norm + RoPE");
-    ok(ltx_attention(big, rows1, el(big, D), rows1, el(big, 2 * D), rows1, o, D, 2, T, T, int(H), int(hd), attn_scale,
-                     cfg->gated_attention ? el(big, 3 * D) : nullptr, rows1, dt, stream),
+    ok(ltx_attention_ws(big, rows1, el(big, D), rows1, el(big, 2 * D), rows1, o, D, 2, T, T, int(H), int(hd),
+                        attn_scale, cfg->gated_attention ? el(big, 3 * D) : nullptr, rows1,
+                        L.attn_bytes > 0 ? base + L.attn : nullptr, L.attn_bytes, dt, stream),
        "self-attention");
     {
       ltx_modulation g2 = table_mod(bw.scale_shift_table, tmod, D, 6, -1, 2);

@@ -390,6 +390,11 @@ LTX_DEVICE void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 LTX_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Barrier `id` (1..15; 0 is __syncthreads) over the first `threads` threads' warps.
+LTX_DEVICE void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // 2^x on the special-function unit (approximate, flushes subnormals; exact 0 for -inf).
 LTX_DEVICE float ex2_approx(float x) {
   float y;

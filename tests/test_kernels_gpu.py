@@ -397,6 +397,49 @@ def test_attention_bf16_tcgen05(b, tq, tk, h, d):
     assert rel_l2(o, _attn_ref(q, k, v, b, tq, tk, h, d)) < 1e-2
 
 
+# ltx_attention_ws splits the (sample, head, 256-query) units that would only partly fill
+# a last wave of SMs into key-range parts merged by the last one. parts = 0: the
+# automatic plan at the per-rank self-attention shapes of 1, 2 and 8 GPUs (it must
+# split them); parts > 0: every unit forced through the part kernel, on a ragged query
+# count, one key tile per part, parts = 1 (the merge of a single part), and head_dim 128.
+@pytest.mark.parametrize("b,tq,tk,h,d,parts", [(2, 6144, 6144, 32, 64, 0), (1, 6144, 6144, 32, 64, 0),
+                                               (1, 6144, 6144, 8, 64, 0), (1, 6144, 6144, 8, 128, 0),
+                                               (2, 2000, 2048, 4, 64, 4), (1, 1000, 1536, 3, 64, 3),
+                                               (1, 300, 384, 2, 64, 3), (2, 700, 1024, 2, 64, 1),
+                                               (1, 1536, 1536, 2, 128, 2), (2, 520, 1024, 3, 128, 8)])
+def test_attention_split_tail_matches_single_pass(b, tq, tk, h, d, parts):
+    torch.manual_seed(16)
+    nat.attention_force_split(parts)
+    try:
+        assert nat.load_library().ltx_attention_workspace_bytes(b, tq, tk, h, d) > 0, "shape must exercise the split"
+        qkv = torch.randn(b * max(tq, tk), 3 * h * d + ((h + 7) // 8) * 8, device=DEV, dtype=torch.bfloat16)
+        q, k, v = qkv[:b * tq, :h * d], qkv[:b * tk, h * d:2 * h * d], qkv[:b * tk, 2 * h * d:3 * h * d]
+        gate = qkv[:b * tq, 3 * h * d:3 * h * d + h]
+        whole = torch.empty(b * tq, h * d, device=DEV, dtype=torch.bfloat16)
+        nat.attention(q, k, v, whole, b, tq, tk, h, d, d ** -0.5, gate, split_tail=False)
+        ref = _attn_ref(q, k, v, b, tq, tk, h, d, gate)
+        e_whole = rel_l2(whole, ref)
+        first = None
+        for _ in range(2):  # the second call starts from the counters the first one left
+            split = torch.full_like(whole, float("nan"))
+            nat.attention(q, k, v, split, b, tq, tk, h, d, d ** -0.5, gate)
+            torch.cuda.synchronize()
+            assert nat.device_error_flags() == 0
+            # Each part rounds P = 2^(s - m) to bf16 against its own running maximum, so
+            # split rows differ from the single pass by bf16 rounding; they must be as
+            # accurate against exact arithmetic.
+            e_split = rel_l2(split, ref)
+            assert e_split < 1e-2 and e_split <= max(1.25 * e_whole, 5e-3), (e_split, e_whole)
+            if first is None:
+                first = split
+            else:
+                assert torch.equal(split, first), "the merge order is fixed: repeated calls are bit-identical"
+        ws = nat.attention_workspace(b, tq, tk, h, d, torch.device(DEV))
+        assert int(ws[:4096].view(torch.int32).abs().sum()) == 0, "arrival counters must return to zero"
+    finally:
+        nat.attention_force_split(0)
+
+
 def test_attention_bf16_config5_sequence():
     """BASELINE config 5 length (T = 33x22x38 = 27588, not a multiple of the 128-key tile)
     for two heads, against a float32 reference computed in query chunks."""

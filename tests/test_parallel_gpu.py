@@ -1,5 +1,10 @@
-"""Multi-GPU step (ltx_parallel) against the single-GPU step on the same inputs: each
-rank runs the same kernels on the same rows, so the next latent must be identical.
+"""Multi-GPU step (ltx_parallel) against the single-GPU step on the same inputs.
+
+With attention running every (sample, head, 256-query) unit whole, each rank runs the
+same kernels on the same rows as the single GPU, so the next latent must be identical.
+With the automatic attention plan the units that would only partly fill the last wave
+of SMs are split over key ranges, and ranks with fewer heads split other units than the
+single GPU does: there the next latent must agree to bf16 rounding (rel-L2 <= 1e-2).
 Needs >= 2 (or 4) visible GPUs; skipped otherwise."""
 
 import os
@@ -56,14 +61,27 @@ def _worker(rank, world, port, cfg_split, q):
         kf = torch.zeros(1, t, 1, device=dev)
         kf[:, : h * w_] = 1
         sigmas = torch.tensor([0.5, 0.25])
-        ref = ltx_dit.cfg_denoise_step(model, latent, pos, ctx[:1], ctx[1:], sigmas, 0, 3.0, keyframes_mask=kf,
-                                       fused_head=False)[2]
+        import _native as nat
+
+        def single():
+            return ltx_dit.cfg_denoise_step(model, latent, pos, ctx[:1], ctx[1:], sigmas, 0, 3.0, keyframes_mask=kf,
+                                            fused_head=False)[2]
+
+        nat.attention_force_split(-1)  # whole units everywhere: the exact comparison
+        ref = single()
         pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=cfg_split)
+        sp = model._sp
         out = pdn.step(latent, pos, ctx[:1], ctx[1:], sigmas, 0, 3.0, keyframes_mask=kf)
+        nat.attention_force_split(0)  # the automatic plan
+        model._sp = None
+        ref_auto = single()
+        model._sp = sp
+        out_auto = pdn.step(latent, pos, ctx[:1], ctx[1:], sigmas, 0, 3.0, keyframes_mask=kf)
         torch.cuda.synchronize()
         model._sp = None
         diff = (out.float() - ref.float()).abs().max().item()
-        q.put((rank, diff, pdn.layout.cfg, pdn.layout.sp))
+        rel = float((out_auto.float() - ref_auto.float()).norm() / ref_auto.float().norm())
+        q.put((rank, diff, rel, pdn.layout.cfg, pdn.layout.sp))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -83,7 +101,9 @@ def test_parallel_step_equals_single_gpu(world, cfg_split):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert all(d == 0.0 for _, d, _, _ in res), res
+    print("\nper rank (max |diff| whole units, rel-L2 automatic plan):", [(r, d, e) for r, d, e, _, _ in res])
+    assert all(d == 0.0 for _, d, _, _, _ in res), res
+    assert all(e < 1e-2 for _, _, e, _, _ in res), res
 
 
 def _av_worker(rank, world, port, cfg_split, q):
