@@ -148,6 +148,12 @@ __device__ __forceinline__ void fmha_body(const CUtensorMap* tmQ_, const CUtenso
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if constexpr (!PART) {
+    // the kernels ahead in the stream (which write q, k, v) complete before any access;
+    // only then may the next kernel (the split units' parts among them) be scheduled
+    pdl_wait();
+    pdl_trigger();
+  }
 
   if (warp == 8) {
     // ------------------------------ TMA producer ------------------------------
@@ -608,10 +614,6 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
                    int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
                    float* __restrict__ o32, float* __restrict__ lse, int64_t ld_lse, const int n_whole) {
-  // Let the part kernel (launched after this one with programmatic stream
-  // serialisation) take SMs as soon as this grid's last wave is resident: it needs
-  // nothing this grid writes.
-  asm volatile("griddepcontrol.launch_dependents;");
   // whole units only: the units from n_whole on run as parts (fmha_part_kernel)
   if (int(blockIdx.x) + int(gridDim.x) * (int(blockIdx.y) + int(gridDim.y) * int(blockIdx.z)) >= n_whole) return;
   const FaSched none{};
@@ -627,6 +629,10 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
                      const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
                      int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
                      const int tk_part, const FaSched sch) {
+  // Launched after fmha_tc_kernel, whose CTAs let it be scheduled only once the kernels
+  // writing q, k and v have completed; it needs nothing that grid writes, so it starts
+  // at once, and it lets the next kernel be scheduled (which waits for its completion).
+  pdl_trigger();
   const int p = int(blockIdx.x);
   const int su = p / sch.split_k, part = p % sch.split_k;
   const int unit = sch.n_full + su;
@@ -711,6 +717,8 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 8) {
     // ------------------------------ TMA producer ------------------------------
@@ -1048,10 +1056,9 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   }
   const dim3 grid{unsigned(nq2), unsigned(H), unsigned(B)};
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk),
-                                             scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate, o32, lse,
-                                             ld_lse, sch.n_full),
-      ltx::note_launch();
+  launch_pdl(kern, grid, dim3(Cfg::THREADS), Cfg::SMEM, s, 1, tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo,
+             int(Tq), int(Tk), scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate, o32, lse, ld_lse,
+             sch.n_full);
   if (sch.n_split > 0) {
     auto pk = fmha_part_kernel<D>;
     static std::atomic<uint64_t> smem_done_p{0};
@@ -1089,9 +1096,8 @@ void launch_fmha_kv1(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   const int64_t n_tasks = int64_t(B) * H * n_qt;
   const int grid = int(std::min<int64_t>(n_tasks, num_sms()));
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, 320, Cfg::SMEM, s>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo, int(Tq), int(Tk), H, n_qt,
-                                    n_tasks, scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate),
-      ltx::note_launch();
+  launch_pdl(kern, dim3(unsigned(grid)), dim3(320), Cfg::SMEM, s, 1, tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo,
+             int(Tq), int(Tk), H, n_qt, n_tasks, scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate);
 }
 
 // ---------------------------------------------------------------------------------

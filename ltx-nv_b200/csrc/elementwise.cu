@@ -107,6 +107,8 @@ __global__ void __launch_bounds__(256) norm_rows_bf16_kernel(const __nv_bfloat16
   const int64_t r0 = b * rows_per_batch + int64_t(chunk) * rows_per_chunk;
   const int64_t r1 = min(min(r0 + rows_per_chunk, (b + 1) * rows_per_batch), rows);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
   // The first row of each warp is loaded before the vectors are built, and every
   // later row one row ahead of its use.
   uint4 raw[NC];
@@ -272,6 +274,8 @@ __global__ void __launch_bounds__(256, 2) qk_rows_bf16_kernel(__nv_bfloat16* __r
   const int per_head = d >> 4;
   const float inv_D = 1.f / float(32 * NI * 16);
   const int n_parts = w2 != nullptr ? 2 : 1;
+  pdl_wait();
+  pdl_trigger();
   for (int64_t r = r0 + warp; r < r1; r += 8) {
     const int64_t b = r / rows_per_batch, t = r - b * rows_per_batch;
     const int64_t ro = b * rope_ld_batch + t * ld_rope;
@@ -681,6 +685,8 @@ __global__ void sp_pack_kernel(const uint4* __restrict__ src, int64_t ld_src8, i
   const int W8 = seg.W >> 3;
   const int64_t total = int64_t(parts) * rows * W8;
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int64_t j = i / (rows * W8);
     const int64_t rem = i - j * rows * W8;
@@ -699,6 +705,8 @@ __global__ void sp_unpack_kernel(const uint4* __restrict__ src, int64_t rows, in
                                  uint4* __restrict__ dst, int64_t ld_dst8) {
   const int64_t total = int64_t(parts) * rows * w8;
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
     const int64_t r = i / (int64_t(parts) * w8);
     const int64_t rem = i - r * parts * w8;
@@ -742,9 +750,8 @@ void launch_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ldy, int6
       const int64_t chunks = (std::min<int64_t>(rpb, rows) + per - 1) / per;
       const unsigned grid = unsigned(n_samples * chunks);
 #define LTX_NORM_ROWS(NCV)                                                                                  \
-  norm_rows_bf16_kernel<NCV><<<grid, 256, 0, s>>>(xp, ldx, yp, ldy, rows, rpb, int(chunks), int(per), kind, eps, \
-                                                  sh, sc),                                                    \
-      ltx::note_launch()
+  launch_pdl(norm_rows_bf16_kernel<NCV>, dim3(grid), dim3(256), 0, s, 1, xp, ldx, yp, ldy, rows, rpb, int(chunks), \
+             int(per), kind, eps, sh, sc)
       switch (nc) {
         case 1: LTX_NORM_ROWS(1); break;
         case 2: LTX_NORM_ROWS(2); break;
@@ -839,9 +846,8 @@ extern "C" int ltx_qk_norm_rope_pair(void* x, int64_t ldx, int64_t k_offset, int
   auto cb = static_cast<const __nv_bfloat16*>(cos_tab);
   auto sb = static_cast<const __nv_bfloat16*>(sin_tab);
 #define LTX_QK_PAIR(NIV)                                                                                           \
-  qk_rows_bf16_kernel<NIV><<<grid, 256, 0, s>>>(xb, ldx, rows, rows_per_batch, per, head_dim, wq, eps, cb, sb, ld_rope, \
-                                                rope_ld_batch, wk, k_offset),                                          \
-      ltx::note_launch()
+  launch_pdl(qk_rows_bf16_kernel<NIV>, dim3(grid), dim3(256), 0, s, 1, xb, ldx, rows, rows_per_batch, per, head_dim, \
+             wq, eps, cb, sb, ld_rope, rope_ld_batch, wk, k_offset)
   switch (ni) {
     case 1: LTX_QK_PAIR(1); break;
     case 2: LTX_QK_PAIR(2); break;
@@ -889,9 +895,8 @@ extern "C" int ltx_qk_norm_rope(void* x, int64_t ldx, int64_t rows, int64_t rows
     auto cb = static_cast<const __nv_bfloat16*>(cos_tab);
     auto sb = static_cast<const __nv_bfloat16*>(sin_tab);
 #define LTX_QK_ROWS(NIV)                                                                                    \
-  qk_rows_bf16_kernel<NIV><<<grid, 256, 0, s>>>(xb, ldx, rows, rows_per_batch, per, head_dim, wb, eps, cb, sb, \
-                                                ld_rope, rope_ld_batch),                                      \
-      ltx::note_launch()
+  launch_pdl(qk_rows_bf16_kernel<NIV>, dim3(grid), dim3(256), 0, s, 1, xb, ldx, rows, rows_per_batch, per, head_dim, \
+             wb, eps, cb, sb, ld_rope, rope_ld_batch, static_cast<const __nv_bfloat16*>(nullptr), int64_t(0))
     switch (ni) {
       case 1: LTX_QK_ROWS(1); break;
       case 2: LTX_QK_ROWS(2); break;

@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(320, 1)
   }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -540,24 +542,12 @@ void launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, void* C, 
   if constexpr (PAIR) {
     // one CTA pair per two SMs, persistent over the 256-row tiles
     const int64_t pairs = std::min<int64_t>(num_sms() / 2, tiles);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned(2 * pairs));
-    cfg.blockDim = dim3(320);
-    cfg.dynamicSmemBytes = Cfg::SMEM;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    LTX_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, Cp, ldc, int(M), int(N), int(K), epi));
-    ltx::note_launch();
+    launch_pdl(kern, dim3(unsigned(2 * pairs)), dim3(320), Cfg::SMEM, s, 2, ta, tb, Cp, ldc, int(M), int(N), int(K),
+               epi);
   } else {
     int64_t grid = num_sms();
     if (tiles < grid) grid = tiles;
-    kern<<<unsigned(grid), 320, Cfg::SMEM, s>>>(ta, tb, Cp, ldc, int(M), int(N), int(K), epi), ltx::note_launch();
+    launch_pdl(kern, dim3(unsigned(grid)), dim3(320), Cfg::SMEM, s, 1, ta, tb, Cp, ldc, int(M), int(N), int(K), epi);
   }
 }
 

@@ -390,6 +390,12 @@ LTX_DEVICE void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 LTX_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Programmatic dependent launch (see launch_pdl): wait until the kernels ahead of this
+// one in the stream have completed and their memory is visible; then let the next
+// kernel of the stream be scheduled.
+LTX_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LTX_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Barrier `id` (1..15; 0 is __syncthreads) over the first `threads` threads' warps.
 LTX_DEVICE void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

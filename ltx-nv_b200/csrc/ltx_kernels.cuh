@@ -4,7 +4,41 @@
 #include "ltx_common.cuh"
 #include "ltx_internal.h"
 
+#include <utility>
+
 namespace ltx {
+
+// Launch with programmatic stream serialisation: the grid may be scheduled while the
+// previous kernel of the stream is still running (once all of that kernel's CTAs have
+// executed pdl_trigger or exited). Every kernel launched this way calls pdl_wait (all
+// threads) after its on-chip prologue and before its first global-memory access, and
+// pdl_trigger after that wait, so a kernel never reads or writes global memory before
+// the kernels ahead of it in the stream have completed.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  LTX_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+  note_launch();
+}
 
 // One adaLN vector: v[c] = round(table[toff + c] + mod[b*ldb + t*ldt + moff + c]).
 // Mirrors get_ada_values (ltx_dit.py:192-198): the table row and the timestep

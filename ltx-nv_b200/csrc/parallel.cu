@@ -41,9 +41,8 @@ extern "C" int ltx_sp_pack(const void* src, int64_t ld_src, int64_t rows, int pa
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = int64_t(num_sms()) * 16;
   if (blocks > cap) blocks = cap;
-  sp_pack_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(src), ld_src * esz / 16, rows, parts, seg, static_cast<uint4*>(dst)),
-      ltx::note_launch();
+  launch_pdl(sp_pack_kernel, dim3(unsigned(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream), 1,
+             static_cast<const uint4*>(src), ld_src * esz / 16, rows, parts, seg, static_cast<uint4*>(dst));
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
@@ -64,9 +63,8 @@ extern "C" int ltx_sp_unpack(const void* src, int64_t rows, int parts, int w, vo
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = int64_t(num_sms()) * 16;
   if (blocks > cap) blocks = cap;
-  sp_unpack_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(src), rows, parts, w8, static_cast<uint4*>(dst), ld_dst * esz / 16),
-      ltx::note_launch();
+  launch_pdl(sp_unpack_kernel, dim3(unsigned(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream), 1,
+             static_cast<const uint4*>(src), rows, parts, w8, static_cast<uint4*>(dst), ld_dst * esz / 16);
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
