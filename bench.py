@@ -344,6 +344,8 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
     # a graph that holds NCCL calls is released before the process group goes away
     used_graph = graph is not None
     del graph
+    if world > 1:
+        pdn.close()  # the peer-memory exchange buffers, on every rank
     torch.cuda.synchronize(dev)
 
     if rank != 0:

@@ -4,8 +4,9 @@
  *
  * Conventions
  *  - Every pointer argument is a device pointer owned by the caller. The library
- *    allocates device memory in one place only: ltx_dit_reserve sizes the workspace an
- *    ltx_ctx owns for the whole-step entry point (freed by ltx_ctx_destroy).
+ *    allocates device memory in two places only: ltx_dit_reserve sizes the workspace an
+ *    ltx_ctx owns for the whole-step entry point (freed by ltx_ctx_destroy), and
+ *    ltx_peer_alloc allocates a buffer that other processes map (ltx_peer_free).
  *  - `stream` is a cudaStream_t passed as void*; every call is asynchronous on it and
  *    performs no device synchronisation.
  *  - Every entry point returns LTX_OK (0) or an ltx_status error code; ltx_last_error()
@@ -47,7 +48,8 @@ int ltx_abi_version(void);
  * counterpart. */
 uint64_t ltx_launch_count(void);
 /* Read (and clear when `clear` != 0) the device error word that bounded waits set when
- * they give up (1 = mbarrier wait timed out). Synchronises `stream`. */
+ * they give up (1 = mbarrier wait timed out, 2 = sequence-parallel peer barrier timed
+ * out). Synchronises `stream`. */
 int ltx_device_error_flags(int* flags, int clear, void* stream);
 
 /* ---------------------------------------------------------------------------------- */
@@ -278,6 +280,44 @@ int ltx_sp_pack(const void* src, int64_t ld_src, int64_t rows, int parts, int n_
 /* dst[r][j*w, (j+1)*w) = src[j][r][:] for j < parts, r < rows. */
 int ltx_sp_unpack(const void* src, int64_t rows, int parts, int w, void* dst, int64_t ld_dst, int dtype,
                   void* stream);
+
+/* The same exchange fused into the kernels on either side of it, over NVLink peer memory
+ * (no counterpart in the reference, which runs on one GPU). Every SP rank owns one
+ * buffer from ltx_peer_alloc (cudaMalloc'd and zero-filled, with a 64-byte CUDA IPC
+ * handle that the other ranks of the node pass to ltx_peer_open to map it); kernels only
+ * store to peer memory and load local memory.
+ *
+ * ltx_qk_norm_rope_scatter: ltx_qk_norm_rope_pair on x = (rows, [q | k | v | gate])
+ * rows of this rank (rows_per_batch tokens per sample, D = heads * head_dim wide blocks,
+ * gate logits when gated), except that the rows are not written back: the q, k, v
+ * columns and gate logits of the heads of SP rank j (heads / parts of them) go to row
+ * b * rows_per_batch * parts + sp_rank * rows_per_batch + t of dst[j], laid out
+ * [q | k | v | gate] of width 3 * D / parts (+ heads / parts): the receive buffer that
+ * pack + all-to-all would fill. bf16 only.
+ * ltx_attention_scatter: self-attention over the B x T tokens of the receive buffer
+ * (as ltx_attention_ws, with the same workspace), each output row written to the rank
+ * that owns its token: row t of sample b to row b * (T / parts) + t % (T / parts) of
+ * out[t / (T / parts)], columns out_col0 .. out_col0 + heads * head_dim (what
+ * all-to-all + unpack would deliver). bf16 only, T > 128.
+ * ltx_sp_barrier: every rank of the SP group calls it in the same order; it returns
+ * (asynchronously, on `stream`) once every rank's preceding kernels have completed their
+ * stores. flags[j] is rank j's flag array (`parts` ints, zero-filled) as mapped in this
+ * process, counter a zero-filled int of this rank. A wait that lasts limit_cycles SM
+ * cycles gives up: bit 2 of the device error word (ltx_device_error_flags). */
+int ltx_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int ltx_peer_open(const void* ipc_handle, void** ptr);
+int ltx_peer_close(void* ptr);
+int ltx_peer_free(void* ptr);
+int ltx_qk_norm_rope_scatter(const void* x, int64_t ldx, int64_t rows, int64_t rows_per_batch, int heads,
+                             int head_dim, const void* q_weight, const void* k_weight, float eps, const void* cos_tab,
+                             const void* sin_tab, int64_t ld_rope, int64_t rope_ld_batch, int gated, int parts,
+                             int sp_rank, void* const* dst, int64_t ld_dst, void* stream);
+int ltx_attention_scatter(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, int B,
+                          int64_t T, int heads, int head_dim, float scale, const void* gate_logits, int64_t ld_gate,
+                          void* workspace, size_t workspace_bytes, int parts, void* const* out, int64_t out_ld,
+                          int out_col0, void* stream);
+int ltx_sp_barrier(int* const* flags, int* counter, int parts, int rank, unsigned long long limit_cycles,
+                   void* stream);
 
 /* Split-KV attention across ranks (the audio queries of the video-to-audio attention,
  * ltx_dit.py:299-307, against video keys sharded by sequence parallelism). No counterpart

@@ -163,6 +163,19 @@ _SIGNATURES = {
     "ltx_sp_pack": (ctypes.c_int, [c_vp, c_i64, c_i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                    ctypes.POINTER(ctypes.c_int), c_vp, ctypes.c_int, c_vp]),
     "ltx_sp_unpack": (ctypes.c_int, [c_vp, c_i64, ctypes.c_int, ctypes.c_int, c_vp, c_i64, ctypes.c_int, c_vp]),
+    "ltx_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(c_vp), c_vp]),
+    "ltx_peer_open": (ctypes.c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "ltx_peer_close": (ctypes.c_int, [c_vp]),
+    "ltx_peer_free": (ctypes.c_int, [c_vp]),
+    "ltx_qk_norm_rope_scatter": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i64, ctypes.c_int, ctypes.c_int, c_vp, c_vp,
+                                                ctypes.c_float, c_vp, c_vp, c_i64, c_i64, ctypes.c_int, ctypes.c_int,
+                                                ctypes.c_int, ctypes.POINTER(c_vp), c_i64, c_vp]),
+    "ltx_attention_scatter": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, ctypes.c_int, c_i64,
+                                             ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, c_vp,
+                                             ctypes.c_size_t, ctypes.c_int, ctypes.POINTER(c_vp), c_i64, ctypes.c_int,
+                                             c_vp]),
+    "ltx_sp_barrier": (ctypes.c_int, [ctypes.POINTER(c_vp), c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_ulonglong,
+                                      c_vp]),
     "ltx_guide": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, ctypes.c_float, c_vp,
                                  ctypes.c_int, c_vp]),
     "ltx_euler": (ctypes.c_int, [c_vp, c_vp, c_i64, ctypes.c_float, ctypes.c_float, c_vp, ctypes.c_int, c_vp]),
@@ -543,6 +556,67 @@ def sp_unpack(src: torch.Tensor, parts: int, dst: torch.Tensor) -> None:
     """dst (rows, parts*w) <- src (parts, rows, w)."""
     p, rows, w = src.shape
     _call("ltx_sp_unpack", _ptr(src), rows, parts, w, _ptr(dst), _ld(dst), _dt(src), _stream(src))
+
+
+def peer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """A zero-filled device buffer other processes of the node can map: (pointer, 64-byte
+    CUDA IPC handle). Freed with peer_free."""
+    ptr = c_vp()
+    handle = ctypes.create_string_buffer(64)
+    _call("ltx_peer_alloc", nbytes, ctypes.byref(ptr), ctypes.cast(handle, c_vp))
+    return int(ptr.value), handle.raw
+
+
+def peer_open(handle: bytes) -> int:
+    """Map another process's peer_alloc buffer into this one (its device pointer here)."""
+    ptr = c_vp()
+    buf = ctypes.create_string_buffer(handle, 64)
+    _call("ltx_peer_open", ctypes.cast(buf, c_vp), ctypes.byref(ptr))
+    return int(ptr.value)
+
+
+def peer_close(ptr: int) -> None:
+    _call("ltx_peer_close", ptr)
+
+
+def peer_free(ptr: int) -> None:
+    _call("ltx_peer_free", ptr)
+
+
+def _ptr_array(ptrs: list[int]):
+    return (c_vp * len(ptrs))(*ptrs)
+
+
+def qk_norm_rope_scatter(x: torch.Tensor, rows_per_batch: int, heads: int, head_dim: int, q_weight: torch.Tensor,
+                         k_weight: torch.Tensor, eps: float, cos: torch.Tensor | None, sin: torch.Tensor | None,
+                         gated: bool, sp_rank: int, dst: list[int], ld_dst: int, rope_ld_batch: int = 0) -> None:
+    """Self-attention q/k RMSNorm + RoPE of x (rows, [q | k | v | gate]) with the rows sent
+    to the SP ranks' receive buffers (dst[j], row stride ld_dst) instead of written back."""
+    _call("ltx_qk_norm_rope_scatter", _ptr(x), _ld(x), x.shape[0], rows_per_batch, heads, head_dim, _ptr(q_weight),
+          _ptr(k_weight), eps, _ptr(cos), _ptr(sin), _ld(cos) if cos is not None else 0, rope_ld_batch, int(gated),
+          len(dst), sp_rank, _ptr_array(dst), ld_dst, _stream(x),
+          label="ltx_qk_norm_rope_scatter" if _profile is not None else None)
+
+
+def attention_scatter(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, batch: int, t: int, heads: int,
+                      head_dim: int, scale: float, gate_logits: torch.Tensor | None, out: list[int], out_ld: int,
+                      out_col0: int) -> None:
+    """Self-attention over the receive buffer (batch x t tokens) with each output row
+    written to its token owner's buffer (out[j], rows t / len(out) per sample)."""
+    ws = attention_workspace(batch, t, t, heads, head_dim, q.device)
+    _call("ltx_attention_scatter", _ptr(q), _ld(q), _ptr(k), _ld(k), _ptr(v), _ld(v), batch, t, heads, head_dim,
+          scale, _ptr(gate_logits), _ld(gate_logits) if gate_logits is not None else 0, _ptr(ws),
+          ws.numel() if ws is not None else 0, len(out), _ptr_array(out), out_ld, out_col0, _stream(q),
+          label=f"attention B={batch} H={heads} Tq={t} Tk={t} d={head_dim} (scatter)" if _profile is not None
+          else None)
+
+
+def sp_barrier(flags: list[int], counter: int, rank: int, limit_cycles: int = 4_000_000_000,
+               stream: torch.cuda.Stream | None = None) -> None:
+    """Flag barrier of the SP group over peer memory (see ltx_sp_barrier)."""
+    s = (stream or torch.cuda.current_stream()).cuda_stream
+    _call("ltx_sp_barrier", _ptr_array(flags), counter, len(flags), rank, limit_cycles, s,
+          label="ltx_sp_barrier" if _profile is not None else None)
 
 
 def _same_elementwise(*ts: torch.Tensor) -> None:

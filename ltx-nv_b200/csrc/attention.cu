@@ -74,9 +74,27 @@ struct FaSched {
   float* part_o;    // [n_split * split_k][256][D]
   float* part_lse;  // [n_split * split_k][256]
   int* counters;    // [n_split], zero before the first launch, left at zero
+  // Output scatter (sequence-parallel exchange), when out_rows > 0: row qi of sample b goes
+  // to row b * out_rows + qi % out_rows of owner qi / out_rows's buffer out[owner] (row
+  // stride out_ld), columns from out_col0 + h * D on; O is not written.
+  __nv_bfloat16* out[8];
+  int64_t out_rows, out_ld;
+  int out_col0;
 };
 
 constexpr int kFaMaxSplit = 8;
+
+// Output row qi of sample b, head h: in O, or scattered to its token owner's buffer.
+template <int D>
+LTX_DEVICE __nv_bfloat16* fa_out_row(__nv_bfloat16* O, int64_t ldo, int Tq, int b, int h, int64_t qi,
+                                     const FaSched& sch) {
+  if (sch.out_rows > 0) {
+    const int64_t owner = qi / sch.out_rows;
+    return sch.out[owner] + (int64_t(b) * sch.out_rows + (qi - owner * sch.out_rows)) * sch.out_ld + sch.out_col0 +
+           int64_t(h) * D;
+  }
+  return O + (int64_t(b) * Tq + qi) * ldo + int64_t(h) * D;
+}
 
 // Exponential pairs (of the 64 in a 128-key row of S) computed on the FMA pipe by the
 // cubic of ex2_poly2 instead of the special-function unit, bit j = pair j.
@@ -540,7 +558,7 @@ __device__ __forceinline__ void fmha_body(const CUtensorMap* tmQ_, const CUtenso
                 o2 *= g;
                 o3 *= g;
               }
-              *reinterpret_cast<uint2*>(O + (int64_t(b) * Tq + qr) * ldo + int64_t(h) * D + col) =
+              *reinterpret_cast<uint2*>(fa_out_row<D>(O, ldo, Tq, b, h, qr, sch) + col) =
                   make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
             }
           }
@@ -577,7 +595,7 @@ __device__ __forceinline__ void fmha_body(const CUtensorMap* tmQ_, const CUtenso
           const float sg = round_bf16(1.f / (1.f + expf(-lg)));
           g = round_bf16(2.f * sg);
         }
-        __nv_bfloat16* op = O + orow * ldo + int64_t(h) * D;
+        __nv_bfloat16* op = fa_out_row<D>(O, ldo, Tq, b, h, qi < Tq ? qi : 0, sch);  // stored only if qi < Tq
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
           uint32_t rr[32];
@@ -613,12 +631,11 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
     fmha_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
                    int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
-                   float* __restrict__ o32, float* __restrict__ lse, int64_t ld_lse, const int n_whole) {
-  // whole units only: the units from n_whole on run as parts (fmha_part_kernel)
-  if (int(blockIdx.x) + int(gridDim.x) * (int(blockIdx.y) + int(gridDim.y) * int(blockIdx.z)) >= n_whole) return;
-  const FaSched none{};
+                   float* __restrict__ o32, float* __restrict__ lse, int64_t ld_lse, const FaSched sch) {
+  // whole units only: the units from n_full on run as parts (fmha_part_kernel)
+  if (int(blockIdx.x) + int(gridDim.x) * (int(blockIdx.y) + int(gridDim.y) * int(blockIdx.z)) >= sch.n_full) return;
   fmha_body<D, false>(&tmQ, &tmK, &tmV, O, ldo, Tq, Tk, scale_log2, gate, ld_gate, o32, lse, ld_lse,
-                      int(blockIdx.y), int(blockIdx.z), int(blockIdx.x) * 2 * FaCfg<D>::BM, 0, 0, -1, -1, none);
+                      int(blockIdx.y), int(blockIdx.z), int(blockIdx.x) * 2 * FaCfg<D>::BM, 0, 0, -1, -1, sch);
 }
 
 // The split units' parts, one CTA each (CTA p = part p % split_k of unit n_full + p /
@@ -1031,7 +1048,9 @@ template <int D>
 void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
                     int64_t ldo, int B, int64_t Tq, int64_t Tk, int H, float scale, const void* gate,
                     int64_t ld_gate, cudaStream_t s, float* o32 = nullptr, float* lse = nullptr,
-                    int64_t ld_lse = 0, void* workspace = nullptr, size_t ws_bytes = 0) {
+                    int64_t ld_lse = 0, void* workspace = nullptr, size_t ws_bytes = 0,
+                    void* const* out_parts = nullptr, int parts = 0, int64_t out_rows = 0, int64_t out_ld = 0,
+                    int out_col0 = 0) {
   using Cfg = FaCfg<D>;
   const uint64_t cols = uint64_t(H) * D;
   const CUtensorMap tq = make_tmap_bf16_2d(q, cols, uint64_t(B) * Tq, uint64_t(ldq), 64, 128);
@@ -1041,7 +1060,18 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   static std::atomic<uint64_t> smem_done{0};
   ensure_smem_limit(smem_done, kern, Cfg::SMEM);
   const int nq2 = int((Tq + 2 * Cfg::BM - 1) / (2 * Cfg::BM));
-  FaSched sch{B, H, nq2, int(int64_t(B) * H * nq2), 0, 1, nullptr, nullptr, nullptr};
+  FaSched sch{};
+  sch.B = B;
+  sch.H = H;
+  sch.nq2 = nq2;
+  sch.n_full = int(int64_t(B) * H * nq2);
+  sch.split_k = 1;
+  if (out_parts != nullptr) {
+    for (int j = 0; j < parts; ++j) sch.out[j] = static_cast<__nv_bfloat16*>(out_parts[j]);
+    sch.out_rows = out_rows;
+    sch.out_ld = out_ld;
+    sch.out_col0 = out_col0;
+  }
   if (o32 == nullptr && workspace != nullptr) {
     const FaPlan p = fa_plan_for(B, Tq, Tk, H);
     if (p.n_split > 0 && ws_bytes >= fa_workspace_bytes(p, D)) {
@@ -1057,8 +1087,7 @@ void launch_fmha_tc(const void* q, int64_t ldq, const void* k, int64_t ldk, cons
   const dim3 grid{unsigned(nq2), unsigned(H), unsigned(B)};
   const float scale_log2 = scale * 1.4426950408889634f;
   launch_pdl(kern, grid, dim3(Cfg::THREADS), Cfg::SMEM, s, 1, tq, tk, tv, static_cast<__nv_bfloat16*>(o), ldo,
-             int(Tq), int(Tk), scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate, o32, lse, ld_lse,
-             sch.n_full);
+             int(Tq), int(Tk), scale_log2, static_cast<const __nv_bfloat16*>(gate), ld_gate, o32, lse, ld_lse, sch);
   if (sch.n_split > 0) {
     auto pk = fmha_part_kernel<D>;
     static std::atomic<uint64_t> smem_done_p{0};
@@ -1231,5 +1260,39 @@ extern "C" int ltx_test_attention_force_split(int parts) {
   LTX_API_BEGIN
   LTX_REQUIRE(parts >= -1 && parts <= kFaMaxSplit, "parts must be in [-1, 8]");
   g_fa_force_split = parts;
+  LTX_API_END
+}
+
+extern "C" int ltx_attention_scatter(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                     int64_t ldv, int B, int64_t T, int heads, int head_dim, float scale,
+                                     const void* gate_logits, int64_t ld_gate, void* workspace, size_t workspace_bytes,
+                                     int parts, void* const* out, int64_t out_ld, int out_col0, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(q && k && v && out, "q, k, v and out must be non-NULL");
+  LTX_REQUIRE(B > 0 && T > 128 && heads > 0, "B and heads must be positive, T > 128");
+  LTX_UNSUPPORTED(head_dim == 64 || head_dim == 128, "bf16 attention supports head_dim 64 and 128");
+  LTX_REQUIRE(parts >= 1 && parts <= 8 && T % parts == 0, "parts must be 1..8 and divide T");
+  LTX_REQUIRE(int64_t(B) * T < (int64_t(1) << 31), "too many rows");
+  const int64_t inner = int64_t(heads) * head_dim;
+  LTX_REQUIRE(ldq >= inner && ldk >= inner && ldv >= inner, "leading dimensions too small");
+  LTX_REQUIRE(ldq % 8 == 0 && ldk % 8 == 0 && ldv % 8 == 0 && out_ld % 8 == 0 && out_col0 % 8 == 0,
+              "leading dims and out_col0 must be multiples of 8");
+  LTX_REQUIRE(out_ld >= out_col0 + inner, "out_ld too small");
+  if (gate_logits) LTX_REQUIRE(ld_gate >= heads, "ld_gate must be >= heads");
+  check_vec_ptr(q, "q");
+  check_vec_ptr(k, "k");
+  check_vec_ptr(v, "v");
+  for (int j = 0; j < parts; ++j) {
+    LTX_REQUIRE(out[j] != nullptr, "out[j] is NULL");
+    check_vec_ptr(out[j], "out[j]");
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (head_dim == 64)
+    launch_fmha_tc<64>(q, ldq, k, ldk, v, ldv, nullptr, 0, B, T, T, heads, scale, gate_logits, ld_gate, s, nullptr,
+                       nullptr, 0, workspace, workspace_bytes, out, parts, T / parts, out_ld, out_col0);
+  else
+    launch_fmha_tc<128>(q, ldq, k, ldk, v, ldv, nullptr, 0, B, T, T, heads, scale, gate_logits, ld_gate, s, nullptr,
+                        nullptr, 0, workspace, workspace_bytes, out, parts, T / parts, out_ld, out_col0);
+  LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

@@ -252,20 +252,30 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(T* __restrict__ x, i
   }
 }
 
+// Destinations of the sequence-parallel exchange fused into the self-attention q/k pass
+// (ltx_qk_norm_rope_scatter): row t of sample b of this rank's tokens goes to row
+// b * t_full + row0 + t of every SP rank's receive buffer, which holds
+// [q | k | v | gate logits] of that rank's hp heads (widths dp, dp, dp, hp).
+struct SpScatter {
+  __nv_bfloat16* dst[8];  // receive buffer of SP rank j, as mapped in this process
+  int64_t ld, t_full, row0;
+  int hp, dp, v_off, gate_off;  // gate_off < 0: no gate logits
+};
+
 // Fast path of the same op for bf16: one warp per row, NI slots of (head, 8 pairs) per
 // lane, no block-wide reduction, the roundings done two to a packed conversion. Same
 // rounding sequence as above. Rows stay packed in registers between the sum-of-squares
 // pass and the output pass, which keeps enough warps resident to cover the load
-// latency.
-template <int NI>
+// latency. SCATTER: the rows are not written back but sent, with the row's v and gate
+// logits, to the SP ranks' receive buffers (SpScatter).
+template <int NI, bool SCATTER = false>
 __global__ void __launch_bounds__(256, 2) qk_rows_bf16_kernel(__nv_bfloat16* __restrict__ x, int64_t ldx, int64_t rows,
                                                            int64_t rows_per_batch, int rows_per_cta, int d,
                                                            const __nv_bfloat16* __restrict__ w, float eps,
                                                            const __nv_bfloat16* __restrict__ cos_t,
                                                            const __nv_bfloat16* __restrict__ sin_t, int64_t ld_rope,
-                                                           int64_t rope_ld_batch,
-                                                           const __nv_bfloat16* __restrict__ w2 = nullptr,
-                                                           int64_t off2 = 0) {
+                                                           int64_t rope_ld_batch, const __nv_bfloat16* __restrict__ w2,
+                                                           int64_t off2, const SpScatter sc) {
   // w2 != nullptr: a second column block at off2 (self-attention k) is normalised with
   // w2 and rotated with the same RoPE entries, which are loaded once per row.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -289,6 +299,12 @@ __global__ void __launch_bounds__(256, 2) qk_rows_bf16_kernel(__nv_bfloat16* __r
         rs[i] = *reinterpret_cast<const uint4*>(sin_t + ro + h * (d >> 1) + j0);
       }
     }
+    const int64_t drow = SCATTER ? b * sc.t_full + sc.row0 + t : 0;  // row in the receive buffers
+    // destination of (head h, column c within the head) of column block `part`
+    auto dst_of = [&](int part, int h, int c) -> __nv_bfloat16* {
+      const int j = h / sc.hp;
+      return sc.dst[j] + drow * sc.ld + part * sc.dp + (h - j * sc.hp) * d + c;
+    };
     for (int part = 0; part < n_parts; ++part) {
     __nv_bfloat16* xr = x + r * ldx + (part ? off2 : 0);
     const __nv_bfloat16* wp = part ? w2 : w;
@@ -356,13 +372,39 @@ __global__ void __launch_bounds__(256, 2) qk_rows_bf16_kernel(__nv_bfloat16* __r
           o1[k] = __fsub_rn(p1, p2);
           o2[k] = __fadd_rn(p3, p4);
         }
-        st8<__nv_bfloat16>(xr + c1, o1);
-        st8<__nv_bfloat16>(xr + c1 + (d >> 1), o2);
+        if constexpr (SCATTER) {
+          st8<__nv_bfloat16>(dst_of(part, h, j0), o1);
+          st8<__nv_bfloat16>(dst_of(part, h, j0 + (d >> 1)), o2);
+        } else {
+          st8<__nv_bfloat16>(xr + c1, o1);
+          st8<__nv_bfloat16>(xr + c1 + (d >> 1), o2);
+        }
       } else {
-        st8<__nv_bfloat16>(xr + c1, a);
-        st8<__nv_bfloat16>(xr + c1 + (d >> 1), bb);
+        if constexpr (SCATTER) {
+          st8<__nv_bfloat16>(dst_of(part, h, j0), a);
+          st8<__nv_bfloat16>(dst_of(part, h, j0 + (d >> 1)), bb);
+        } else {
+          st8<__nv_bfloat16>(xr + c1, a);
+          st8<__nv_bfloat16>(xr + c1 + (d >> 1), bb);
+        }
       }
     }
+    }
+    if constexpr (SCATTER) {
+      // v and the gate logits of the row, unchanged, to the owners of their heads
+      const int D = 32 * NI * 16;
+      const __nv_bfloat16* xv = x + r * ldx + sc.v_off;
+      for (int u = lane; u < D / 8; u += 32) {
+        const int h = (u * 8) / d, c = u * 8 - h * d;
+        *reinterpret_cast<uint4*>(dst_of(2, h, c)) = *reinterpret_cast<const uint4*>(xv + u * 8);
+      }
+      if (sc.gate_off >= 0) {
+        const int heads = D / d;
+        for (int h = lane; h < heads; h += 32) {
+          const int j = h / sc.hp;
+          sc.dst[j][drow * sc.ld + 3 * sc.dp + (h - j * sc.hp)] = x[r * ldx + sc.gate_off + h];
+        }
+      }
     }
   }
 }
@@ -846,8 +888,8 @@ extern "C" int ltx_qk_norm_rope_pair(void* x, int64_t ldx, int64_t k_offset, int
   auto cb = static_cast<const __nv_bfloat16*>(cos_tab);
   auto sb = static_cast<const __nv_bfloat16*>(sin_tab);
 #define LTX_QK_PAIR(NIV)                                                                                           \
-  launch_pdl(qk_rows_bf16_kernel<NIV>, dim3(grid), dim3(256), 0, s, 1, xb, ldx, rows, rows_per_batch, per, head_dim, \
-             wq, eps, cb, sb, ld_rope, rope_ld_batch, wk, k_offset)
+  launch_pdl(qk_rows_bf16_kernel<NIV, false>, dim3(grid), dim3(256), 0, s, 1, xb, ldx, rows, rows_per_batch, per, \
+             head_dim, wq, eps, cb, sb, ld_rope, rope_ld_batch, wk, k_offset, SpScatter{})
   switch (ni) {
     case 1: LTX_QK_PAIR(1); break;
     case 2: LTX_QK_PAIR(2); break;
@@ -855,6 +897,67 @@ extern "C" int ltx_qk_norm_rope_pair(void* x, int64_t ldx, int64_t k_offset, int
     default: LTX_QK_PAIR(4); break;
   }
 #undef LTX_QK_PAIR
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+extern "C" int ltx_qk_norm_rope_scatter(const void* x, int64_t ldx, int64_t rows, int64_t rows_per_batch, int heads,
+                                        int head_dim, const void* q_weight, const void* k_weight, float eps,
+                                        const void* cos_tab, const void* sin_tab, int64_t ld_rope,
+                                        int64_t rope_ld_batch, int gated, int parts, int sp_rank,
+                                        void* const* dst, int64_t ld_dst, void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(x != nullptr && q_weight != nullptr && k_weight != nullptr && dst != nullptr, "NULL argument");
+  LTX_REQUIRE(parts >= 1 && parts <= 8 && sp_rank >= 0 && sp_rank < parts, "parts must be 1..8 and sp_rank < parts");
+  LTX_REQUIRE(heads % parts == 0, "heads must split evenly over the SP ranks");
+  const int nthr = heads * (head_dim / 16);
+  LTX_UNSUPPORTED(head_dim % 16 == 0 && nthr % 32 == 0 && nthr / 32 <= 4,
+                  "the fused exchange needs heads * head_dim / 16 a multiple of 32, at most 128");
+  LTX_REQUIRE(rows > 0 && rows_per_batch > 0 && rows % rows_per_batch == 0, "rows must be whole samples");
+  LTX_REQUIRE((cos_tab == nullptr) == (sin_tab == nullptr), "cos and sin go together");
+  const int64_t D = int64_t(heads) * head_dim;
+  const int hp = heads / parts, dp = hp * head_dim;
+  LTX_REQUIRE(ldx % 8 == 0 && ldx >= 3 * D + (gated ? heads : 0), "ldx too small for q, k, v (and gate logits)");
+  LTX_REQUIRE(dp % 8 == 0 && ld_dst % 8 == 0 && ld_dst >= 3 * dp + (gated ? hp : 0), "bad receive-buffer row");
+  LTX_REQUIRE(cos_tab == nullptr || (ld_rope % 8 == 0 && rope_ld_batch % 8 == 0), "RoPE strides must be multiples of 8");
+  check_vec_ptr(x, "x");
+  check_vec_ptr(q_weight, "q_weight");
+  check_vec_ptr(k_weight, "k_weight");
+  check_vec_ptr(cos_tab, "cos");
+  check_vec_ptr(sin_tab, "sin");
+  SpScatter sc{};
+  for (int j = 0; j < parts; ++j) {
+    LTX_REQUIRE(dst[j] != nullptr, "dst[j] is NULL");
+    check_vec_ptr(dst[j], "dst[j]");
+    sc.dst[j] = static_cast<__nv_bfloat16*>(dst[j]);
+  }
+  sc.ld = ld_dst;
+  sc.t_full = rows_per_batch * parts;
+  sc.row0 = int64_t(sp_rank) * rows_per_batch;
+  sc.hp = hp;
+  sc.dp = dp;
+  sc.v_off = int(2 * D);
+  sc.gate_off = gated ? int(3 * D) : -1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int ni = nthr / 32;
+  const int64_t target = int64_t(num_sms()) * 2;
+  const int per = int(std::max<int64_t>(8, (rows + target - 1) / target));
+  const unsigned grid = unsigned((rows + per - 1) / per);
+  auto xb = static_cast<__nv_bfloat16*>(const_cast<void*>(x));
+  auto wq = static_cast<const __nv_bfloat16*>(q_weight);
+  auto wk = static_cast<const __nv_bfloat16*>(k_weight);
+  auto cb = static_cast<const __nv_bfloat16*>(cos_tab);
+  auto sb = static_cast<const __nv_bfloat16*>(sin_tab);
+#define LTX_QK_SCATTER(NIV)                                                                                      \
+  launch_pdl(qk_rows_bf16_kernel<NIV, true>, dim3(grid), dim3(256), 0, s, 1, xb, ldx, rows, rows_per_batch, per, \
+             head_dim, wq, eps, cb, sb, ld_rope, rope_ld_batch, wk, D, sc)
+  switch (ni) {
+    case 1: LTX_QK_SCATTER(1); break;
+    case 2: LTX_QK_SCATTER(2); break;
+    case 3: LTX_QK_SCATTER(3); break;
+    default: LTX_QK_SCATTER(4); break;
+  }
+#undef LTX_QK_SCATTER
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
@@ -895,8 +998,9 @@ extern "C" int ltx_qk_norm_rope(void* x, int64_t ldx, int64_t rows, int64_t rows
     auto cb = static_cast<const __nv_bfloat16*>(cos_tab);
     auto sb = static_cast<const __nv_bfloat16*>(sin_tab);
 #define LTX_QK_ROWS(NIV)                                                                                    \
-  launch_pdl(qk_rows_bf16_kernel<NIV>, dim3(grid), dim3(256), 0, s, 1, xb, ldx, rows, rows_per_batch, per, head_dim, \
-             wb, eps, cb, sb, ld_rope, rope_ld_batch, static_cast<const __nv_bfloat16*>(nullptr), int64_t(0))
+  launch_pdl(qk_rows_bf16_kernel<NIV, false>, dim3(grid), dim3(256), 0, s, 1, xb, ldx, rows, rows_per_batch, per, \
+             head_dim, wb, eps, cb, sb, ld_rope, rope_ld_batch, static_cast<const __nv_bfloat16*>(nullptr), int64_t(0), \
+             SpScatter{})
     switch (ni) {
       case 1: LTX_QK_ROWS(1); break;
       case 2: LTX_QK_ROWS(2); break;

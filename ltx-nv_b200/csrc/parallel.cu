@@ -6,6 +6,8 @@
 // token order: exactly the (T, W) row-major operand the attention kernel reads. After
 // attention the (T, D/P) output goes back the same way and unpack rebuilds the
 // (T/P, D) rows the out-projection GEMM consumes.
+#include <cstring>
+
 #include "ltx_kernels.cuh"
 
 using namespace ltx;
@@ -170,6 +172,112 @@ extern "C" int ltx_attention_merge(const float* o_parts, const float* lse_parts,
       o_parts, lse_parts, parts, rows, heads, head_dim, static_cast<const __nv_bfloat16*>(gate_logits), ld_gate,
       static_cast<__nv_bfloat16*>(out), ldo),
       ltx::note_launch();
+  LTX_CUDA(cudaGetLastError());
+  LTX_API_END
+}
+
+// ---------------------------------------------------------------------------------
+// Ulysses exchange over NVLink peer memory. Each SP rank owns one buffer (ltx_peer_alloc,
+// shared through a CUDA IPC handle): the q/k pass writes every row's head blocks straight
+// into the receive buffer of the rank that owns the heads, the attention epilogue writes
+// every output row straight into the buffer of the rank that owns the token, and a flag
+// barrier (ltx_sp_barrier) separates writers from readers. Kernels only store to peer
+// memory; every load is local.
+// ---------------------------------------------------------------------------------
+namespace ltx {
+namespace detail {
+
+struct SpFlags {
+  int* flag[8];  // flag[j]: SP rank j's flag array (one int per rank), as mapped here
+};
+
+LTX_DEVICE void st_release_sys(int* p, int v) { asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory"); }
+LTX_DEVICE int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One thread: count this barrier on this rank, publish the count in this rank's slot of
+// every peer's flag array, then wait until every peer has published at least the same
+// count here. All ranks pass the same sequence of barriers, so their counts agree; the
+// count lives in device memory, so a captured graph replays correctly. The wait gives up
+// after limit SM cycles: device error bit 2, and the kernel returns.
+__global__ void sp_barrier_kernel(SpFlags f, int* counter, int parts, int rank, unsigned long long limit) {
+  if (threadIdx.x != 0) return;
+  const int epoch = *counter + 1;
+  *counter = epoch;
+  __threadfence_system();
+  for (int j = 0; j < parts; ++j)
+    if (j != rank) st_release_sys(f.flag[j] + rank, epoch);
+  const unsigned long long t0 = clock64();
+  for (int j = 0; j < parts; ++j) {
+    if (j == rank) continue;
+    while (ld_acquire_sys(f.flag[rank] + j) < epoch) {
+      if (clock64() - t0 > limit) {
+        ltx_flag_error(2);
+        return;
+      }
+      __nanosleep(128);
+    }
+  }
+  __threadfence_system();
+}
+
+}  // namespace detail
+}  // namespace ltx
+
+extern "C" int ltx_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(ptr != nullptr && ipc_handle != nullptr && bytes > 0, "bad argument");
+  void* p = nullptr;
+  LTX_CUDA(cudaMalloc(&p, bytes));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    LTX_CUDA(e);
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  LTX_API_END
+}
+
+extern "C" int ltx_peer_open(const void* ipc_handle, void** ptr) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(ptr != nullptr && ipc_handle != nullptr, "bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  LTX_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  LTX_API_END
+}
+
+extern "C" int ltx_peer_close(void* ptr) {
+  LTX_API_BEGIN
+  if (ptr != nullptr) LTX_CUDA(cudaIpcCloseMemHandle(ptr));
+  LTX_API_END
+}
+
+extern "C" int ltx_peer_free(void* ptr) {
+  LTX_API_BEGIN
+  if (ptr != nullptr) LTX_CUDA(cudaFree(ptr));
+  LTX_API_END
+}
+
+extern "C" int ltx_sp_barrier(int* const* flags, int* counter, int parts, int rank, unsigned long long limit_cycles,
+                              void* stream) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(flags != nullptr && counter != nullptr, "NULL argument");
+  LTX_REQUIRE(parts >= 1 && parts <= 8 && rank >= 0 && rank < parts, "parts must be 1..8 and rank < parts");
+  LTX_REQUIRE(limit_cycles > 0 && limit_cycles <= 20000000000ull, "limit must be in (0, 2e10] cycles");
+  SpFlags f{};
+  for (int j = 0; j < parts; ++j) {
+    LTX_REQUIRE(flags[j] != nullptr, "flags[j] is NULL");
+    f.flag[j] = flags[j];
+  }
+  sp_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, counter, parts, rank, limit_cycles),
+      note_launch();
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }

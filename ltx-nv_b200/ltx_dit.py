@@ -362,8 +362,16 @@ class LTXModel(torch.nn.Module):
         gated = cfg.gated_attention
         # self-attention
         nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_RMS, eps, st.mod(table, st.tmod, 0, 1))
-        qkv = attn1.project_qkv(h, st.T, st.pe)
         perturbed = [b for b, k in enumerate(keep_self) if k == 0] if keep_self is not None else []
+        if self._sp is not None and not a and not perturbed and self._sp.fused_for(attn1, st):
+            # sequence-parallel over peer memory: q/k normalisation fused into the exchange
+            qkv = attn1.project_qkv(h, st.T, st.pe, normalize=False)
+            o = self._sp.self_attention_fused(attn1, qkv, st)
+            nat.linear(o, attn1.to_out.weight, st.x,
+                       nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn1.to_out.bias, residual=st.x,
+                                    gate=st.mod(table, st.tmod, None, 2), rows_per_batch=st.T))
+            return self._text_cross(blk, st, h, attn2, table, d, eps, rows, inner, gated)
+        qkv = attn1.project_qkv(h, st.T, st.pe)
         v_cols = qkv[:, 2 * inner:3 * inner]
         g_cols = qkv[:, 3 * inner:3 * inner + attn1.heads] if gated else None
         if self._sp is not None and not a:
@@ -384,6 +392,13 @@ class LTXModel(torch.nn.Module):
         nat.linear(o, attn1.to_out.weight, st.x,
                    nat.epilogue(nat.EPI_GATE_RESIDUAL, bias=attn1.to_out.bias, residual=st.x,
                                 gate=st.mod(table, st.tmod, None, 2), rows_per_batch=st.T))
+        self._text_cross(blk, st, h, attn2, table, d, eps, rows, inner, gated)
+
+    def _text_cross(self, blk: Block, st: _Stream, h: torch.Tensor, attn2, table, d: int, eps: float, rows: int,
+                    inner: int, gated: bool):
+        """Text cross-attention of one stream (ltx_dit.py:267-282)."""
+        cfg = self.cfg
+        a = st.name == "audio"
         # text cross-attention
         if cfg.cross_attention_adaln:
             nat.norm_modulate(st.x, h, st.T, nat.LTX_NORM_RMS, eps, st.mod(table, st.tmod, 6, 7))

@@ -297,13 +297,16 @@ class Attention(torch.nn.Module):
 
     # native core ----------------------------------------------------------------------
     def project_qkv(self, x2: torch.Tensor, rows_per_batch: int, pe: RopeTables | None,
-                    k_pe: RopeTables | None = None) -> torch.Tensor:
+                    k_pe: RopeTables | None = None, normalize: bool = True) -> torch.Tensor:
         """Self-attention projections of x2 (B*T, D) -> packed (B*T, 3I(+H)) buffer with
-        q and k normalised and rotated in place."""
+        q and k normalised and rotated in place (normalize=False: left as projected, for a
+        caller that fuses the normalisation into its exchange)."""
         inner = self.heads * self.dim_head
         w, b = self.packed_self()
         qkv = torch.empty(x2.shape[0], w.shape[0], device=x2.device, dtype=x2.dtype)
         nat.linear(x2, w, qkv, nat.epilogue(bias=b))
+        if not normalize:
+            return qkv
         if k_pe is None:
             # q and k share the tables: one pass over both blocks
             if pe is None:

@@ -26,6 +26,7 @@ No remote memory is read by any kernel: NCCL moves every byte into local HBM fir
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -86,12 +87,109 @@ def qkv_segments(dim: int, heads: int, sp: int, gated: bool) -> list[tuple[int, 
     return segs
 
 
+class _CudaArray:
+    """A device buffer of this process seen as a torch tensor (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 2,
+                                         "strides": None}
+
+
+def _bf16_view(ptr: int, rows: int, cols: int, device: torch.device) -> torch.Tensor:
+    return torch.as_tensor(_CudaArray(ptr, (rows, cols), "<i2"), device=device).view(torch.bfloat16)
+
+
+class PeerExchange:
+    """Buffers of the Ulysses exchange over NVLink peer memory for one SP group.
+
+    Every rank allocates one buffer (nat.peer_alloc) laid out as
+        [flags: one int per rank | counter | receive buffer (B*T, W) | output (B*T/P, D)]
+    and maps the others' through CUDA IPC handles gathered over the group. The q/k pass
+    stores each row's head blocks into the owners' receive buffers, the attention
+    epilogue stores each output row into its token owner's output buffer, and
+    nat.sp_barrier separates writers from readers. Buffers are made per shape on first
+    use (outside any graph capture) and kept until close()."""
+
+    def __init__(self, group, size: int, rank: int, device: torch.device):
+        self.group, self.size, self.rank, self.device = group, size, rank, device
+        self._bufs: dict[tuple, dict] = {}
+
+    def get(self, batch: int, rows: int, width: int, dim: int) -> dict:
+        key = (batch, rows, width, dim)
+        if key in self._bufs:
+            return self._bufs[key]
+        t_full = rows * self.size
+        head = 512  # flags and counter
+        recv_bytes = batch * t_full * width * 2
+        out_off = head + (recv_bytes + 255) // 256 * 256
+        total = out_off + batch * rows * dim * 2
+        ptr, handle = nat.peer_alloc(total)
+        handles = [None] * self.size
+        dist.all_gather_object(handles, handle, group=self.group)
+        bases = [ptr if j == self.rank else nat.peer_open(handles[j]) for j in range(self.size)]
+        buf = {"own": ptr, "bases": bases, "flags": list(bases), "counter": ptr + 256,
+               "recv": [b + head for b in bases], "out": [b + out_off for b in bases],
+               "recv_local": _bf16_view(ptr + head, batch * t_full, width, self.device),
+               "out_local": _bf16_view(ptr + out_off, batch * rows, dim, self.device)}
+        self._bufs[key] = buf
+        return buf
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (call on every rank, after a
+        barrier, with no exchange in flight)."""
+        for buf in self._bufs.values():
+            for j, b in enumerate(buf["bases"]):
+                if j != self.rank:
+                    nat.peer_close(b)
+            nat.peer_free(buf["own"])
+        self._bufs.clear()
+
+
 class SequenceParallel:
     """Self-attention replacement installed as `model._sp` (see LTXModel._self_and_text)."""
 
-    def __init__(self, group, size: int):
+    def __init__(self, group, size: int, exchange: PeerExchange | None = None):
         self.group = group
         self.size = size
+        self.exchange = exchange
+
+    def fused_for(self, attn, st) -> bool:
+        """Whether this self-attention runs the fused peer-memory exchange."""
+        if self.exchange is None or st.x.dtype != torch.bfloat16 or attn.dim_head not in (64, 128):
+            return False
+        heads = attn.heads
+        if heads % self.size or (heads // self.size) % 8 or (heads * attn.dim_head // 16) % 32 \
+                or heads * attn.dim_head // 16 > 128 or st.T * self.size <= 128:
+            return False
+        return st.pe is None or st.pe.heads == heads
+
+    def self_attention_fused(self, attn, qkv: torch.Tensor, st) -> torch.Tensor:
+        """q/k RMSNorm + RoPE with the rows sent to their heads' owners, a barrier, attention
+        over all tokens of this rank's heads with each output row sent to its token's
+        owner, a barrier: returns this rank's (B*T, D) attention output."""
+        p, heads, d = self.size, attn.heads, attn.dim_head
+        dim, hp = heads * d, heads // p
+        dp = hp * d
+        gated = attn.to_gate_logits is not None
+        width = (3 * dp + (hp if gated else 0) + 7) // 8 * 8
+        ex = self.exchange
+        buf = ex.get(st.B, st.T, width, dim)
+        pe = st.pe
+        cos = sin = None
+        ld_batch = 0
+        if pe is not None:
+            cos = pe.cos.view(-1, dim // 2) if pe.cos.dim() == 3 else pe.cos
+            sin = pe.sin.view(-1, dim // 2) if pe.sin.dim() == 3 else pe.sin
+            ld_batch = pe.ld_batch
+        nat.qk_norm_rope_scatter(qkv, st.T, heads, d, attn.q_norm.weight, attn.k_norm.weight, attn.norm_eps, cos, sin,
+                                 gated, ex.rank, buf["recv"], width, rope_ld_batch=ld_batch)
+        nat.sp_barrier(buf["flags"], buf["counter"], ex.rank)
+        recv = buf["recv_local"]
+        t_full = st.T * p
+        nat.attention_scatter(recv[:, :dp], recv[:, dp:2 * dp], recv[:, 2 * dp:3 * dp], st.B, t_full, hp, d,
+                              d ** -0.5, recv[:, 3 * dp:3 * dp + hp] if gated else None, buf["out"], dim, ex.rank * dp)
+        nat.sp_barrier(buf["flags"], buf["counter"], ex.rank)
+        return buf["out_local"]
 
     def self_attention(self, attn, qkv: torch.Tensor, st) -> torch.Tensor:
         p = self.size
@@ -150,7 +248,10 @@ class SequenceParallel:
 class ParallelDenoiser:
     """CFG x SP execution of ltx_dit.cfg_denoise_step across the default process group."""
 
-    def __init__(self, model: ltx_dit.LTXModel, cfg_split: int | None = None):
+    def __init__(self, model: ltx_dit.LTXModel, cfg_split: int | None = None, exchange: str = "auto"):
+        """exchange: "peer" runs the Ulysses exchange inside the q/k and attention kernels
+        over NVLink peer memory (one node, NCCL process group), "nccl" as pack +
+        all_to_all + unpack; "auto" picks "peer" when the whole group is on one node."""
         self.model = model
         self.layout = Layout.make(dist.get_world_size(), dist.get_rank(), cfg_split)
         lay = self.layout
@@ -163,7 +264,24 @@ class ParallelDenoiser:
             g = dist.new_group(ranks)
             if lay.rank in ranks:
                 self.cfg_group = g
-        model._sp = SequenceParallel(self.sp_group, lay.sp) if lay.sp > 1 else None
+        if exchange not in ("auto", "peer", "nccl"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        one_node = int(os.environ.get("LOCAL_WORLD_SIZE", lay.world)) == lay.world
+        use_peer = lay.sp > 1 and (exchange == "peer" or (
+            exchange == "auto" and one_node and dist.get_backend() == "nccl" and torch.cuda.is_available()))
+        self.exchange = PeerExchange(self.sp_group, lay.sp, lay.sp_rank,
+                                     torch.device("cuda", torch.cuda.current_device())) if use_peer else None
+        model._sp = SequenceParallel(self.sp_group, lay.sp, self.exchange) if lay.sp > 1 else None
+
+    def close(self) -> None:
+        """Release the peer-memory exchange (every rank; no step in flight)."""
+        if self.exchange is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            self.exchange.close()
+            self.exchange = None
+            if self.model._sp is not None:
+                self.model._sp.exchange = None
 
     @torch.inference_mode()
     def step(self, latent: torch.Tensor, positions: torch.Tensor, context_pos: torch.Tensor,

@@ -611,6 +611,28 @@ def test_split_kv_attention_merge_matches_full_attention(hd, parts, tk):
     assert torch.allclose(lse_all[0], lse_ref, atol=2e-2, rtol=1e-3)
 
 
+def test_peer_barrier_wait_expires_and_reports_on_the_host():
+    """The sequence-parallel flag barrier with a peer that never arrives (rank 0 of 2, the
+    peer's slot in this rank's flag array stays 0) gives up after its limit, sets bit 2
+    of the device error word and returns; the context keeps working."""
+    assert nat.device_error_flags(clear=True) == 0
+    flags = torch.zeros(2, dtype=torch.int32, device=DEV)
+    counter = torch.zeros(1, dtype=torch.int32, device=DEV)
+    nat.sp_barrier([flags.data_ptr(), flags.data_ptr()], counter.data_ptr(), 0, limit_cycles=2_000_000)
+    torch.cuda.synchronize()
+    assert int(counter.item()) == 1
+    # both "ranks'" flag arrays are this one: rank 0 published its count in slot 0 and
+    # waited for slot 1, which nothing writes
+    assert flags.tolist() == [1, 0]
+    assert nat.device_error_flags(clear=True) == 2
+    assert nat.device_error_flags() == 0
+    x = torch.randn(4096, device=DEV).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    nat.gelu_tanh(x, y)
+    torch.cuda.synchronize()
+    assert rel_l2(y, torch.nn.functional.gelu(x.float(), approximate="tanh")) < 1e-2
+
+
 def test_bounded_wait_expires_and_reports_on_the_host():
     """Failure detection without a GPU fault: a bounded mbarrier wait on a barrier that
     nothing arrives on (the wait the tcgen05 kernels use, with a 2M-cycle limit instead
@@ -629,3 +651,62 @@ def test_bounded_wait_expires_and_reports_on_the_host():
     torch.cuda.synchronize()
     ref = torch.nn.functional.gelu(x.float(), approximate="tanh")
     assert rel_l2(y, ref) < 1e-2
+
+
+# ------------------------------------------------------- sequence-parallel exchange kernels
+
+
+@pytest.mark.parametrize("p,b,heads,hd,gated", [(4, 1, 32, 64, True), (2, 2, 32, 64, True), (2, 1, 16, 128, False)])
+def test_sp_scatter_kernels_emulating_ranks_on_one_gpu(p, b, heads, hd, gated):
+    """The fused Ulysses exchange with every "rank" on this GPU (all destination buffers
+    local): ltx_qk_norm_rope_scatter must fill the receive buffers exactly as q/k norm +
+    RoPE in place followed by pack and all-to-all would, and ltx_attention_scatter must
+    deliver exactly what attention followed by all-to-all and unpack would."""
+    torch.manual_seed(30)
+    n = 384  # tokens per rank and sample
+    dim, hp = heads * hd, heads // p
+    dp = hp * hd
+    t_full = n * p
+    width = (3 * dp + (hp if gated else 0) + 7) // 8 * 8
+    ldx = 3 * dim + (((heads + 7) // 8) * 8 if gated else 0)
+    wq = (1 + 0.02 * torch.randn(dim, device=DEV)).to(torch.bfloat16)
+    wk = (1 + 0.02 * torch.randn(dim, device=DEV)).to(torch.bfloat16)
+    xs = [torch.randn(b * n, ldx, device=DEV).to(torch.bfloat16) for _ in range(p)]
+    cos = [torch.randn(n, dim // 2, device=DEV).to(torch.bfloat16) for _ in range(p)]
+    sin = [torch.randn(n, dim // 2, device=DEV).to(torch.bfloat16) for _ in range(p)]
+    # reference: normalise in place, then the receive buffers all-to-all would deliver
+    want = [torch.zeros(b * t_full, width, device=DEV, dtype=torch.bfloat16) for _ in range(p)]
+    for r in range(p):
+        y = xs[r].clone()
+        nat.qk_norm_rope_pair(y, dim, n, heads, hd, wq, wk, 1e-6, cos[r], sin[r], 0)
+        for j in range(p):
+            rows = [bb * t_full + r * n + t for bb in range(b) for t in range(n)]
+            blk = [y[:, j * dp:(j + 1) * dp], y[:, dim + j * dp:dim + (j + 1) * dp],
+                   y[:, 2 * dim + j * dp:2 * dim + (j + 1) * dp]]
+            if gated:
+                blk.append(y[:, 3 * dim + j * hp:3 * dim + (j + 1) * hp])
+            want[j][rows, :sum(t.shape[1] for t in blk)] = torch.cat(blk, 1)
+    recv = [torch.zeros(b * t_full, width, device=DEV, dtype=torch.bfloat16) for _ in range(p)]
+    for r in range(p):
+        nat.qk_norm_rope_scatter(xs[r], n, heads, hd, wq, wk, 1e-6, cos[r], sin[r], gated, r,
+                                 [t.data_ptr() for t in recv], width)
+    torch.cuda.synchronize()
+    for j in range(p):
+        assert torch.equal(recv[j], want[j]), j
+    # attention over each rank's heads, output rows to their token owners
+    outs = [torch.zeros(b * n, dim, device=DEV, dtype=torch.bfloat16) for _ in range(p)]
+    want_o = [torch.zeros(b * n, dim, device=DEV, dtype=torch.bfloat16) for _ in range(p)]
+    for j in range(p):
+        rv = recv[j]
+        q, k, v = rv[:, :dp], rv[:, dp:2 * dp], rv[:, 2 * dp:3 * dp]
+        g = rv[:, 3 * dp:3 * dp + hp] if gated else None
+        o = torch.empty(b * t_full, dp, device=DEV, dtype=torch.bfloat16)
+        nat.attention(q, k, v, o, b, t_full, t_full, hp, hd, hd ** -0.5, g)
+        for r in range(p):
+            rows = [bb * t_full + r * n + t for bb in range(b) for t in range(n)]
+            want_o[r][:, j * dp:(j + 1) * dp] = o[rows]
+        nat.attention_scatter(q, k, v, b, t_full, hp, hd, hd ** -0.5, g, [t.data_ptr() for t in outs], dim, j * dp)
+    torch.cuda.synchronize()
+    assert nat.device_error_flags() == 0
+    for r in range(p):
+        assert torch.equal(outs[r], want_o[r]), r

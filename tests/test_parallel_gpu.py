@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cfg_split, q):
+def _worker(rank, world, port, cfg_split, exchange, q):
     import sys
     from datetime import timedelta
     from pathlib import Path
@@ -69,7 +69,7 @@ def _worker(rank, world, port, cfg_split, q):
 
         nat.attention_force_split(-1)  # whole units everywhere: the exact comparison
         ref = single()
-        pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=cfg_split)
+        pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=cfg_split, exchange=exchange)
         sp = model._sp
         out = pdn.step(latent, pos, ctx[:1], ctx[1:], sigmas, 0, 3.0, keyframes_mask=kf)
         nat.attention_force_split(0)  # the automatic plan
@@ -82,19 +82,23 @@ def _worker(rank, world, port, cfg_split, q):
         diff = (out.float() - ref.float()).abs().max().item()
         rel = float((out_auto.float() - ref_auto.float()).norm() / ref_auto.float().norm())
         q.put((rank, diff, rel, pdn.layout.cfg, pdn.layout.sp))
+        pdn.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,cfg_split", [(2, 2), (2, 1), (4, 2)])
-def test_parallel_step_equals_single_gpu(world, cfg_split):
+@pytest.mark.parametrize("world,cfg_split,exchange", [(2, 2, "nccl"), (2, 1, "nccl"), (2, 1, "peer"), (4, 2, "nccl"),
+                                                     (4, 2, "peer")])
+def test_parallel_step_equals_single_gpu(world, cfg_split, exchange):
+    """exchange "nccl": pack + all_to_all + unpack; "peer": the exchange fused into the q/k
+    and attention kernels over NVLink peer memory."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_split, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_split, exchange, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=600) for _ in range(world)]
@@ -106,7 +110,7 @@ def test_parallel_step_equals_single_gpu(world, cfg_split):
     assert all(e < 1e-2 for _, _, e, _, _ in res), res
 
 
-def _av_worker(rank, world, port, cfg_split, q):
+def _av_worker(rank, world, port, cfg_split, exchange, q):
     import sys
     from datetime import timedelta
     from pathlib import Path
@@ -150,7 +154,7 @@ def _av_worker(rank, world, port, cfg_split, q):
         sigmas = torch.tensor([0.5, 0.25])
         args = (v_lat, a_lat, v_pos, a_pos, v_ctx[:1], v_ctx[1:], a_ctx[:1], a_ctx[1:], sigmas, 0, 3.0)
         ref_v, ref_a = ltx_dit.av_cfg_denoise_step(model, *args, v_keyframes_mask=kf)
-        pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=cfg_split)
+        pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=cfg_split, exchange=exchange)
         out_v, out_a = pdn.step_av(*args, v_keyframes_mask=kf)
         torch.cuda.synchronize()
         model._sp = None
@@ -159,13 +163,14 @@ def _av_worker(rank, world, port, cfg_split, q):
             return float((a.float() - b.float()).norm() / b.float().norm())
 
         q.put((rank, rel(out_v, ref_v), rel(out_a, ref_a), pdn.layout.cfg, pdn.layout.sp))
+        pdn.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,cfg_split", [(2, 1), (4, 2)])
-def test_parallel_av_step_matches_single_gpu(world, cfg_split):
+@pytest.mark.parametrize("world,cfg_split,exchange", [(2, 1, "nccl"), (2, 1, "peer"), (4, 2, "peer")])
+def test_parallel_av_step_matches_single_gpu(world, cfg_split, exchange):
     """Audio-video step under sequence parallelism (audio replicated, video-to-audio
     attention merged from split-KV partials) against the single-GPU av_cfg_denoise_step.
     The split softmax rounds differently from the single pass, so the check is relative
@@ -176,7 +181,7 @@ def test_parallel_av_step_matches_single_gpu(world, cfg_split):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_av_worker, args=(r, world, port, cfg_split, q)) for r in range(world)]
+    procs = [ctx.Process(target=_av_worker, args=(r, world, port, cfg_split, exchange, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=600) for _ in range(world)]
