@@ -229,7 +229,7 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         if world > 1:
             import ltx_parallel
 
-            pdn = ltx_parallel.ParallelDenoiser(model)
+            pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=args.cfg_split, exchange=args.exchange)
             layout = pdn.layout
 
             def step(lat, idx=0):
@@ -244,7 +244,7 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
     elif world > 1:
         import ltx_parallel
 
-        pdn = ltx_parallel.ParallelDenoiser(model)
+        pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=args.cfg_split, exchange=args.exchange)
         layout = pdn.layout
 
         def step(lat, idx=0):
@@ -375,7 +375,9 @@ def run_ours(args, rank: int, world: int, dev: torch.device) -> dict | None:
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": workload_config(c),
         "execution": {"parallelism": "single GPU" if world == 1 else
-                      f"cfg{layout.cfg} x sp{layout.sp} (Ulysses, NCCL)", "cuda_graph": used_graph,
+                      f"cfg{layout.cfg} x sp{layout.sp} (Ulysses, exchange: "
+                      f"{'NVLink peer memory in the q/k and attention kernels' if pdn.exchange_kind == 'peer' else 'NCCL all-to-all'})",
+                      "cuda_graph": used_graph,
                       "step_flops": flops, "text_kv": "projected once, cached across denoise steps (the context "
                       "is constant); not counted in step_flops"},
         "steps_per_s": 1e3 / ms_per_step, "step_tflops_per_gpu": tflops / world,
@@ -864,6 +866,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--cfg-split", type=int, choices=[1, 2], default=None,
+                    help="N > 1: CFG groups (default 2: cond and uncond on separate ranks)")
+    ap.add_argument("--exchange", choices=["auto", "peer", "nccl"], default="auto",
+                    help="N > 1: the Ulysses exchange fused into the kernels over peer memory, or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))

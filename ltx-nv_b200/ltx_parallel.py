@@ -271,6 +271,7 @@ class ParallelDenoiser:
             exchange == "auto" and one_node and dist.get_backend() == "nccl" and torch.cuda.is_available()))
         self.exchange = PeerExchange(self.sp_group, lay.sp, lay.sp_rank,
                                      torch.device("cuda", torch.cuda.current_device())) if use_peer else None
+        self.exchange_kind = "peer" if use_peer else ("nccl" if lay.sp > 1 else "none")
         model._sp = SequenceParallel(self.sp_group, lay.sp, self.exchange) if lay.sp > 1 else None
 
     def close(self) -> None:
