@@ -91,13 +91,14 @@ __global__ void __launch_bounds__(1024) norm_modulate_kernel(const T* __restrict
 // one sample, so round(1 + scale) and round(shift) are built once per CTA in shared
 // memory; a row then costs its load, its store and three bf16 roundings per element
 // (two of them packed two to an instruction). Same rounding sequence as
-// norm_modulate_kernel.
-template <int NC>
+// norm_modulate_kernel. KIND (ltx_norm_kind) is a template parameter so that RMSNorm
+// carries no mean and LTX_NORM_NONE no normalisation; the products run as packed
+// fp32x2 operations.
+template <int NC, int KIND>
 __global__ void __launch_bounds__(256) norm_rows_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                              __nv_bfloat16* __restrict__ y, int64_t ldy,
                                                              int64_t rows, int64_t rows_per_batch,
-                                                             int chunks_per_sample, int rows_per_chunk, int kind,
-                                                             float eps,
+                                                             int chunks_per_sample, int rows_per_chunk, float eps,
                                                              ModVec<__nv_bfloat16> shift, ModVec<__nv_bfloat16> scale) {
   constexpr int D = 256 * NC;
   __shared__ float s1p[D];  // round(1 + scale)
@@ -142,11 +143,11 @@ __global__ void __launch_bounds__(256) norm_rows_bf16_kernel(const __nv_bfloat16
       unpack_bf16x2(raw[i].z, v[i][4], v[i][5]);
       unpack_bf16x2(raw[i].w, v[i][6], v[i][7]);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) s += (kind == LTX_NORM_LAYER) ? v[i][k] : v[i][k] * v[i][k];
+      for (int k = 0; k < 8; ++k) s += (KIND == LTX_NORM_LAYER) ? v[i][k] : v[i][k] * v[i][k];
     }
     if (r + 8 < r1) load_row(r + 8);
     float mean = 0.f, rstd = 1.f;
-    if (kind == LTX_NORM_LAYER) {
+    if constexpr (KIND == LTX_NORM_LAYER) {
       mean = warp_sum(s) / float(D);
       float s2 = 0.f;
 #pragma unroll
@@ -157,9 +158,10 @@ __global__ void __launch_bounds__(256) norm_rows_bf16_kernel(const __nv_bfloat16
           s2 += d * d;
         }
       rstd = rsqrtf(warp_sum(s2) / float(D) + eps);
-    } else if (kind == LTX_NORM_RMS) {
+    } else if constexpr (KIND == LTX_NORM_RMS) {
       rstd = rsqrtf(warp_sum(s) / float(D) + eps);
     }
+    const uint64_t r2 = f2_pack(rstd, rstd), m2 = f2_pack(mean, mean);
     __nv_bfloat16* yr = y + r * ldy;
 #pragma unroll
     for (int i = 0; i < NC; ++i) {
@@ -167,21 +169,32 @@ __global__ void __launch_bounds__(256) norm_rows_bf16_kernel(const __nv_bfloat16
       float o[8];
 #pragma unroll
       for (int k = 0; k < 8; k += 2) {
-        o[k] = (v[i][k] - mean) * rstd;
-        o[k + 1] = (v[i][k + 1] - mean) * rstd;
-        round_bf16_pair(o[k], o[k + 1]);
+        if constexpr (KIND == LTX_NORM_NONE) {
+          o[k] = v[i][k];  // (v - 0) * 1, already bf16
+          o[k + 1] = v[i][k + 1];
+        } else {
+          uint64_t t = f2_pack(v[i][k], v[i][k + 1]);
+          if constexpr (KIND == LTX_NORM_LAYER) t = f2_sub(t, m2);
+          f2_unpack(f2_mul(t, r2), o[k], o[k + 1]);
+          round_bf16_pair(o[k], o[k + 1]);
+        }
       }
       if (scale.on) {
+        const float4 sa = *reinterpret_cast<const float4*>(&s1p[c]);
+        const float4 sb = *reinterpret_cast<const float4*>(&s1p[c + 4]);
+        const uint64_t s2v[4] = {f2_pack(sa.x, sa.y), f2_pack(sa.z, sa.w), f2_pack(sb.x, sb.y), f2_pack(sb.z, sb.w)};
 #pragma unroll
         for (int k = 0; k < 8; k += 2) {
-          o[k] *= s1p[c + k];
-          o[k + 1] *= s1p[c + k + 1];
+          f2_unpack(f2_mul(f2_pack(o[k], o[k + 1]), s2v[k >> 1]), o[k], o[k + 1]);
           round_bf16_pair(o[k], o[k + 1]);
         }
       }
       if (shift.on) {
+        const float4 ha = *reinterpret_cast<const float4*>(&shf[c]);
+        const float4 hb = *reinterpret_cast<const float4*>(&shf[c + 4]);
+        const uint64_t h2v[4] = {f2_pack(ha.x, ha.y), f2_pack(ha.z, ha.w), f2_pack(hb.x, hb.y), f2_pack(hb.z, hb.w)};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) o[k] += shf[c + k];
+        for (int k = 0; k < 8; k += 2) f2_unpack(f2_add(f2_pack(o[k], o[k + 1]), h2v[k >> 1]), o[k], o[k + 1]);
       }
       st8<__nv_bfloat16>(yr + c, o);
     }
@@ -791,9 +804,13 @@ void launch_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ldy, int6
       per = std::min<int64_t>(per, std::min<int64_t>(rpb, rows));
       const int64_t chunks = (std::min<int64_t>(rpb, rows) + per - 1) / per;
       const unsigned grid = unsigned(n_samples * chunks);
-#define LTX_NORM_ROWS(NCV)                                                                                  \
-  launch_pdl(norm_rows_bf16_kernel<NCV>, dim3(grid), dim3(256), 0, s, 1, xp, ldx, yp, ldy, rows, rpb, int(chunks), \
-             int(per), kind, eps, sh, sc)
+#define LTX_NORM_ROWS_K(NCV, KV)                                                                             \
+  launch_pdl(norm_rows_bf16_kernel<NCV, KV>, dim3(grid), dim3(256), 0, s, 1, xp, ldx, yp, ldy, rows, rpb, int(chunks), \
+             int(per), eps, sh, sc)
+#define LTX_NORM_ROWS(NCV)                                                                 \
+  (kind == LTX_NORM_LAYER ? LTX_NORM_ROWS_K(NCV, LTX_NORM_LAYER)                           \
+                          : kind == LTX_NORM_NONE ? LTX_NORM_ROWS_K(NCV, LTX_NORM_NONE)     \
+                                                  : LTX_NORM_ROWS_K(NCV, LTX_NORM_RMS))
       switch (nc) {
         case 1: LTX_NORM_ROWS(1); break;
         case 2: LTX_NORM_ROWS(2); break;
@@ -805,6 +822,7 @@ void launch_norm_modulate(const void* x, int64_t ldx, void* y, int64_t ldy, int6
         default: LTX_NORM_ROWS(8); break;
       }
 #undef LTX_NORM_ROWS
+#undef LTX_NORM_ROWS_K
       return;
     }
   }
