@@ -632,8 +632,14 @@ __global__ void __launch_bounds__(FaCfg<D>::THREADS, 1)
                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O, int64_t ldo, int Tq,
                    int Tk, float scale_log2, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
                    float* __restrict__ o32, float* __restrict__ lse, int64_t ld_lse, const FaSched sch) {
-  // whole units only: the units from n_full on run as parts (fmha_part_kernel)
-  if (int(blockIdx.x) + int(gridDim.x) * (int(blockIdx.y) + int(gridDim.y) * int(blockIdx.z)) >= sch.n_full) return;
+  // Whole units only: the units from n_full on run as parts (fmha_part_kernel). A CTA
+  // that leaves still waits for the kernels ahead of it: fmha_part_kernel is scheduled
+  // once every CTA here has passed that wait or exited, and it reads q, k, v without a
+  // wait of its own (with n_full = 0 every CTA leaves here).
+  if (int(blockIdx.x) + int(gridDim.x) * (int(blockIdx.y) + int(gridDim.y) * int(blockIdx.z)) >= sch.n_full) {
+    pdl_wait();
+    return;
+  }
   fmha_body<D, false>(&tmQ, &tmK, &tmV, O, ldo, Tq, Tk, scale_log2, gate, ld_gate, o32, lse, ld_lse,
                       int(blockIdx.y), int(blockIdx.z), int(blockIdx.x) * 2 * FaCfg<D>::BM, 0, 0, -1, -1, sch);
 }
