@@ -1,27 +1,34 @@
-"""Multi-GPU denoise step: CFG split x Ulysses sequence parallelism over NCCL.
+"""Multi-GPU denoise step: CFG split x Ulysses sequence parallelism.
 
 One process per GPU. The world of W ranks is split into `cfg` CFG groups (2 when W >= 2:
 cond on the first W/2 ranks, uncond on the rest) of `sp = W / cfg` ranks each. Inside a
 CFG group the latent's T tokens are sharded contiguously over the sp ranks; everything
 except self-attention is token-local (GEMMs, norms, FFN, text cross-attention against
-the replicated 128-token context). Self-attention runs Ulysses-style:
+the replicated text context). Self-attention runs Ulysses-style:
 
     QKV(+gate) GEMM on local tokens -> q/k RMSNorm + RoPE (needs all heads of a token)
-    -> ltx_sp_pack -> NCCL all_to_all (tokens -> heads) -> tcgen05 attention over all T
-    tokens for the rank's H/sp heads -> NCCL all_to_all back -> ltx_sp_unpack -> out GEMM
+    -> exchange (tokens -> heads) -> tcgen05 attention over all T tokens for the rank's
+    H/sp heads -> exchange back (heads -> tokens) -> out GEMM
+
+On one node the exchange runs inside the kernels over NVLink peer memory (PeerExchange):
+the q/k kernel stores each row's head blocks into the receive buffer of the rank owning
+those heads, the attention epilogue stores each output row into the buffer of the rank
+owning the token, and a flag barrier separates writers from readers; kernels only store
+to peer memory and read local memory. Otherwise (exchange="nccl") it is ltx_sp_pack ->
+NCCL all_to_all -> attention -> all_to_all -> ltx_sp_unpack.
 
 The step ends with one all_gather of the (T/sp, 128) velocity inside each CFG pair (the
 X0 + CFG + Euler update needs cond and uncond of the same tokens) and one all_gather of
 the next latent's shards inside each SP group, so every rank holds the full next latent.
-Each rank runs the same kernels on the same rows as the single-GPU step, so the result
-equals the single-GPU result.
+Each rank runs the same kernels on the same rows as the single-GPU step: with attention
+running every (sample, head, 256-query) unit whole the result equals the single-GPU
+result bit for bit; the attention tail split makes other units split on a rank than on
+one GPU, which changes the result by bf16 rounding only.
 
 The audio-video model (step_av) keeps the audio stream (126 tokens) replicated on every
 rank of a CFG group: audio-to-video attention reads the full audio keys locally, and
 video-to-audio attention runs over the sharded video keys as split-KV partial attentions
 (fp32 O / l and log2-sum-exp per row and head) merged after an all_gather.
-
-No remote memory is read by any kernel: NCCL moves every byte into local HBM first.
 """
 
 from __future__ import annotations
