@@ -569,6 +569,8 @@ PROBES = {
     # name: (description, builder) -- one kernel at its config-3 shape
     "attention": "self-attention FMHA, B=2, H=32, T=6144, d=64 (q/k/v/gate read from the packed QKV buffer)",
     "attention128": "self-attention FMHA at config 4's video width: B=2, H=32, T=6144, d=128 (packed QKV buffer)",
+    "attention_rank8": "self-attention of one rank at 8 GPUs (CFG2 x SP4): B=1, H=8, T=6144, d=64, units of the "
+                       "partly filled last wave split over key ranges (packed QKV buffer)",
     "ffn_in": "FFN-in tcgen05 GEMM + GELU epilogue, M=12288, N=8192, K=2048",
     "qkv": "packed QKV(+gate) tcgen05 GEMM, M=12288, N=6176, K=2048",
     "ffn_out": "FFN-out tcgen05 GEMM + gate*out+residual epilogue, M=12288, N=2048, K=8192",
@@ -746,14 +748,16 @@ def run_probe(args, dev: torch.device) -> dict:
     def rnd(*shape, scale=1.0):
         return (torch.randn(*shape, generator=g, device=dev) * scale).to(torch.bfloat16)
 
-    if args.probe in ("attention", "attention128"):
-        hd = 64 if args.probe == "attention" else 128
-        d = c["heads"] * hd
-        qkv = rnd(m, 3 * d + c["heads"])
-        o = torch.empty(m, d, device=dev, dtype=torch.bfloat16)
-        fn = lambda: nat.attention(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:3 * d], o, 2, t, t, c["heads"],  # noqa
-                                   hd, hd ** -0.5, qkv[:, 3 * d:])
-        flops = 4.0 * 2 * c["heads"] * t * t * hd
+    if args.probe in ("attention", "attention128", "attention_rank8"):
+        hd = 128 if args.probe == "attention128" else 64
+        # attention_rank8: what one rank of 8 attends over (CFG2 x SP4: 1 sample, 8 heads)
+        nb, heads = (1, c["heads"] // 4) if args.probe == "attention_rank8" else (2, c["heads"])
+        d = heads * hd
+        qkv = rnd(nb * t, 3 * d + ((heads + 7) // 8) * 8)
+        o = torch.empty(nb * t, d, device=dev, dtype=torch.bfloat16)
+        fn = lambda: nat.attention(qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:3 * d], o, nb, t, t, heads,  # noqa
+                                   hd, hd ** -0.5, qkv[:, 3 * d:3 * d + heads])
+        flops = 4.0 * nb * heads * t * t * hd
         nbytes = 2 * (qkv.numel() + o.numel())
     elif args.probe in ("ffn_in", "qkv", "ffn_out", "attn_out"):
         n, k = {"ffn_in": (4 * d, d), "qkv": (3 * d + c["heads"], d), "ffn_out": (d, 4 * d),
