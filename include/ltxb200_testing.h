@@ -28,6 +28,10 @@ int ltx_gemm_set_tile_n(int bn);
  * error word that ltx_device_error_flags reads, writes 1 to the device int `returned`
  * (2 would mean the wait completed) and returns. The context stays usable. */
 int ltx_test_attention_force_split(int parts);
+/* The automatic split plan of one attention launch, host arithmetic only: for `units`
+ * (sample, head, 256-query) units over Tk keys on `sms` SMs, the units that run whole
+ * (*n_full) and the parts each remaining unit is split into (*split_k; 1: no split). */
+int ltx_test_attention_plan(int64_t units, int64_t Tk, int sms, int* n_full, int* split_k);
 int ltx_test_bounded_wait(unsigned long long limit_cycles, int* returned, void* stream);
 
 #ifdef __cplusplus

@@ -156,6 +156,8 @@ _SIGNATURES = {
     "ltx_gemm_set_tile_n": (ctypes.c_int, [ctypes.c_int]),
     "ltx_test_bounded_wait": (ctypes.c_int, [ctypes.c_ulonglong, c_vp, c_vp]),
     "ltx_test_attention_force_split": (ctypes.c_int, [ctypes.c_int]),
+    "ltx_test_attention_plan": (ctypes.c_int, [c_i64, c_i64, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                               ctypes.POINTER(ctypes.c_int)]),
     "ltx_attention": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, ctypes.c_int, c_i64, c_i64,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_float, c_vp, c_i64, ctypes.c_int, c_vp]),
     "ltx_cfg_euler": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, ctypes.c_int, ctypes.c_float, ctypes.c_float,
@@ -474,6 +476,13 @@ def attention_force_split(parts: int) -> None:
     """Test hook (include/ltxb200_testing.h): run every unit of the calling thread's
     attention calls as `parts` key-range parts (0: the automatic plan; -1: never split)."""
     _call("ltx_test_attention_force_split", parts)
+
+
+def attention_plan(units: int, tk: int, sms: int) -> tuple[int, int]:
+    """Test hook: (units run whole, parts per remaining unit) of the automatic split plan."""
+    n_full, split_k = ctypes.c_int(), ctypes.c_int()
+    _call("ltx_test_attention_plan", units, tk, sms, ctypes.byref(n_full), ctypes.byref(split_k))
+    return n_full.value, split_k.value
 
 
 def gemm_set_tile_n(bn: int) -> None:

@@ -1302,3 +1302,12 @@ extern "C" int ltx_attention_scatter(const void* q, int64_t ldq, const void* k, 
   LTX_CUDA(cudaGetLastError());
   LTX_API_END
 }
+
+extern "C" int ltx_test_attention_plan(int64_t units, int64_t Tk, int sms, int* n_full, int* split_k) {
+  LTX_API_BEGIN
+  LTX_REQUIRE(units > 0 && Tk > 0 && sms > 0 && n_full != nullptr && split_k != nullptr, "bad argument");
+  const FaPlan p = fa_plan(units, Tk, sms);
+  *n_full = p.n_full;
+  *split_k = p.n_split > 0 ? p.split_k : 1;
+  LTX_API_END
+}

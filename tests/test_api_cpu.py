@@ -188,3 +188,55 @@ def test_load_transformer_maps_checkpoint_keys_like_the_reference(tmp_path):
     assert set(got) == set(sd)
     for name, t in sd.items():
         assert torch.equal(got[name], t), name
+
+
+def test_attention_split_plan():
+    """The attention launch's split plan (host arithmetic, ltx_test_attention_plan): the
+    per-rank self-attention shapes of config 3 at 1, 2, 4 and 8 GPUs, config 5 (keys not a
+    multiple of the 128-key tile: never split) and the 126 audio queries over 6144 video
+    keys (64 units, fewer than the SMs: all split). Every plan keeps whole units to full
+    waves, splits into a divisor of the key tiles with at least 3 tiles per part, and has
+    the least cost of the measured model (whole unit 11 + n key-tile times, part 16 + n/k)."""
+    sms = 148
+    cases = {(2, 32, 6144, 6144): (1480, 2), (1, 32, 6144, 6144): (740, 4), (1, 16, 6144, 6144): (384, 1),
+             (1, 8, 6144, 6144): (148, 3), (2, 32, 27588, 27588): (6912, 1), (2, 32, 126, 6144): (0, 2)}
+    for (b, h, tq, tk), want in cases.items():
+        units = b * h * ((tq + 255) // 256)
+        assert nat.attention_plan(units, tk, sms) == want, (b, h, tq, tk)
+    for units in range(1, 1200, 7):
+        for tk in (384, 1024, 1536, 6144, 6000):
+            n_full, k = nat.attention_plan(units, tk, sms)
+            r = units % sms
+            if k == 1:
+                assert n_full == units
+                continue
+            n = tk // 128
+            assert tk % 128 == 0 and n % k == 0 and n // k >= 3
+            assert n_full == units - r and n_full % sms == 0 and r * k <= 4 * sms
+            cost = -(-(r * k) // sms) * (16 + n / k)
+            assert cost < 11 + n
+            for k2 in range(2, 9):
+                if n % k2 == 0 and n // k2 >= 3 and r * k2 <= 4 * sms:
+                    assert cost <= -(-(r * k2) // sms) * (16 + n / k2) + 1e-9
+
+
+def test_exchange_entry_points_validate_without_a_gpu():
+    """The peer-memory exchange entry points reject bad arguments with a status code
+    before any CUDA call."""
+    lib = nat.load_library()
+    fake = (ctypes.c_void_p * 9)(*([16] * 9))
+    cnt = ctypes.c_void_p(16)
+    assert lib.ltx_sp_barrier(fake, cnt, 9, 0, 1000, None) == 1  # more than 8 ranks
+    assert lib.ltx_sp_barrier(fake, cnt, 2, 2, 1000, None) == 1  # rank out of range
+    assert lib.ltx_sp_barrier(None, cnt, 2, 0, 1000, None) == 1
+    x = ctypes.c_void_p(256)
+    # 30 heads do not split over 4 ranks
+    assert lib.ltx_qk_norm_rope_scatter(x, 6200, 64, 64, 30, 64, x, x, ctypes.c_float(1e-6), None, None, 0, 0, 1,
+                                        4, 0, fake, 1600, None) == 1
+    # attention_scatter needs more than 128 keys and parts dividing T
+    assert lib.ltx_attention_scatter(x, 1544, x, 1544, x, 1544, 1, 128, 8, 64, ctypes.c_float(0.125), None, 0, None,
+                                     0, 4, fake, 2048, 0, None) == 1
+    assert lib.ltx_attention_scatter(x, 1544, x, 1544, x, 1544, 1, 1000, 8, 64, ctypes.c_float(0.125), None, 0,
+                                     None, 0, 3, fake, 2048, 0, None) == 1
+    assert lib.ltx_peer_alloc(0, None, None) == 1
+    assert lib.ltx_peer_close(None) == 0 and lib.ltx_peer_free(None) == 0
