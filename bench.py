@@ -734,6 +734,104 @@ def run_gpu_bar(args, dev: torch.device) -> dict:
             "torch": torch.__version__, "cudnn": torch.backends.cudnn.version(), "ops": rows}
 
 
+# Guidance of the reference's production run (run_all.py:43-44): video cfg 3, STG 1,
+# rescale 0.7, modality 3; audio cfg 7, STG 1, rescale 0.7, modality 3. STG perturbs the
+# self-attention of one block (block 29 of the 48-block model; block 13 of config 3's 28).
+GUIDED_V = (3.0, 1.0, 0.7, 3.0)
+GUIDED_A = (7.0, 1.0, 0.7, 3.0)
+
+
+def run_guided(args, dev: torch.device) -> dict:
+    """The production sampling step on one GPU: guided_denoise_step (one transformer call
+    on the B = 4 guidance batch [cond, uncond, STG-perturbed, A<->V-isolated], X0 per pass,
+    guidance with std rescale) and the Euler update per modality, as run_dit runs it. The
+    step has host synchronisations (keep masks, per-sample timesteps), so it runs eagerly."""
+    import _native as nat
+    import ltx_dit
+
+    c = CONFIGS[args.config]
+    if c.get("loop"):
+        raise SystemExit("--guided takes config 3 or 4")
+    t = c["f"] * c["h"] * c["w"]
+    model, cfg = build_model(dev, c=c)
+    inp = make_inputs(dev, seed=7, c=c)
+    stg_block = (29 if c["num_layers"] > 29 else c["num_layers"] // 2,)
+    vp = ltx_dit.GuiderParams(*GUIDED_V, stg_blocks=stg_block)
+    video = ltx_dit.LatentState(latent=inp["latent"], denoise_mask=torch.ones(1, t, 1, device=dev),
+                                positions=inp["pos"], clean_latent=inp["latent"], keyframes_mask=inp["kf"])
+    contexts = {"v_pos": inp["ctx"][:1], "v_neg": inp["ctx"][1:]}
+    audio, ap = None, None
+    if c["kind"] == "av":
+        ta = c["audio_tokens"]
+        audio = ltx_dit.LatentState(latent=inp["a_latent"], denoise_mask=torch.ones(1, ta, 1, device=dev),
+                                    positions=inp["a_pos"], clean_latent=inp["a_latent"])
+        contexts.update(a_pos=inp["a_ctx"][:1], a_neg=inp["a_ctx"][1:])
+        ap = ltx_dit.GuiderParams(*GUIDED_A, stg_blocks=stg_block)
+    sigmas = inp["sigmas"]
+
+    def step():
+        dv, da, _ = ltx_dit.guided_denoise_step(model, video, audio, contexts, sigmas[0], 0, vp, ap, cfg)
+        nv = ltx_dit.euler_step(video.latent, dv, sigmas, 0)
+        na = ltx_dit.euler_step(audio.latent, da, sigmas, 0) if audio is not None else None
+        return nv, na
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize(dev)
+    n0 = nat.launch_count()
+    step()
+    torch.cuda.synchronize(dev)
+    launches_per_step = nat.launch_count() - n0
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms_per_step = ev0.elapsed_time(ev1) / args.steps
+    with nat.profile() as prof:
+        step()
+    kern = prof.summary()
+    flops = sum((kernel_flops(k) or 0.0) * v["launches"] for k, v in kern.items())
+    step_ms_instr = sum(v["total_ms"] for v in kern.values())
+    peaks = load_peaks()
+    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    dom_label, dom = max(kern.items(), key=lambda kv: kv[1]["total_ms"])
+    dom_flops = kernel_flops(dom_label)
+    achieved = dom_flops / (dom["avg_ms"] / 1e3) / 1e12 if dom_flops else None
+    tokens = 4 * t  # the four guidance passes of one latent
+    tflops = flops / (ms_per_step / 1e3) / 1e12
+    workload = dict(workload_config(c))
+    workload["workload"] = (f"production sampling step of {c['workload'].split(':')[0]}: run_dit's guided_denoise_step "
+                            "(B = 4 guidance batch [cond, uncond, STG, A<->V-isolated], X0, guidance with std "
+                            "rescale) + Euler per modality")
+    workload["global_batch"] = 4
+    workload["guidance"] = {"video": list(GUIDED_V) + [list(stg_block)],
+                            "audio": (list(GUIDED_A) + [list(stg_block)]) if ap is not None else None}
+    return {
+        "metric": METRIC, "value": tokens / (ms_per_step / 1e3), "unit": "latent tokens/s (4 passes x T)",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload,
+        "execution": {"parallelism": "single GPU", "cuda_graph": False, "step_flops": flops,
+                      "note": "eager: the guided step synchronises with the host (keep masks, timesteps)"},
+        "steps_per_s": 1e3 / ms_per_step, "step_tflops_per_gpu": tflops,
+        "pct_bf16_peak": tflops / peaks["bf16_tflops"], "pct_bf16_peak_sustained": tflops / peak,
+        "roofline": {"kernel": dom_label, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (achieved / peak) if achieved else None, "traffic": None,
+                     "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+                     "avg_launch_ms": dom["avg_ms"], "share_of_step": dom["total_ms"] / step_ms_instr},
+        "gpu_launches": launches_per_step * args.steps, "gpu_launches_per_step": launches_per_step,
+        "kernels": {k: {"launches": v["launches"], "total_ms": round(v["total_ms"], 4),
+                        "share": round(v["total_ms"] / step_ms_instr, 4)}
+                    for k, v in sorted(kern.items(), key=lambda kv: -kv[1]["total_ms"])[:12]},
+        "clocks": clocks.summary(),
+        "cpu_baseline": None,
+    }
+
+
 def run_probe(args, dev: torch.device) -> dict:
     """Launch one kernel of the step at its config-3 shape W + K times and time the K
     launches with CUDA events (the small, single-kernel case for ncu captures)."""
@@ -870,6 +968,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--guided", action="store_true",
+                    help="one GPU: the production sampling step (B = 4 guidance batch, run_dit) instead of the CFG step")
     ap.add_argument("--cfg-split", type=int, choices=[1, 2], default=None,
                     help="N > 1: CFG groups (default 2: cond and uncond on separate ranks)")
     ap.add_argument("--exchange", choices=["auto", "peer", "nccl"], default="auto",
@@ -893,6 +993,11 @@ def main():
         return
     if args.probe:
         print(json.dumps(run_probe(args, dev)), flush=True)
+        return
+    if args.guided:
+        if world > 1:
+            raise SystemExit("--guided runs on one GPU")
+        print(json.dumps(run_guided(args, dev)), flush=True)
         return
     # Libraries (NCCL's banner among them) write to file descriptor 1; keep stdout for the
     # one JSON line by pointing fd 1 at stderr until it is printed.
