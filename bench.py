@@ -736,7 +736,7 @@ def run_gpu_bar(args, dev: torch.device) -> dict:
 
 # Guidance of the reference's production run (run_all.py:43-44): video cfg 3, STG 1,
 # rescale 0.7, modality 3; audio cfg 7, STG 1, rescale 0.7, modality 3. STG perturbs the
-# self-attention of one block (block 29 of the 48-block model; block 13 of config 3's 28).
+# self-attention of one block (block 29 of the 48-block model; block 14 of config 3's 28).
 GUIDED_V = (3.0, 1.0, 0.7, 3.0)
 GUIDED_A = (7.0, 1.0, 0.7, 3.0)
 
