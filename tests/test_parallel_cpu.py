@@ -156,3 +156,48 @@ def test_split_kv_merge_equals_full_attention_gloo(world):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert all(err < 1e-5 for _, err in res), res
+
+
+def _transport_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import ltx_dit
+        import ltx_parallel
+
+        cfg = ltx_dit.DiTConfig.video_only(num_layers=1, heads=8, head_dim=16, cross_dim=32)
+        with torch.device("meta"):
+            model = ltx_dit.LTXModel(cfg)
+        got = []
+        for cfg_split, exchange in ((2, "auto"), (1, "auto"), (1, "nccl")):
+            pdn = ltx_parallel.ParallelDenoiser(model, cfg_split=cfg_split, exchange=exchange)
+            got.append((pdn.layout.sp, pdn.exchange_kind, pdn.exchange is None,
+                        model._sp is not None and model._sp.exchange is None))
+            pdn.close()
+        try:
+            ltx_parallel.ParallelDenoiser(model, exchange="shared-memory")
+            got.append("no error")
+        except ValueError:
+            got.append("ValueError")
+        q.put((rank, got))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_transport_choice_gloo():
+    """ParallelDenoiser's exchange transport: with CFG2 at 2 ranks there is no sequence
+    parallelism (no exchange); with SP2 "auto" picks the NCCL formulation when the process
+    group is not NCCL on CUDA (here gloo on CPU), and an unknown transport is refused."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_transport_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for _, got in res:
+        assert got == [(1, "none", True, False), (2, "nccl", True, True), (2, "nccl", True, True), "ValueError"]
